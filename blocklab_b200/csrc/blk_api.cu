@@ -1,0 +1,1013 @@
+// C ABI of libblk_world.so and the small kernels around the tile kernel:
+// override column-CSR build, torch placement, edit application with
+// World::setBlock semantics + dirty-window marking, render voxel list,
+// day/night effective light, RGBA8 -> float NCHW.
+#include "blk_internal.h"
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+namespace blk {
+
+size_t tile_smem_bytes();
+int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream);
+
+namespace {
+thread_local std::string g_last_error;
+constexpr int kScanThreads = 1024;
+constexpr int kScanItems = 4; // per thread
+constexpr uint32_t kScanTile = kScanThreads * kScanItems;
+
+inline cudaStream_t as_stream(uintptr_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------- scans --
+__device__ inline uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sums, uint32_t& total)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+        if (lane >= o)
+            x += y;
+    }
+    if (lane == 31)
+        warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+            if (lane >= o)
+                w += y;
+        }
+        warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const uint32_t warp_prefix = warp > 0 ? warp_sums[warp - 1] : 0u;
+    total = warp_sums[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return warp_prefix + x - v;
+}
+
+__global__ void scan_reduce_kernel(const uint32_t* in, uint64_t n, uint32_t* partials)
+{
+    __shared__ uint32_t ws[32];
+    const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kScanTile + threadIdx.x * kScanItems;
+    uint32_t sum = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+        if (base + k < n)
+            sum += in[base + k];
+    uint32_t total;
+    block_exclusive_scan(sum, ws, total);
+    if (threadIdx.x == 0)
+        partials[blockIdx.x] = total;
+}
+
+__global__ void scan_partials_kernel(uint32_t* partials, uint64_t n)
+{
+    __shared__ uint32_t ws[32];
+    uint32_t carry = 0;
+    for (uint64_t base = 0; base < n; base += blockDim.x) {
+        const uint64_t i = base + threadIdx.x;
+        const uint32_t v = i < n ? partials[i] : 0u;
+        uint32_t total;
+        const uint32_t ex = block_exclusive_scan(v, ws, total);
+        if (i < n)
+            partials[i] = carry + ex;
+        carry += total;
+    }
+}
+
+__global__ void scan_final_kernel(const uint32_t* in, uint64_t n, const uint32_t* partials, uint32_t* out)
+{
+    __shared__ uint32_t ws[32];
+    const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kScanTile + threadIdx.x * kScanItems;
+    uint32_t v[kScanItems];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+        v[k] = base + k < n ? in[base + k] : 0u;
+        sum += v[k];
+    }
+    uint32_t total;
+    uint32_t run = partials[blockIdx.x] + block_exclusive_scan(sum, ws, total);
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+        if (base + k < n) {
+            out[base + k] = run;
+            run += v[k];
+        }
+}
+
+// Exclusive scan of n uint32 (n <= scan capacity of the context).
+int exclusive_scan(blk_ctx* ctx, const uint32_t* in, uint32_t* out, uint64_t n, cudaStream_t st)
+{
+    const uint64_t blocks = (n + kScanTile - 1) / kScanTile;
+    if (blocks > ctx->scan_blocks) {
+        set_error("internal: scan larger than its scratch");
+        return BLK_ERR_CAPACITY;
+    }
+    scan_reduce_kernel<<<static_cast<unsigned>(blocks), kScanThreads, 0, st>>>(in, n, ctx->scan_partials);
+    scan_partials_kernel<<<1, kScanThreads, 0, st>>>(ctx->scan_partials, blocks);
+    scan_final_kernel<<<static_cast<unsigned>(blocks), kScanThreads, 0, st>>>(in, n, ctx->scan_partials, out);
+    return cuda_fail(cudaGetLastError(), "scan launch");
+}
+
+// ------------------------------------------------------------ overrides --
+struct RegionDims {
+    int32_t ox, oy, oz;
+    int32_t W, H, D;
+    uint32_t num_envs;
+};
+
+__device__ inline bool local_cell(const RegionDims& r, const blk_override& o, int32_t& x, int32_t& y, int32_t& z)
+{
+    x = o.x - r.ox;
+    y = o.y - r.oy;
+    z = o.z - r.oz;
+    return o.env < r.num_envs && x >= 0 && y >= 0 && z >= 0 && x < r.W && y < r.H && z < r.D && o.block <= Torch;
+}
+
+__global__ void ovr_count_kernel(const blk_override* ovr, uint32_t n, RegionDims r, uint32_t* col_count)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const blk_override o = ovr[i];
+        int32_t x, y, z;
+        if (!local_cell(r, o, x, y, z))
+            continue;
+        const uint64_t col = static_cast<uint64_t>(o.env) * r.W * r.D + static_cast<uint64_t>(z) * r.W + x;
+        atomicAdd(col_count + col, 1u);
+    }
+}
+
+__global__ void ovr_scatter_kernel(const blk_override* ovr, uint32_t n, RegionDims r, const uint32_t* col_offset,
+    uint32_t* cursor, uint64_t* entries)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const blk_override o = ovr[i];
+        int32_t x, y, z;
+        if (!local_cell(r, o, x, y, z))
+            continue;
+        const uint64_t col = static_cast<uint64_t>(o.env) * r.W * r.D + static_cast<uint64_t>(z) * r.W + x;
+        const uint32_t pos = col_offset[col] + atomicAdd(cursor + col, 1u);
+        entries[pos] = (static_cast<uint64_t>(y) << 40) | (static_cast<uint64_t>(i) << 8) | o.block;
+    }
+}
+
+// Sorts each column segment by (y, input order); the override with the
+// smallest input index in its column does the (insertion) sort.
+__global__ void ovr_sort_kernel(const blk_override* ovr, uint32_t n, RegionDims r, const uint32_t* col_offset,
+    uint64_t* entries)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const blk_override o = ovr[i];
+        int32_t x, y, z;
+        if (!local_cell(r, o, x, y, z))
+            continue;
+        const uint64_t col = static_cast<uint64_t>(o.env) * r.W * r.D + static_cast<uint64_t>(z) * r.W + x;
+        const uint32_t beg = col_offset[col], end = col_offset[col + 1];
+        if (end - beg < 2)
+            continue;
+        uint32_t min_order = 0xFFFFFFFFu;
+        for (uint32_t k = beg; k < end; ++k)
+            min_order = min(min_order, static_cast<uint32_t>((entries[k] >> 8) & 0xFFFFFFFFu));
+        if (min_order != i)
+            continue;
+        for (uint32_t k = beg + 1; k < end; ++k) {
+            const uint64_t v = entries[k];
+            uint32_t m = k;
+            while (m > beg && entries[m - 1] > v) {
+                entries[m] = entries[m - 1];
+                --m;
+            }
+            entries[m] = v;
+        }
+    }
+}
+
+// --------------------------------------------------------------- torches --
+__global__ void place_torches_kernel(const uint32_t* seeds, uint32_t num_envs, uint32_t per_env, RegionDims r,
+    TerrainParams t, blk_override* out, uint32_t* out_count, uint32_t* flags)
+{
+    const uint64_t total = static_cast<uint64_t>(num_envs) * per_env;
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        *out_count = static_cast<uint32_t>(total);
+    const uint32_t columns = static_cast<uint32_t>(r.W) * static_cast<uint32_t>(r.D);
+    for (uint64_t g = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; g < total;
+         g += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t env = static_cast<uint32_t>(g / per_env);
+        const uint32_t i = static_cast<uint32_t>(g % per_env);
+        blk_override o {};
+        o.env = static_cast<uint16_t>(env);
+        o.block = Torch;
+        o.kind = 0;
+        o.x = 0;
+        o.y = INT32_MIN; // "not placed": outside every region
+        o.z = 0;
+        if (i < columns) {
+            const uint32_t seed = seeds[env];
+            const uint32_t key = hash_combine2(seed, 0x7f4a7c15u);
+            uint32_t c;
+            if (!permute(i, columns, key, c))
+                atomicOr(flags, kFlagPermuteGuard);
+            const int32_t x = static_cast<int32_t>(c % static_cast<uint32_t>(r.W));
+            const int32_t z = static_cast<int32_t>(c / static_cast<uint32_t>(r.W));
+            const int32_t top = clamp_top(terrain_top_local(t, seed, r.ox + x, r.oz + z), r.H);
+            if (top + 1 < r.H) {
+                o.x = r.ox + x;
+                o.y = r.oy + top + 1;
+                o.z = r.oz + z;
+            }
+        }
+        out[g] = o;
+    }
+}
+
+// ----------------------------------------------------------- conversion --
+__global__ void rgba_to_nchw_vec_kernel(const uint4* __restrict__ in, float4* __restrict__ out, uint32_t quads_per_image,
+    uint64_t total_quads)
+{
+    const float inv255 = 1.0f / 255.0f;
+    for (uint64_t q = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; q < total_quads;
+         q += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t img = q / quads_per_image;
+        const uint64_t p = q - img * quads_per_image;
+        const uint4 v = __ldcs(in + q);
+        const uint32_t px[4] = { v.x, v.y, v.z, v.w };
+        float4 c[3];
+        float* cr = reinterpret_cast<float*>(&c[0]);
+        float* cg = reinterpret_cast<float*>(&c[1]);
+        float* cbl = reinterpret_cast<float*>(&c[2]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            cr[k] = __fmul_rn(static_cast<float>(px[k] & 0xFFu), inv255);
+            cg[k] = __fmul_rn(static_cast<float>((px[k] >> 8) & 0xFFu), inv255);
+            cbl[k] = __fmul_rn(static_cast<float>((px[k] >> 16) & 0xFFu), inv255);
+        }
+        float4* base = out + img * 3 * quads_per_image + p;
+        base[0] = c[0];
+        base[quads_per_image] = c[1];
+        base[2 * static_cast<uint64_t>(quads_per_image)] = c[2];
+    }
+}
+
+__global__ void rgba_to_nchw_scalar_kernel(const uchar4* in, float* out, uint32_t pixels_per_image, uint64_t total)
+{
+    const float inv255 = 1.0f / 255.0f;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t img = i / pixels_per_image;
+        const uint64_t p = i - img * pixels_per_image;
+        const uchar4 s = in[i];
+        float* base = out + img * 3 * pixels_per_image + p;
+        base[0] = __fmul_rn(static_cast<float>(s.x), inv255);
+        base[pixels_per_image] = __fmul_rn(static_cast<float>(s.y), inv255);
+        base[2 * static_cast<uint64_t>(pixels_per_image)] = __fmul_rn(static_cast<float>(s.z), inv255);
+    }
+}
+
+// ---------------------------------------------------------------- edits --
+__global__ void edit_count_kernel(const blk_override* e, uint32_t n, uint32_t num_envs, uint32_t* env_count)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        if (e[i].env < num_envs)
+            atomicAdd(env_count + e[i].env, 1u);
+}
+
+__global__ void edit_scatter_kernel(const blk_override* e, uint32_t n, uint32_t num_envs, const uint32_t* env_offset,
+    uint32_t* cursor, uint32_t* order)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        if (e[i].env < num_envs)
+            order[env_offset[e[i].env] + atomicAdd(cursor + e[i].env, 1u)] = i;
+}
+
+struct EditArgs {
+    const blk_override* edits;
+    const uint32_t* env_offset;
+    uint32_t* order;
+    uint8_t* ids;
+    int16_t* hmap;
+    uint32_t* win_lo;  // per env tile, atomicMin
+    uint32_t* win_hi;  // per env tile, atomicMax
+    RegionDims r;
+    uint64_t env_stride;
+    uint32_t tiles_x, tiles_z;
+};
+
+__device__ void mark_dirty(const EditArgs& a, uint32_t env, int32_t x, int32_t z, int32_t ylo, int32_t yhi)
+{
+    const int32_t lo = max(ylo - kMaxDistance, 0), hi = min(yhi + kMaxDistance, a.r.H - 1);
+    const int32_t tx0 = max(x - kMaxDistance, 0) / 32, tx1 = min(x + kMaxDistance, a.r.W - 1) / 32;
+    const int32_t tz0 = max(z - kMaxDistance, 0) / 32, tz1 = min(z + kMaxDistance, a.r.D - 1) / 32;
+    for (int32_t tz = tz0; tz <= tz1; ++tz)
+        for (int32_t tx = tx0; tx <= tx1; ++tx) {
+            const uint64_t t = static_cast<uint64_t>(env) * a.tiles_x * a.tiles_z + static_cast<uint64_t>(tz) * a.tiles_x + tx;
+            atomicMin(a.win_lo + t, static_cast<uint32_t>(lo));
+            atomicMax(a.win_hi + t, static_cast<uint32_t>(hi));
+        }
+}
+
+// One thread per env: sort the env's edit indices (insertion sort restores
+// input order after the atomic scatter), then apply them sequentially with
+// World::setBlock semantics (src/world/World.cpp:239-287).
+__global__ void apply_edits_kernel(EditArgs a)
+{
+    const uint32_t env = blockIdx.x * blockDim.x + threadIdx.x;
+    if (env >= a.r.num_envs)
+        return;
+    const uint32_t beg = a.env_offset[env], end = a.env_offset[env + 1];
+    for (uint32_t k = beg + 1; k < end; ++k) {
+        const uint32_t v = a.order[k];
+        uint32_t m = k;
+        while (m > beg && a.order[m - 1] > v) {
+            a.order[m] = a.order[m - 1];
+            --m;
+        }
+        a.order[m] = v;
+    }
+    uint8_t* ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
+    int16_t* hm = a.hmap + static_cast<uint64_t>(env) * a.r.W * a.r.D;
+    const int32_t H = a.r.H;
+    for (uint32_t k = beg; k < end; ++k) {
+        const blk_override e = a.edits[a.order[k]];
+        int32_t x = e.x - a.r.ox, y = e.y - a.r.oy, z = e.z - a.r.oz;
+        uint8_t block = e.kind == 1 ? Air : e.block;
+        if (x < 0 || z < 0 || y < 0 || x >= a.r.W || z >= a.r.D || y >= H || block > Torch)
+            continue;
+        const uint64_t col = static_cast<uint64_t>(z) * a.r.W + x;
+        if (e.kind == 1 && ids[col * H + y] != Torch)
+            continue;
+        // setBlock, with the torch-support rule unrolled (the torch removal
+        // cannot cascade: Air is not solid).
+        for (int pass = 0; pass < 2; ++pass) {
+            uint8_t& cell = ids[col * H + y];
+            const uint8_t old = cell;
+            if (old == block)
+                break;
+            cell = block;
+            const int32_t old_top = hm[col] - a.r.oy;
+            int32_t top = old_top;
+            if (is_opaque(block) && y > top)
+                top = y;
+            else if (!is_opaque(block) && is_opaque(old) && y == top) {
+                top = -1;
+                for (int32_t yy = y - 1; yy >= 0; --yy)
+                    if (is_opaque(ids[col * H + yy])) {
+                        top = yy;
+                        break;
+                    }
+            }
+            hm[col] = static_cast<int16_t>(top + a.r.oy);
+            int32_t ylo = y, yhi = y;
+            if (top != old_top) {
+                ylo = min(ylo, min(top, old_top) + 1);
+                yhi = max(yhi, max(top, old_top));
+            }
+            mark_dirty(a, env, x, z, max(ylo, 0), min(yhi, H - 1));
+            if (!(is_opaque(old) && !is_opaque(block) && y + 1 < H && ids[col * H + y + 1] == Torch))
+                break;
+            y = y + 1;
+            block = Air;
+        }
+    }
+}
+
+__global__ void dirty_compact_kernel(const uint32_t* win_lo, const uint32_t* win_hi, uint64_t n_tiles,
+    uint32_t* window, uint32_t* list, uint32_t* count)
+{
+    for (uint64_t t = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; t < n_tiles;
+         t += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t lo = win_lo[t], hi = win_hi[t];
+        if (lo <= hi && hi != 0xFFFFFFFFu) {
+            window[t] = lo | (hi << 16);
+            list[atomicAdd(count, 1u)] = static_cast<uint32_t>(t);
+        }
+    }
+}
+
+// --------------------------------------------------------- render voxels --
+struct VoxelArgs {
+    const uint8_t* ids;
+    const uint8_t* light;
+    int32_t W, H, D;
+    uint32_t* row_count;  // [D*H]
+};
+
+__device__ inline bool voxel_at(const VoxelArgs& a, int x, int y, int z, uint32_t out[3])
+{
+    const uint64_t idx = (static_cast<uint64_t>(z) * a.W + x) * a.H + y;
+    const uint8_t b = a.ids[idx];
+    if (b == Air)
+        return false;
+    // left, right, top, bottom, front, back (src/world/Voxel.h:10-17)
+    const int nx[6] = { x - 1, x + 1, x, x, x, x };
+    const int ny[6] = { y, y, y + 1, y - 1, y, y };
+    const int nz[6] = { z, z, z, z, z + 1, z - 1 };
+    uint8_t nb[6], nl[6];
+#pragma unroll
+    for (int f = 0; f < 6; ++f) {
+        if (nx[f] < 0 || ny[f] < 0 || nz[f] < 0 || nx[f] >= a.W || ny[f] >= a.H || nz[f] >= a.D) {
+            nb[f] = Air;
+            nl[f] = 0;
+        } else {
+            const uint64_t j = (static_cast<uint64_t>(nz[f]) * a.W + nx[f]) * a.H + ny[f];
+            nb[f] = a.ids[j];
+            nl[f] = a.light[j];
+        }
+    }
+    uint32_t faces = 0, bl = 0, sl = 0;
+    if (b == Torch) {
+        faces = 0x1 | 0x2 | 0x4 | 0x10 | 0x20;
+        bl = 0xFFFFFFu;
+    } else {
+        bool all = true;
+#pragma unroll
+        for (int f = 0; f < 6; ++f)
+            all = all && is_opaque(nb[f]);
+        if (all)
+            return false;
+#pragma unroll
+        for (int f = 0; f < 6; ++f) {
+            faces |= is_opaque(nb[f]) ? 0u : (1u << f);
+            bl |= static_cast<uint32_t>(nl[f] & 0xF) << (4 * f);
+        }
+    }
+#pragma unroll
+    for (int f = 0; f < 6; ++f)
+        sl |= static_cast<uint32_t>(nl[f] >> 4) << (4 * f);
+    out[0] = static_cast<uint32_t>(b) | (faces << 5) | (static_cast<uint32_t>(z) << 11) | (static_cast<uint32_t>(y) << 17)
+        | (static_cast<uint32_t>(x) << 26);
+    out[1] = bl;
+    out[2] = sl;
+    return true;
+}
+
+__global__ void voxel_count_kernel(VoxelArgs a)
+{
+    const int row = blockIdx.x * blockDim.x + threadIdx.x; // row = z*H + y
+    if (row >= a.D * a.H)
+        return;
+    const int z = row / a.H, y = row % a.H;
+    uint32_t n = 0, tmp[3];
+    for (int x = 0; x < a.W; ++x)
+        n += voxel_at(a, x, y, z, tmp) ? 1u : 0u;
+    a.row_count[row] = n;
+}
+
+__global__ void voxel_write_kernel(VoxelArgs a, const uint32_t* row_offset, uint32_t* voxels, uint32_t max_voxels,
+    uint32_t* count, int32_t* header, int3 origin)
+{
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    const int rows = a.D * a.H;
+    if (row == 0) {
+        header[0] = origin.x;
+        header[1] = origin.y;
+        header[2] = origin.z;
+    }
+    if (row >= rows)
+        return;
+    if (row == rows - 1)
+        *count = row_offset[row] + a.row_count[row];
+    const int z = row / a.H, y = row % a.H;
+    uint32_t pos = row_offset[row], v[3];
+    for (int x = 0; x < a.W; ++x)
+        if (voxel_at(a, x, y, z, v)) {
+            if (pos < max_voxels) {
+                voxels[3 * static_cast<uint64_t>(pos)] = v[0];
+                voxels[3 * static_cast<uint64_t>(pos) + 1] = v[1];
+                voxels[3 * static_cast<uint64_t>(pos) + 2] = v[2];
+            }
+            ++pos;
+        }
+}
+
+// ------------------------------------------------------- effective light --
+__global__ void effective_light_kernel(const uint4* light, uint4* out, const uint8_t* dimming, uint64_t quads_per_env,
+    uint64_t total)
+{
+    for (uint64_t q = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; q < total;
+         q += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t d = dimming[q / quads_per_env] * 0x01010101u;
+        const uint4 v = light[q];
+        uint32_t w[4] = { v.x, v.y, v.z, v.w };
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t sky = (w[k] >> 4) & 0x0F0F0F0Fu;
+            w[k] = (__vsubus4(sky, d) << 4) | (w[k] & 0x0F0F0F0Fu);
+        }
+        out[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+int grid_for(uint64_t work, int threads)
+{
+    uint64_t blocks = (work + threads - 1) / threads;
+    if (blocks > 148ull * 16)
+        blocks = 148ull * 16;
+    return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+RegionDims region(const blk_ctx* ctx)
+{
+    RegionDims r;
+    r.ox = ctx->cfg.origin_x;
+    r.oy = ctx->cfg.origin_y;
+    r.oz = ctx->cfg.origin_z;
+    r.W = static_cast<int32_t>(ctx->cfg.width);
+    r.H = static_cast<int32_t>(ctx->cfg.height);
+    r.D = static_cast<int32_t>(ctx->cfg.depth);
+    r.num_envs = ctx->cfg.num_envs;
+    return r;
+}
+
+template <typename T>
+int dalloc(T** p, size_t count, const char* what)
+{
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16);
+    if (e != cudaSuccess) {
+        *p = nullptr;
+        cudaGetLastError();
+        set_error(std::string("cudaMalloc ") + what + ": " + cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? BLK_ERR_OUT_OF_MEMORY : BLK_ERR_CUDA;
+    }
+    return BLK_OK;
+}
+
+} // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+    if (e == cudaSuccess)
+        return BLK_OK;
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return BLK_ERR_CUDA;
+}
+
+int stage_input(const void* src, size_t bytes, void* staging, cudaStream_t stream, const void** out)
+{
+    if (bytes == 0) {
+        *out = src;
+        return BLK_OK;
+    }
+    cudaPointerAttributes attr {};
+    cudaError_t e = cudaPointerGetAttributes(&attr, src);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        attr.type = cudaMemoryTypeUnregistered;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) {
+        *out = src;
+        return BLK_OK;
+    }
+    e = cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "cudaMemcpyAsync (input staging)");
+    *out = staging;
+    return BLK_OK;
+}
+
+TerrainParams terrain_params(const blk_ctx* ctx)
+{
+    TerrainParams t;
+    t.mode = ctx->cfg.terrain_mode;
+    t.base = ctx->cfg.fbm_base;
+    t.amplitude = ctx->cfg.fbm_amplitude;
+    t.origin_x = ctx->cfg.origin_x;
+    t.origin_y = ctx->cfg.origin_y;
+    t.origin_z = ctx->cfg.origin_z;
+    t.height = static_cast<int32_t>(ctx->cfg.height);
+    return t;
+}
+
+} // namespace blk
+
+using namespace blk;
+
+#define BLK_CHECK(expr)                                                                                                \
+    do {                                                                                                               \
+        const int rc_ = (expr);                                                                                        \
+        if (rc_ != BLK_OK)                                                                                             \
+            return rc_;                                                                                                \
+    } while (0)
+
+#define BLK_CUDA(expr, what) BLK_CHECK(cuda_fail((expr), what))
+
+extern "C" {
+
+const char* blk_last_error(void) { return g_last_error.c_str(); }
+
+int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
+{
+    if (!config || !out) {
+        set_error("blk_ctx_create: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    *out = nullptr;
+    const blk_world_config& c = *config;
+    if (c.num_envs == 0 || c.num_envs > 65536 || c.width == 0 || c.depth == 0 || c.width > 4096 || c.depth > 4096
+        || c.height == 0 || c.height % 32 != 0 || c.height > 128 || c.terrain_mode < 0 || c.terrain_mode > 2) {
+        set_error("blk_ctx_create: unsupported configuration (num_envs 1..65536, W/D 1..4096, H a multiple of 32 up "
+                  "to 128, terrain_mode 0..2)");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    BLK_CUDA(cudaSetDevice(device), "cudaSetDevice");
+    auto* ctx = new blk_ctx();
+    ctx->device = device;
+    ctx->cfg = c;
+    if (ctx->cfg.max_overrides == 0)
+        ctx->cfg.max_overrides = 1;
+    if (ctx->cfg.max_edits == 0)
+        ctx->cfg.max_edits = 1;
+    ctx->tiles_x = (c.width + 31) / 32;
+    ctx->tiles_z = (c.depth + 31) / 32;
+    ctx->columns_per_env = static_cast<uint64_t>(c.width) * c.depth;
+    ctx->env_stride = ctx->columns_per_env * c.height;
+    const uint64_t envs = c.num_envs;
+    const uint64_t n_cols = envs * ctx->columns_per_env + 1;
+    const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;
+    const uint64_t scan_n = (n_cols > n_tiles ? n_cols : n_tiles) + envs + 1;
+    ctx->scan_blocks = (scan_n + kScanTile - 1) / kScanTile;
+    int rc = BLK_OK;
+    auto A = [&](int r) {
+        if (rc == BLK_OK)
+            rc = r;
+    };
+    A(dalloc(&ctx->ids, envs * ctx->env_stride, "ids"));
+    A(dalloc(&ctx->light, envs * ctx->env_stride, "light"));
+    A(dalloc(&ctx->hmap, envs * ctx->columns_per_env, "height map"));
+    A(dalloc(&ctx->seeds, envs, "seeds"));
+    A(dalloc(&ctx->ovr, ctx->cfg.max_overrides, "override staging"));
+    A(dalloc(&ctx->col_count, n_cols, "column counts"));
+    A(dalloc(&ctx->col_offset, n_cols, "column offsets"));
+    A(dalloc(&ctx->entries, ctx->cfg.max_overrides, "override entries"));
+    A(dalloc(&ctx->scan_partials, ctx->scan_blocks, "scan partials"));
+    A(dalloc(&ctx->edits, ctx->cfg.max_edits, "edit staging"));
+    A(dalloc(&ctx->edit_env_count, envs + 1, "edit counts"));
+    A(dalloc(&ctx->edit_env_offset, envs + 1, "edit offsets"));
+    A(dalloc(&ctx->edit_order, ctx->cfg.max_edits, "edit order"));
+    A(dalloc(&ctx->dirty_window, 2 * n_tiles, "dirty windows"));
+    A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
+    A(dalloc(&ctx->dirty_count, 1, "dirty count"));
+    A(dalloc(&ctx->flags, 1, "flags"));
+    if (rc == BLK_OK) {
+        if (cudaMallocHost(reinterpret_cast<void**>(&ctx->h_flags), sizeof(uint32_t)) != cudaSuccess
+            || cudaMallocHost(reinterpret_cast<void**>(&ctx->h_dirty_count), sizeof(uint32_t)) != cudaSuccess) {
+            cudaGetLastError();
+            set_error("cudaMallocHost failed");
+            rc = BLK_ERR_OUT_OF_MEMORY;
+        }
+    }
+    if (rc == BLK_OK)
+        rc = cuda_fail(cudaMemset(ctx->flags, 0, sizeof(uint32_t)), "cudaMemset flags");
+    if (rc == BLK_OK)
+        rc = cuda_fail(cudaMemset(ctx->hmap, 0, envs * ctx->columns_per_env * sizeof(int16_t)), "cudaMemset hmap");
+    if (rc == BLK_OK)
+        rc = launch_tiles(ctx, 0, 0, 0); // sets the kernel's shared-memory attribute
+    if (rc == BLK_OK)
+        rc = cuda_fail(cudaDeviceSynchronize(), "context setup");
+    if (rc != BLK_OK) {
+        blk_ctx_destroy(ctx);
+        return rc;
+    }
+    *out = ctx;
+    return BLK_OK;
+}
+
+int blk_ctx_destroy(blk_ctx* ctx)
+{
+    if (!ctx)
+        return BLK_OK;
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->ovr, ctx->col_count, ctx->col_offset,
+        ctx->entries, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->flags };
+    for (void* b : bufs)
+        if (b)
+            cudaFree(b);
+    if (ctx->h_flags)
+        cudaFreeHost(ctx->h_flags);
+    if (ctx->h_dirty_count)
+        cudaFreeHost(ctx->h_dirty_count);
+    delete ctx;
+    cudaGetLastError();
+    return BLK_OK;
+}
+
+int blk_views(blk_ctx* ctx, blk_world_views* out)
+{
+    if (!ctx || !out) {
+        set_error("blk_views: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    out->ids = ctx->ids;
+    out->light = ctx->light;
+    out->height_map = ctx->hmap;
+    out->env_stride = ctx->env_stride;
+    out->num_envs = ctx->cfg.num_envs;
+    out->width = ctx->cfg.width;
+    out->height = ctx->cfg.height;
+    out->depth = ctx->cfg.depth;
+    return BLK_OK;
+}
+
+int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* overrides, uint32_t n_overrides,
+    uintptr_t stream_handle)
+{
+    if (!ctx || !env_seeds || (n_overrides && !overrides)) {
+        set_error("blk_generate: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (n_overrides > ctx->cfg.max_overrides) {
+        set_error("blk_generate: " + std::to_string(n_overrides) + " overrides exceed max_overrides "
+            + std::to_string(ctx->cfg.max_overrides));
+        return BLK_ERR_CAPACITY;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t envs = ctx->cfg.num_envs;
+    const void* seeds_dev = nullptr;
+    BLK_CHECK(stage_input(env_seeds, envs * sizeof(uint32_t), ctx->seeds, st, &seeds_dev));
+    if (seeds_dev != ctx->seeds)
+        BLK_CUDA(cudaMemcpyAsync(ctx->seeds, seeds_dev, envs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st),
+            "seed copy");
+    const void* ovr_dev = nullptr;
+    BLK_CHECK(stage_input(overrides, static_cast<size_t>(n_overrides) * sizeof(blk_override), ctx->ovr, st, &ovr_dev));
+    const auto* ovr = static_cast<const blk_override*>(ovr_dev);
+    const uint64_t n_cols = envs * ctx->columns_per_env;
+    const RegionDims r = region(ctx);
+    BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
+    if (n_overrides)
+        ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
+    BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, n_cols + 1, st));
+    if (n_overrides) {
+        BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset cursors");
+        ovr_scatter_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset,
+            ctx->col_count, ctx->entries);
+        ovr_sort_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset, ctx->entries);
+        BLK_CUDA(cudaGetLastError(), "override kernels");
+    }
+    const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;
+    BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_tiles), st));
+    ctx->generated = true;
+    return BLK_OK;
+}
+
+int blk_place_torches(blk_ctx* ctx, const uint32_t* env_seeds, uint32_t per_env, blk_override* out,
+    uint32_t* out_count, uintptr_t stream_handle)
+{
+    if (!ctx || !env_seeds || !out || !out_count) {
+        set_error("blk_place_torches: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t envs = ctx->cfg.num_envs;
+    const void* seeds_dev = nullptr;
+    BLK_CHECK(stage_input(env_seeds, envs * sizeof(uint32_t), ctx->seeds, st, &seeds_dev));
+    const uint64_t total = envs * per_env;
+    if (total > 0xFFFFFFFFull) {
+        set_error("blk_place_torches: too many torches");
+        return BLK_ERR_CAPACITY;
+    }
+    // Entry g = env * per_env + i; entries that found no free surface cell
+    // carry y = INT32_MIN and are ignored by blk_generate.
+    place_torches_kernel<<<grid_for(total ? total : 1, 256), 256, 0, st>>>(static_cast<const uint32_t*>(seeds_dev),
+        ctx->cfg.num_envs, per_env, region(ctx), terrain_params(ctx), out, out_count, ctx->flags);
+    return cuda_fail(cudaGetLastError(), "place_torches launch");
+}
+
+int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, uintptr_t stream_handle)
+{
+    if (!ctx || (n_edits && !edits)) {
+        set_error("blk_apply_edits: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!ctx->generated) {
+        set_error("blk_apply_edits: call blk_generate first");
+        return BLK_ERR_NOT_READY;
+    }
+    if (n_edits > ctx->cfg.max_edits) {
+        set_error("blk_apply_edits: " + std::to_string(n_edits) + " edits exceed max_edits "
+            + std::to_string(ctx->cfg.max_edits));
+        return BLK_ERR_CAPACITY;
+    }
+    if (n_edits == 0)
+        return BLK_OK;
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const void* e_dev = nullptr;
+    BLK_CHECK(stage_input(edits, static_cast<size_t>(n_edits) * sizeof(blk_override), ctx->edits, st, &e_dev));
+    const auto* e = static_cast<const blk_override*>(e_dev);
+    const uint32_t envs = ctx->cfg.num_envs;
+    BLK_CUDA(cudaMemsetAsync(ctx->edit_env_count, 0, (envs + 1) * sizeof(uint32_t), st), "memset edit counts");
+    edit_count_kernel<<<grid_for(n_edits, 256), 256, 0, st>>>(e, n_edits, envs, ctx->edit_env_count);
+    BLK_CHECK(exclusive_scan(ctx, ctx->edit_env_count, ctx->edit_env_offset, envs + 1, st));
+    BLK_CUDA(cudaMemsetAsync(ctx->edit_env_count, 0, (envs + 1) * sizeof(uint32_t), st), "memset edit cursors");
+    edit_scatter_kernel<<<grid_for(n_edits, 256), 256, 0, st>>>(e, n_edits, envs, ctx->edit_env_offset,
+        ctx->edit_env_count, ctx->edit_order);
+    const uint64_t n_tiles = static_cast<uint64_t>(envs) * ctx->tiles_x * ctx->tiles_z;
+    uint32_t* win_lo = ctx->dirty_window;
+    uint32_t* win_hi = ctx->dirty_window + n_tiles;
+    BLK_CUDA(cudaMemsetAsync(win_lo, 0xFF, n_tiles * sizeof(uint32_t), st), "memset windows");
+    BLK_CUDA(cudaMemsetAsync(win_hi, 0, n_tiles * sizeof(uint32_t), st), "memset windows");
+    EditArgs a;
+    a.edits = e;
+    a.env_offset = ctx->edit_env_offset;
+    a.order = ctx->edit_order;
+    a.ids = ctx->ids;
+    a.hmap = ctx->hmap;
+    a.win_lo = win_lo;
+    a.win_hi = win_hi;
+    a.r = region(ctx);
+    a.env_stride = ctx->env_stride;
+    a.tiles_x = ctx->tiles_x;
+    a.tiles_z = ctx->tiles_z;
+    apply_edits_kernel<<<(envs + 127) / 128, 128, 0, st>>>(a);
+    BLK_CUDA(cudaGetLastError(), "apply edits launch");
+    return launch_relight(ctx, st);
+}
+
+int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t max_voxels, uint32_t* count,
+    int32_t* header, uintptr_t stream_handle)
+{
+    if (!ctx || !count || !header || (max_voxels && !voxels) || env >= ctx->cfg.num_envs) {
+        set_error("blk_build_render_voxels: invalid argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!ctx->generated) {
+        set_error("blk_build_render_voxels: call blk_generate first");
+        return BLK_ERR_NOT_READY;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    VoxelArgs a;
+    a.ids = ctx->ids + static_cast<uint64_t>(env) * ctx->env_stride;
+    a.light = ctx->light + static_cast<uint64_t>(env) * ctx->env_stride;
+    a.W = static_cast<int32_t>(ctx->cfg.width);
+    a.H = static_cast<int32_t>(ctx->cfg.height);
+    a.D = static_cast<int32_t>(ctx->cfg.depth);
+    const uint64_t rows = static_cast<uint64_t>(a.D) * a.H;
+    if (rows + 1 > static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->columns_per_env + 1) {
+        set_error("blk_build_render_voxels: region too small for the row scratch");
+        return BLK_ERR_CAPACITY;
+    }
+    a.row_count = ctx->col_count; // scratch: the override counts are not live between calls
+    uint32_t* row_offset = ctx->col_offset;
+    voxel_count_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, st>>>(a);
+    BLK_CHECK(exclusive_scan(ctx, a.row_count, row_offset, rows, st));
+    voxel_write_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, st>>>(a, row_offset,
+        static_cast<uint32_t*>(voxels), max_voxels, count, header,
+        make_int3(ctx->cfg.origin_x, ctx->cfg.origin_y, ctx->cfg.origin_z));
+    return cuda_fail(cudaGetLastError(), "render voxel launch");
+}
+
+int blk_effective_light(blk_ctx* ctx, const uint8_t* dimming, uint8_t* out, uintptr_t stream_handle)
+{
+    if (!ctx || !dimming || !out) {
+        set_error("blk_effective_light: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const void* d_dev = nullptr;
+    // dimming is staged through the edit-count scratch (num_envs + 1 words >= num_envs bytes).
+    BLK_CHECK(stage_input(dimming, ctx->cfg.num_envs, ctx->edit_env_count, st, &d_dev));
+    if (ctx->env_stride % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0) {
+        set_error("blk_effective_light: output must be 16-byte aligned");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    const uint64_t quads_per_env = ctx->env_stride / 16;
+    const uint64_t total = quads_per_env * ctx->cfg.num_envs;
+    effective_light_kernel<<<grid_for(total, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(ctx->light),
+        reinterpret_cast<uint4*>(out), static_cast<const uint8_t*>(d_dev), quads_per_env, total);
+    return cuda_fail(cudaGetLastError(), "effective light launch");
+}
+
+uint8_t blk_sky_light_at_time(uint32_t t)
+{
+    // src/world/Lighting.cpp:21-49 with src/world/WorldTime.h:10-18.
+    const int sunsetStart = 12000, sunsetEnd = 13702, sunriseStart = 22300, sunriseEnd = 23961;
+    const int tt = static_cast<int>(t % 24000u);
+    if (tt < sunsetStart)
+        return 15;
+    if (tt <= sunsetEnd)
+        return static_cast<uint8_t>(15 - 11 * (tt - sunsetStart) / (sunsetEnd - sunsetStart));
+    if (tt <= sunriseStart)
+        return 4;
+    if (tt <= sunriseEnd)
+        return static_cast<uint8_t>(4 + 11 * (tt - sunriseStart) / (sunriseEnd - sunriseStart));
+    return 15;
+}
+
+int blk_readback(blk_ctx* ctx, uint32_t env_begin, uint32_t n_envs, uint8_t* ids, uint8_t* light, int16_t* height_map,
+    uintptr_t stream_handle)
+{
+    if (!ctx || static_cast<uint64_t>(env_begin) + n_envs > ctx->cfg.num_envs) {
+        set_error("blk_readback: invalid env range");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t vb = ctx->env_stride * n_envs, off = ctx->env_stride * env_begin;
+    if (ids)
+        BLK_CUDA(cudaMemcpyAsync(ids, ctx->ids + off, vb, cudaMemcpyDefault, st), "readback ids");
+    if (light)
+        BLK_CUDA(cudaMemcpyAsync(light, ctx->light + off, vb, cudaMemcpyDefault, st), "readback light");
+    if (height_map)
+        BLK_CUDA(cudaMemcpyAsync(height_map, ctx->hmap + ctx->columns_per_env * env_begin,
+                     ctx->columns_per_env * n_envs * sizeof(int16_t), cudaMemcpyDefault, st),
+            "readback height map");
+    return BLK_OK;
+}
+
+int blk_sync(blk_ctx* ctx, uintptr_t stream_handle)
+{
+    if (!ctx) {
+        set_error("blk_sync: null context");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    BLK_CUDA(cudaMemcpyAsync(ctx->h_flags, ctx->flags, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "flag copy");
+    BLK_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    const uint32_t f = *ctx->h_flags;
+    if (f) {
+        BLK_CUDA(cudaMemsetAsync(ctx->flags, 0, sizeof(uint32_t), st), "flag reset");
+        BLK_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        std::string msg = "device flags:";
+        if (f & kFlagOverrideList)
+            msg += " override list of a column longer than 65535";
+        if (f & kFlagBandTooWide)
+            msg += " light band wider than supported";
+        if (f & kFlagEditOverflow)
+            msg += " edit bookkeeping overflow";
+        if (f & kFlagPermuteGuard)
+            msg += " permutation guard hit";
+        set_error(msg);
+        return BLK_ERR_DEVICE_FLAG;
+    }
+    return BLK_OK;
+}
+
+int blk_convert_rgba8_to_float_nchw(const void* rgba8, float* nchw, uint32_t batch, uint32_t width, uint32_t height,
+    uintptr_t stream_handle)
+{
+    if ((!rgba8 || !nchw) && batch && width && height) {
+        set_error("blk_convert_rgba8_to_float_nchw: null pointer");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    const uint64_t ppi = static_cast<uint64_t>(width) * height;
+    const uint64_t total = ppi * batch;
+    if (total == 0)
+        return BLK_OK;
+    if (ppi > 0xFFFFFFFFull) {
+        set_error("blk_convert_rgba8_to_float_nchw: image too large");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    const bool vec = ppi % 4 == 0 && reinterpret_cast<uintptr_t>(rgba8) % 16 == 0 && reinterpret_cast<uintptr_t>(nchw) % 16 == 0;
+    if (vec) {
+        const uint64_t quads = total / 4;
+        int blocks = static_cast<int>((quads + 255) / 256);
+        if (blocks > 148 * 32)
+            blocks = 148 * 32;
+        rgba_to_nchw_vec_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(rgba8), reinterpret_cast<float4*>(nchw),
+            static_cast<uint32_t>(ppi / 4), quads);
+    } else {
+        int blocks = static_cast<int>((total + 255) / 256);
+        if (blocks > 148 * 32)
+            blocks = 148 * 32;
+        rgba_to_nchw_scalar_kernel<<<blocks, 256, 0, st>>>(static_cast<const uchar4*>(rgba8), nchw,
+            static_cast<uint32_t>(ppi), total);
+    }
+    return cuda_fail(cudaGetLastError(), "rgba8 conversion launch");
+}
+
+} // extern "C"
+
+namespace blk {
+
+int launch_relight(blk_ctx* ctx, cudaStream_t st)
+{
+    const uint64_t n_tiles = static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->tiles_x * ctx->tiles_z;
+    uint32_t* win_lo = ctx->dirty_window;
+    uint32_t* win_hi = ctx->dirty_window + n_tiles;
+    BLK_CUDA(cudaMemsetAsync(ctx->dirty_count, 0, sizeof(uint32_t), st), "memset dirty count");
+    // Pack windows in place into win_lo's slots: window[t] = lo | hi << 16.
+    dirty_compact_kernel<<<grid_for(n_tiles, 256), 256, 0, st>>>(win_lo, win_hi, n_tiles, win_lo, ctx->dirty_list,
+        ctx->dirty_count);
+    BLK_CUDA(cudaGetLastError(), "dirty compact launch");
+    // One CTA per tile of the batch; CTAs past the device-side dirty count exit
+    // at once, so no host round trip is needed.
+    return launch_tiles(ctx, 1, static_cast<uint32_t>(n_tiles), st);
+}
+
+} // namespace blk

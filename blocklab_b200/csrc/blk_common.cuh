@@ -1,0 +1,184 @@
+// Device-side primitives shared by the world-state kernels: hashing, terrain
+// heights, block predicates, device error flags.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace blk {
+
+constexpr int kMaxDistance = 14;   // light reach, src/world/WorldGenerator.cu:22
+constexpr int kHalo = kMaxDistance;
+
+enum : uint8_t { Air = 0, Grass = 1, Dirt = 2, Stone = 3, Torch = 4 };
+
+// Opaque == solid == not Air and not Torch (src/world/Block.h:30-34).
+__host__ __device__ inline bool is_opaque(uint8_t b) { return b != Air && b != Torch; }
+
+// Device error flag bits (ORed into the context's flag word).
+enum : uint32_t {
+    kFlagOverrideList = 1u << 0,   // per-column override list longer than supported
+    kFlagBandTooWide = 1u << 1,    // light band wider than the compiled maximum
+    kFlagEditOverflow = 1u << 2,   // changed-cell list of an edit batch overflowed
+    kFlagPermuteGuard = 1u << 3,   // permutation walk hit its iteration bound
+};
+
+// src/utility/Hash.h:10-24
+__host__ __device__ inline uint32_t hash_combine2(uint32_t a, uint32_t b)
+{
+    a ^= b + 0x9e3779b9u + (a << 6) + (a >> 2);
+    return a;
+}
+__host__ __device__ inline uint32_t hash_combine3(uint32_t a, uint32_t b, uint32_t c)
+{
+    return hash_combine2(a, hash_combine2(b, c));
+}
+// src/utility/Hash.h:26-34
+__host__ __device__ inline uint32_t hash32(uint32_t v)
+{
+    v ^= v >> 16U;
+    v *= 0x7feb352dU;
+    v ^= v >> 15U;
+    v *= 0x846ca68bU;
+    v ^= v >> 16U;
+    return v;
+}
+// src/utility/Hash.h:36-41
+__host__ __device__ inline int32_t seed_offset(uint32_t seed, uint32_t salt)
+{
+    return static_cast<int32_t>(hash_combine2(seed, salt) % (4096U * 2U + 1U)) - 4096;
+}
+
+// Reference terrain, written with the same expression shape as
+// src/world/WorldGenerator.cu:112-127 so that nvcc makes the same choices
+// (fast __sinf/__cosf, contraction) as for the reference's CUDA build.
+__device__ inline float ref_value_noise(uint32_t seed, int32_t x, int32_t z)
+{
+    const uint32_t hash = hash_combine3(seed, static_cast<uint32_t>(x), static_cast<uint32_t>(z));
+    return static_cast<float>(hash & 0x00ffffffU) / static_cast<float>(0x00ffffffU) * 2.0f - 1.0f;
+}
+
+__device__ inline float ref_terrain_height(uint32_t seed, int32_t x, int32_t z)
+{
+    const int32_t sampleX = x + seed_offset(seed, 0x4f1bbc21U);
+    const int32_t sampleZ = z + seed_offset(seed, 0x9a7c15d3U);
+    const float low = __sinf(static_cast<float>(sampleX) * 0.17f) * 2.2f;
+    const float high = __cosf(static_cast<float>(sampleZ) * 0.13f) * 1.8f;
+    const float diagonal = __sinf(static_cast<float>(sampleX + sampleZ) * 0.08f) * 2.0f;
+    const float rough = ref_value_noise(seed, sampleX / 3, sampleZ / 3) * 0.55f;
+    return 9.0f + low + high + diagonal + rough;
+}
+
+// Lattice value of the fBm terrain: the reference's value noise, evaluated
+// with explicitly rounded single operations (no contraction) so the CPU
+// oracle reproduces it bit for bit.
+__device__ inline float fbm_lattice(uint32_t seed, int32_t x, int32_t z)
+{
+    const uint32_t h = hash_combine3(seed, static_cast<uint32_t>(x), static_cast<uint32_t>(z));
+    const float q = __fdiv_rn(static_cast<float>(h & 0x00ffffffU), 16777215.0f);
+    return __fsub_rn(__fmul_rn(q, 2.0f), 1.0f);
+}
+
+// 4-octave value-noise fBm in [-1, 1]: lattice spacing 64 >> o, lacunarity 2,
+// gain 0.5, smoothstep-weighted bilinear interpolation, normalised by 1.875.
+__device__ inline float fbm(uint32_t seed, int32_t x, int32_t z)
+{
+    float acc = 0.0f;
+    float amp = 1.0f;
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+        const uint32_t s = hash_combine2(seed, static_cast<uint32_t>(o));
+        const float scale = 1.0f / static_cast<float>(64 >> o);
+        const float fx = __fmul_rn(static_cast<float>(x), scale);
+        const float fz = __fmul_rn(static_cast<float>(z), scale);
+        const float flx = floorf(fx);
+        const float flz = floorf(fz);
+        const int32_t ix = static_cast<int32_t>(flx);
+        const int32_t iz = static_cast<int32_t>(flz);
+        const float tx = __fsub_rn(fx, flx);
+        const float tz = __fsub_rn(fz, flz);
+        const float wx = __fmul_rn(__fmul_rn(tx, tx), __fsub_rn(3.0f, __fmul_rn(2.0f, tx)));
+        const float wz = __fmul_rn(__fmul_rn(tz, tz), __fsub_rn(3.0f, __fmul_rn(2.0f, tz)));
+        const float v00 = fbm_lattice(s, ix, iz);
+        const float v10 = fbm_lattice(s, ix + 1, iz);
+        const float v01 = fbm_lattice(s, ix, iz + 1);
+        const float v11 = fbm_lattice(s, ix + 1, iz + 1);
+        const float a = __fadd_rn(v00, __fmul_rn(__fsub_rn(v10, v00), wx));
+        const float b = __fadd_rn(v01, __fmul_rn(__fsub_rn(v11, v01), wx));
+        const float n = __fadd_rn(a, __fmul_rn(__fsub_rn(b, a), wz));
+        acc = __fadd_rn(acc, __fmul_rn(amp, n));
+        amp = __fmul_rn(amp, 0.5f);
+    }
+    return __fdiv_rn(acc, 1.875f);
+}
+
+struct TerrainParams {
+    int32_t mode;       // blk_terrain_mode
+    int32_t base;
+    float amplitude;
+    int32_t origin_x, origin_y, origin_z;
+    int32_t height;     // H
+};
+
+// Surface (highest terrain block) of world column (wx, wz) as a LOCAL y, not
+// clamped: the layer rule needs the true surface even when it lies outside
+// the region. Callers clamp to [-1, H-1] where they need a cell index.
+__device__ inline int32_t terrain_top_local(const TerrainParams& t, uint32_t seed, int32_t wx, int32_t wz)
+{
+    int32_t h;
+    if (t.mode == 0)
+        h = static_cast<int32_t>(ref_terrain_height(seed, wx, wz));
+    else if (t.mode == 1)
+        h = t.base + static_cast<int32_t>(roundf(__fmul_rn(t.amplitude, fbm(seed, wx, wz))));
+    else
+        h = t.base;
+    return h - t.origin_y;
+}
+
+__device__ inline int32_t clamp_top(int32_t top, int32_t height)
+{
+    return top < -1 ? -1 : (top > height - 1 ? height - 1 : top);
+}
+
+// Terrain layer rule on local coordinates (src/world/WorldGenerator.cu:129-140).
+__device__ inline uint8_t layer_block(int32_t y, int32_t top)
+{
+    if (y > top)
+        return Air;
+    if (y == top)
+        return Grass;
+    if (y > top - 4)
+        return Dirt;
+    return Stone;
+}
+
+// Keyed permutation of [0, n) by a 4-round Feistel network with cycle walking.
+// Returns false if the walk exceeded its bound (cannot happen for a bijection;
+// kept as a guard).
+__device__ inline bool permute(uint32_t i, uint32_t n, uint32_t key, uint32_t& out)
+{
+    uint32_t bits = 2;
+    while ((1u << bits) < n)
+        bits += 2;
+    const uint32_t half = bits / 2, mask = (1u << half) - 1u;
+    uint32_t v = i;
+    for (uint32_t guard = 0; guard <= (1u << bits); ++guard) {
+        uint32_t l = v >> half, r = v & mask;
+#pragma unroll
+        for (uint32_t round = 0; round < 4; ++round) {
+            const uint32_t f = hash32(hash_combine2(key + round, r)) & mask;
+            const uint32_t nl = r;
+            r = l ^ f;
+            l = nl;
+        }
+        v = (l << half) | r;
+        if (v < n) {
+            out = v;
+            return true;
+        }
+    }
+    out = i % n;
+    return false;
+}
+
+} // namespace blk

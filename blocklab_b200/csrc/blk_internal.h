@@ -1,0 +1,61 @@
+// Internal context and launch declarations of libblk_world.so.
+#pragma once
+
+#include "../../include/blk_world.h"
+#include "blk_common.cuh"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+struct blk_ctx {
+    int device = 0;
+    blk_world_config cfg {};
+    uint32_t tiles_x = 0, tiles_z = 0;
+    uint64_t columns_per_env = 0;
+    uint64_t env_stride = 0;          // bytes per env in ids / light
+
+    uint8_t* ids = nullptr;           // [env][z][x][y]
+    uint8_t* light = nullptr;         // [env][z][x][y], sky<<4 | block
+    int16_t* hmap = nullptr;          // [env][z][x], world y
+
+    uint32_t* seeds = nullptr;        // [env]
+    bool generated = false;
+
+    // Override column CSR (generation input).
+    blk_override* ovr = nullptr;      // staging of host-resident override lists
+    uint32_t* col_count = nullptr;    // [env * columns + 1]
+    uint32_t* col_offset = nullptr;   // [env * columns + 1]
+    uint64_t* entries = nullptr;      // [max_overrides], key y<<40 | order<<8 | block
+    uint32_t* scan_partials = nullptr;
+    uint64_t scan_blocks = 0;
+
+    // Edits (incremental relight).
+    blk_override* edits = nullptr;        // staging of host-resident edit lists
+    uint32_t* edit_env_count = nullptr;   // [num_envs + 1]
+    uint32_t* edit_env_offset = nullptr;  // [num_envs + 1]
+    uint32_t* edit_order = nullptr;       // [max_edits] edit indices grouped by env, stable
+    uint32_t* dirty_window = nullptr;     // [num_envs * tiles] packed ylo | yhi<<16, 0xFFFFFFFF = clean
+    uint32_t* dirty_list = nullptr;       // [num_envs * tiles] dirty tile ids
+    uint32_t* dirty_count = nullptr;      // [1]
+    uint32_t* h_dirty_count = nullptr;    // pinned [1]
+
+    uint32_t* flags = nullptr;            // device error flag word
+    uint32_t* h_flags = nullptr;          // pinned mirror
+};
+
+namespace blk {
+
+void set_error(const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+// Copies `bytes` from host or device memory `src` into the device buffer
+// `staging` (when src is host memory) and returns the device pointer to use.
+int stage_input(const void* src, size_t bytes, void* staging, cudaStream_t stream, const void** out);
+
+TerrainParams terrain_params(const blk_ctx* ctx);
+
+int launch_relight(blk_ctx* ctx, cudaStream_t stream);
+
+} // namespace blk

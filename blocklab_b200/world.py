@@ -1,0 +1,220 @@
+"""Host-side mirror of the reference's world-state interface over the C ABI.
+
+``WorldBatch`` plays the role of the reference's ``WorldGenerator``
+(src/world/WorldGenerator.h:69-89) for a whole batch of environments on one
+GPU: it owns the resident block-id / light / height-map arrays and enqueues
+generation, edits with incremental relight, the render voxel list and the
+day/night effective light on the caller's CUDA stream. ``World``-level edit
+semantics (src/world/World.cpp:239-287) are applied on the device by
+``apply_edits``.
+
+Device arrays are exposed zero-copy as torch tensors:
+    ids, light   (num_envs, D, W, H) uint8   — column-major, y fastest
+    height_map   (num_envs, D, W)    int16   — world y of the top solid block
+``light`` packs sky << 4 | block.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _native as N
+from ._native import check
+
+OVERRIDE_DTYPE = np.dtype([("x", "<i4"), ("y", "<i4"), ("z", "<i4"), ("env", "<u2"), ("block", "u1"),
+                           ("kind", "u1")])
+assert OVERRIDE_DTYPE.itemsize == 16
+
+
+@dataclass(frozen=True)
+class WorldConfig:
+    num_envs: int
+    width: int
+    height: int
+    depth: int
+    origin: tuple[int, int, int] = (0, 0, 0)
+    terrain: int = N.TERRAIN_FBM
+    base: int = 40
+    amplitude: float = 50.0
+    max_overrides: int = 1 << 20
+    max_edits: int = 1 << 16
+
+    def to_c(self) -> N.WorldConfigC:
+        return N.WorldConfigC(self.num_envs, self.width, self.height, self.depth, self.origin[0], self.origin[1],
+                              self.origin[2], self.terrain, self.base, float(self.amplitude), self.max_overrides,
+                              self.max_edits)
+
+    @property
+    def voxels_per_env(self) -> int:
+        return self.width * self.height * self.depth
+
+
+def make_overrides(xyz, block, env=0, kind=0) -> np.ndarray:
+    """Packs override / edit records (world coordinates) into the C layout."""
+    xyz = np.asarray(xyz, np.int32).reshape(-1, 3)
+    out = np.zeros(len(xyz), OVERRIDE_DTYPE)
+    out["x"], out["y"], out["z"] = xyz[:, 0], xyz[:, 1], xyz[:, 2]
+    out["env"] = np.broadcast_to(np.asarray(env, np.uint16), len(xyz))
+    out["block"] = np.broadcast_to(np.asarray(block, np.uint8), len(xyz))
+    out["kind"] = np.broadcast_to(np.asarray(kind, np.uint8), len(xyz))
+    return out
+
+
+class _CudaArray:
+    """__cuda_array_interface__ over memory owned by a WorldBatch."""
+
+    def __init__(self, owner, ptr: int, shape, typestr: str) -> None:
+        self._owner = owner
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": tuple(shape), "typestr": typestr,
+                                         "strides": None, "version": 3, "stream": None}
+
+
+def _stream_handle(stream: Optional[torch.cuda.Stream], device: int) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return int(s.cuda_stream)
+
+
+def _ptr(obj) -> tuple[int, object]:
+    """Pointer + keep-alive for a numpy array or torch tensor (host or device)."""
+    if isinstance(obj, torch.Tensor):
+        if not obj.is_contiguous():
+            obj = obj.contiguous()
+        return obj.data_ptr(), obj
+    arr = np.ascontiguousarray(obj)
+    return arr.ctypes.data, arr
+
+
+class WorldBatch:
+    """A batch of resident worlds on one GPU (one blk_ctx)."""
+
+    def __init__(self, config: WorldConfig, device: int = 0) -> None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("WorldBatch needs a CUDA device; the world-state path has no CPU implementation")
+        self.config = config
+        self.device = device
+        handle = ctypes.c_void_p()
+        c = config.to_c()
+        check(N.lib.blk_ctx_create(device, ctypes.byref(c), ctypes.byref(handle)))
+        self._ctx = handle
+        v = N.WorldViewsC()
+        check(N.lib.blk_views(self._ctx, ctypes.byref(v)))
+        dev = torch.device("cuda", device)
+        E, D, W, H = config.num_envs, config.depth, config.width, config.height
+        self.ids = torch.as_tensor(_CudaArray(self, v.ids, (E, D, W, H), "|u1"), device=dev)
+        self.light = torch.as_tensor(_CudaArray(self, v.light, (E, D, W, H), "|u1"), device=dev)
+        self.height_map = torch.as_tensor(_CudaArray(self, v.height_map, (E, D, W), "<i2"), device=dev)
+
+    # -- lifetime -------------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_ctx", None):
+            N.lib.blk_ctx_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self) -> None:  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- the hot path -----------------------------------------------------------
+    def generate(self, env_seeds, overrides=None, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Full generation + light of every env (reference WorldGenerator::generate)."""
+        seeds_p, keep1 = _ptr(np.asarray(env_seeds, np.uint32) if not isinstance(env_seeds, torch.Tensor)
+                              else env_seeds)
+        if overrides is None:
+            ovr_p, n, keep2 = 0, 0, None
+        elif isinstance(overrides, torch.Tensor):
+            ovr_p, keep2 = _ptr(overrides)
+            n = overrides.numel() * overrides.element_size() // 16
+        else:
+            arr = np.ascontiguousarray(overrides, OVERRIDE_DTYPE)
+            ovr_p, keep2 = _ptr(arr)
+            n = len(arr)
+        check(N.lib.blk_generate(self._ctx, seeds_p, ovr_p, n, _stream_handle(stream, self.device)))
+        del keep1, keep2
+
+    def place_torches(self, env_seeds, per_env: int, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """Device override list of `per_env` torches per env on the terrain surface."""
+        n = self.config.num_envs * per_env
+        out = torch.empty(max(n, 1) * 16, dtype=torch.uint8, device=torch.device("cuda", self.device))
+        cnt = torch.zeros(1, dtype=torch.int32, device=out.device)
+        seeds_p, keep = _ptr(np.asarray(env_seeds, np.uint32) if not isinstance(env_seeds, torch.Tensor)
+                             else env_seeds)
+        check(N.lib.blk_place_torches(self._ctx, seeds_p, per_env, out.data_ptr(), cnt.data_ptr(),
+                                      _stream_handle(stream, self.device)))
+        del keep
+        return out[: n * 16]
+
+    def apply_edits(self, edits, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """World::setBlock semantics per env in list order + exact incremental relight."""
+        if isinstance(edits, torch.Tensor):
+            p, keep = _ptr(edits)
+            n = edits.numel() * edits.element_size() // 16
+        else:
+            arr = np.ascontiguousarray(edits, OVERRIDE_DTYPE)
+            p, keep = _ptr(arr)
+            n = len(arr)
+        check(N.lib.blk_apply_edits(self._ctx, p, n, _stream_handle(stream, self.device)))
+        del keep
+
+    def render_voxels(self, env: int, max_voxels: Optional[int] = None,
+                      stream: Optional[torch.cuda.Stream] = None) -> tuple[torch.Tensor, int, tuple[int, int, int]]:
+        """Reference 12-byte Voxel list of one env, ascending (z, y, x) order."""
+        cap = self.config.voxels_per_env if max_voxels is None else max_voxels
+        dev = torch.device("cuda", self.device)
+        vox = torch.empty((max(cap, 1), 3), dtype=torch.int32, device=dev)
+        cnt = torch.zeros(1, dtype=torch.int32, device=dev)
+        hdr = torch.zeros(3, dtype=torch.int32, device=dev)
+        check(N.lib.blk_build_render_voxels(self._ctx, env, vox.data_ptr(), cap, cnt.data_ptr(), hdr.data_ptr(),
+                                            _stream_handle(stream, self.device)))
+        n = int(cnt.item())
+        return vox[: min(n, cap)], n, tuple(int(v) for v in hdr.tolist())
+
+    def effective_light(self, dimming, out: Optional[torch.Tensor] = None,
+                        stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """(sky - min(sky, dimming[env])) << 4 | block for every cell."""
+        if out is None:
+            out = torch.empty_like(self.light)
+        p, keep = _ptr(np.asarray(dimming, np.uint8) if not isinstance(dimming, torch.Tensor) else dimming)
+        check(N.lib.blk_effective_light(self._ctx, p, out.data_ptr(), _stream_handle(stream, self.device)))
+        del keep
+        return out
+
+    def sync(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Waits for the stream and raises if a kernel flagged an internal limit."""
+        check(N.lib.blk_sync(self._ctx, _stream_handle(stream, self.device)))
+
+    def readback(self, env_begin: int = 0, n_envs: Optional[int] = None, ids=True, light=True, height_map=True,
+                 stream: Optional[torch.cuda.Stream] = None):
+        """Copies env range to pinned host tensors (same layout as the device arrays)."""
+        n = self.config.num_envs - env_begin if n_envs is None else n_envs
+        c = self.config
+        shp = (n, c.depth, c.width, c.height)
+        out_ids = torch.empty(shp, dtype=torch.uint8, pin_memory=True) if ids else None
+        out_light = torch.empty(shp, dtype=torch.uint8, pin_memory=True) if light else None
+        out_hm = torch.empty((n, c.depth, c.width), dtype=torch.int16, pin_memory=True) if height_map else None
+        check(N.lib.blk_readback(self._ctx, env_begin, n, out_ids.data_ptr() if ids else None,
+                                 out_light.data_ptr() if light else None, out_hm.data_ptr() if height_map else None,
+                                 _stream_handle(stream, self.device)))
+        return out_ids, out_light, out_hm
+
+
+def sky_light_at_time(tick: int) -> int:
+    """Integer sky level [4..15] at a day tick (src/world/Lighting.cpp:21-49)."""
+    return int(N.lib.blk_sky_light_at_time(tick))
+
+
+def sky_light_dimming(tick: int) -> int:
+    """Renderer dimming uniform 15 - skyLightAtTime(t) (src/graphics/Renderer.cpp:803)."""
+    return 15 - sky_light_at_time(tick)
+
+
+def torch_key(seed: int) -> int:
+    """Key of the torch-placement permutation for an env seed."""
+    a, b = seed & 0xFFFFFFFF, 0x7F4A7C15
+    a ^= (b + 0x9E3779B9 + ((a << 6) & 0xFFFFFFFF) + (a >> 2)) & 0xFFFFFFFF
+    return a & 0xFFFFFFFF

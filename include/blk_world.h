@@ -1,0 +1,180 @@
+/*
+ * blk_world.h — C ABI of the B200 world-state library (libblk_world.so).
+ *
+ * The library owns, per GPU context, a batch of `num_envs` independent voxel
+ * regions (W x H x D each) resident in HBM, and exposes the reference's
+ * world-state hot path over them:
+ *   generation (seed + sparse override overlay -> block ids, height map),
+ *   sky-light column fill and 6-neighbour flood-fill block/sky light,
+ *   exact incremental relight after edits,
+ *   the render voxel list, day/night effective light,
+ *   and the RGBA8 -> float32 NCHW observation conversion.
+ *
+ * Conventions
+ *   - Every entry point returns an int status (BLK_OK == 0); nothing aborts.
+ *     blk_last_error() returns the message of the last failure on the
+ *     calling thread.
+ *   - All work is enqueued on the caller's stream (cudaStream_t passed as
+ *     uintptr_t; 0 = legacy default stream). Calls are asynchronous unless
+ *     stated otherwise; device-side error flags are reported by blk_sync().
+ *   - Array arguments may live in host memory (pageable or pinned) or device
+ *     memory; the library detects which and stages host data itself.
+ *   - One context per GPU per host thread; a context is not thread-safe.
+ *
+ * Block ids are the reference's (src/world/Block.h:11-19):
+ *   Air=0 Grass=1 Dirt=2 Stone=3 Torch=4. Opaque == solid == not Air/Torch.
+ * Light bytes pack sky<<4 | block, each 0..15.
+ *
+ * Device layout of the world arrays (per env, column-major, y fastest):
+ *   ids[env][z][x][y], light[env][z][x][y]  (uint8)
+ *   height_map[env][z][x]                   (int16, world y of the highest
+ *                                            solid block, origin_y-1 if none)
+ * so one column of H cells is H contiguous bytes.
+ */
+#ifndef BLK_WORLD_H
+#define BLK_WORLD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum blk_status {
+    BLK_OK = 0,
+    BLK_ERR_INVALID_ARGUMENT = 1,
+    BLK_ERR_CUDA = 2,
+    BLK_ERR_OUT_OF_MEMORY = 3,
+    BLK_ERR_CAPACITY = 4,     /* an input exceeds a documented limit */
+    BLK_ERR_DEVICE_FLAG = 5,  /* a kernel reported an internal limit or bound */
+    BLK_ERR_NOT_READY = 6,    /* world not generated yet */
+};
+
+enum blk_terrain_mode {
+    BLK_TERRAIN_REFERENCE = 0, /* reference sin/cos + value-noise heights */
+    BLK_TERRAIN_FBM = 1,       /* 4-octave value-noise fBm: base + round(amplitude * fbm) */
+    BLK_TERRAIN_FLAT = 2,      /* every column at height `fbm_base` */
+};
+
+enum blk_block {
+    BLK_AIR = 0,
+    BLK_GRASS = 1,
+    BLK_DIRT = 2,
+    BLK_STONE = 3,
+    BLK_TORCH = 4,
+};
+
+enum blk_edit_kind {
+    BLK_EDIT_SET = 0,          /* World::setBlock(pos, block) */
+    BLK_EDIT_REMOVE_TORCH = 1, /* setBlock(pos, Air) only if the cell holds a torch */
+};
+
+typedef struct blk_world_config {
+    uint32_t num_envs;
+    uint32_t width;    /* W: x extent, 1..4096 */
+    uint32_t height;   /* H: y extent, multiple of 32, 32..128 */
+    uint32_t depth;    /* D: z extent, 1..4096 */
+    int32_t origin_x;  /* world coordinate of local (0, 0, 0), shared by all envs */
+    int32_t origin_y;
+    int32_t origin_z;
+    int32_t terrain_mode;   /* blk_terrain_mode */
+    int32_t fbm_base;
+    float fbm_amplitude;
+    uint32_t max_overrides; /* capacity of one blk_generate override list */
+    uint32_t max_edits;     /* capacity of one blk_apply_edits list */
+} blk_world_config;
+
+/* One sparse override / edit; world coordinates. Mirrors the reference's
+ * BlockOverride {IVec3 coord; Block block} (src/world/Block.h:55-58) plus the
+ * env index of the batch and the edit kind. */
+typedef struct blk_override {
+    int32_t x, y, z;
+    uint16_t env;
+    uint8_t block; /* blk_block */
+    uint8_t kind;  /* blk_edit_kind; ignored by blk_generate */
+} blk_override;
+
+typedef struct blk_world_views {
+    uint8_t* ids;          /* device, num_envs * D * W * H */
+    uint8_t* light;        /* device, same shape, sky<<4 | block */
+    int16_t* height_map;   /* device, num_envs * D * W */
+    uint64_t env_stride;   /* bytes between envs in ids/light */
+    uint32_t num_envs, width, height, depth;
+} blk_world_views;
+
+typedef struct blk_ctx blk_ctx;
+
+/* Context lifetime. Replaces the reference's WorldGenerator constructor /
+ * destructor (src/world/WorldGenerator.h:69-72, src/world/WorldGenerator.cu:594-619);
+ * allocates the resident world arrays for `num_envs` regions. */
+int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out);
+int blk_ctx_destroy(blk_ctx* ctx);
+
+/* Message of the last failure on this thread ("" if none). */
+const char* blk_last_error(void);
+
+/* Device pointers of the resident world arrays (valid until destroy). */
+int blk_views(blk_ctx* ctx, blk_world_views* out);
+
+/* Full generation + light of every env: terrain from env_seeds[num_envs],
+ * sparse overrides applied (at most one per cell; with duplicates the
+ * latest in list order wins), height map, sky column fill, block and sky
+ * flood fill. Replaces WorldGenerator::generate
+ * (src/world/WorldGenerator.h:79-82, src/world/WorldGenerator.cu:673-829) for
+ * a whole batch at once. Overrides outside the region are ignored. */
+int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* overrides, uint32_t n_overrides,
+    uintptr_t stream);
+
+/* Writes up to `per_env` torch overrides per env at distinct pseudo-random
+ * columns, one cell above the terrain surface (benchmark world construction).
+ * `out` is device memory of num_envs*per_env entries; *out_count (device)
+ * receives the number written. Keyed by env_seeds (host or device). */
+int blk_place_torches(blk_ctx* ctx, const uint32_t* env_seeds, uint32_t per_env, blk_override* out,
+    uint32_t* out_count, uintptr_t stream);
+
+/* Applies edits with World::setBlock semantics (src/world/World.cpp:239-287),
+ * sequentially per env in list order, then relights exactly the cells whose
+ * light can change. The reference instead regenerates and relights the whole
+ * region on any edit (src/graphics/Renderer.cpp:1121-1141). */
+int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, uintptr_t stream);
+
+/* Render voxel list of one env in the reference's 12-byte Voxel format and
+ * TerrainHeader (src/world/WorldGenerator.cu:27-67, :171-178, :221-303;
+ * shaders/voxel.vert.hlsl:14-24). Voxels are written in ascending
+ * (z, y, x) order. `voxels`, `count` and `header` are device memory. The
+ * packing holds x, z < 64 and y < 512, as in the reference. */
+int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t max_voxels, uint32_t* count,
+    int32_t* header, uintptr_t stream);
+
+/* Day/night effective light: out[i] = (sky - min(sky, dimming[env])) << 4 | block
+ * for every cell, dimming = 15 - skyLightAtTime(t) as the reference renderer
+ * applies it per face (src/graphics/Renderer.cpp:803, shaders/voxel.vert.hlsl:151).
+ * `dimming` holds num_envs bytes; `out` is device memory shaped like light. */
+int blk_effective_light(blk_ctx* ctx, const uint8_t* dimming, uint8_t* out, uintptr_t stream);
+
+/* Integer sky level at a day tick (src/world/Lighting.cpp:21-49). Host only. */
+uint8_t blk_sky_light_at_time(uint32_t tick);
+
+/* Copies env range [env_begin, env_begin + n_envs) of the world arrays to
+ * caller memory in the device layout (any of the outputs may be NULL).
+ * Replaces the per-generation cache readback (src/world/WorldGenerator.cu:798-815). */
+int blk_readback(blk_ctx* ctx, uint32_t env_begin, uint32_t n_envs, uint8_t* ids, uint8_t* light,
+    int16_t* height_map, uintptr_t stream);
+
+/* Waits for `stream` and reports any device-side flag raised since the last
+ * call (BLK_ERR_DEVICE_FLAG with a message). */
+int blk_sync(blk_ctx* ctx, uintptr_t stream);
+
+/* RGBA8 -> float32 NCHW with the alpha channel dropped, value * (1.0f/255.0f).
+ * Same signature and meaning as the reference's convertRgba8ToFloatNchw
+ * (src/environment/CudaObservation.h:7-8); both pointers are device memory.
+ * Returns a status instead of aborting. */
+int blk_convert_rgba8_to_float_nchw(const void* rgba8, float* nchw, uint32_t batch, uint32_t width, uint32_t height,
+    uintptr_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BLK_WORLD_H */
