@@ -77,6 +77,17 @@ class WorldViewsC(ctypes.Structure):
     ]
 
 
+class ProfileC(ctypes.Structure):
+    _fields_ = [
+        ("generate_prep_ms", ctypes.c_double),
+        ("generate_tiles_ms", ctypes.c_double),
+        ("edits_prep_ms", ctypes.c_double),
+        ("relight_ms", ctypes.c_double),
+        ("generate_calls", ctypes.c_uint64),
+        ("edit_calls", ctypes.c_uint64),
+    ]
+
+
 assert ctypes.sizeof(OverrideC) == 16
 
 # Every symbol include/blk_world.h declares, with its ctypes signature.
@@ -94,6 +105,8 @@ SIGNATURES = {
     "blk_sky_light_at_time": (ctypes.c_uint8, [_U32]),
     "blk_readback": (ctypes.c_int, [_VP, _U32, _U32, _VP, _VP, _VP, _UP]),
     "blk_sync": (ctypes.c_int, [_VP, _UP]),
+    "blk_profile_enable": (ctypes.c_int, [_VP, ctypes.c_int]),
+    "blk_profile_read": (ctypes.c_int, [_VP, ctypes.POINTER(ProfileC), ctypes.c_int]),
     "blk_convert_rgba8_to_float_nchw": (ctypes.c_int, [_VP, _VP, _U32, _U32, _U32, _UP]),
 }
 
@@ -101,7 +114,7 @@ SIGNATURES = {
 def load(path: str = LIB_PATH) -> ctypes.CDLL:
     if not os.path.exists(path):
         raise ImportError(
-            f"{path} is missing: build it with `python -m blocklab_b200.build` (nvcc, sm_100a). "
+            f"{path} is missing: build it with `python blocklab_b200/build.py` (nvcc, sm_100a). "
             "There is no CPU fallback for the world-state path.")
     lib = ctypes.CDLL(path)
     for name, (res, args) in SIGNATURES.items():

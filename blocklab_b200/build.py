@@ -1,6 +1,6 @@
 """Builds libblk_world.so in-tree for sm_100a with nvcc.
 
-    python -m blocklab_b200.build [--verbose-ptxas]
+    python blocklab_b200/build.py [--verbose-ptxas]
 
 The library is written next to this file (blocklab_b200/libblk_world.so) so it
 travels with the source tree; it is rebuilt when any source is newer.

@@ -686,6 +686,9 @@ int blk_ctx_destroy(blk_ctx* ctx)
         return BLK_OK;
     cudaSetDevice(ctx->device);
     cudaDeviceSynchronize();
+    for (auto& m : ctx->marks)
+        for (cudaEvent_t ev : m.e)
+            cudaEventDestroy(ev);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
         ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->flags };
@@ -743,6 +746,7 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
     const auto* ovr = static_cast<const blk_override*>(ovr_dev);
     const uint64_t n_cols = envs * ctx->columns_per_env;
     const RegionDims r = region(ctx);
+    const int mark = prof_begin(ctx, 0, st);
     BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
     if (n_overrides)
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
@@ -755,7 +759,9 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
         BLK_CUDA(cudaGetLastError(), "override kernels");
     }
     const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;
+    prof_mark(ctx, mark, 1, st);
     BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_tiles), st));
+    prof_mark(ctx, mark, 2, st);
     ctx->generated = true;
     return BLK_OK;
 }
@@ -807,6 +813,7 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     BLK_CHECK(stage_input(edits, static_cast<size_t>(n_edits) * sizeof(blk_override), ctx->edits, st, &e_dev));
     const auto* e = static_cast<const blk_override*>(e_dev);
     const uint32_t envs = ctx->cfg.num_envs;
+    const int mark = prof_begin(ctx, 1, st);
     BLK_CUDA(cudaMemsetAsync(ctx->edit_env_count, 0, (envs + 1) * sizeof(uint32_t), st), "memset edit counts");
     edit_count_kernel<<<grid_for(n_edits, 256), 256, 0, st>>>(e, n_edits, envs, ctx->edit_env_count);
     BLK_CHECK(exclusive_scan(ctx, ctx->edit_env_count, ctx->edit_env_offset, envs + 1, st));
@@ -832,7 +839,10 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     a.tiles_z = ctx->tiles_z;
     apply_edits_kernel<<<(envs + 127) / 128, 128, 0, st>>>(a);
     BLK_CUDA(cudaGetLastError(), "apply edits launch");
-    return launch_relight(ctx, st);
+    prof_mark(ctx, mark, 1, st);
+    BLK_CHECK(launch_relight(ctx, st));
+    prof_mark(ctx, mark, 2, st);
+    return BLK_OK;
 }
 
 int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t max_voxels, uint32_t* count,
@@ -957,6 +967,47 @@ int blk_sync(blk_ctx* ctx, uintptr_t stream_handle)
     return BLK_OK;
 }
 
+int blk_profile_enable(blk_ctx* ctx, int enable)
+{
+    if (!ctx) {
+        set_error("blk_profile_enable: null context");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    ctx->profiling = enable != 0;
+    return BLK_OK;
+}
+
+int blk_profile_read(blk_ctx* ctx, blk_profile* out, int reset)
+{
+    if (!ctx || !out) {
+        set_error("blk_profile_read: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    for (auto& m : ctx->marks) {
+        BLK_CUDA(cudaEventSynchronize(m.e[2]), "cudaEventSynchronize");
+        float a = 0.f, b = 0.f;
+        BLK_CUDA(cudaEventElapsedTime(&a, m.e[0], m.e[1]), "cudaEventElapsedTime");
+        BLK_CUDA(cudaEventElapsedTime(&b, m.e[1], m.e[2]), "cudaEventElapsedTime");
+        if (m.kind == 0) {
+            ctx->prof.generate_prep_ms += a;
+            ctx->prof.generate_tiles_ms += b;
+            ctx->prof.generate_calls += 1;
+        } else {
+            ctx->prof.edits_prep_ms += a;
+            ctx->prof.relight_ms += b;
+            ctx->prof.edit_calls += 1;
+        }
+        for (cudaEvent_t ev : m.e)
+            cudaEventDestroy(ev);
+    }
+    ctx->marks.clear();
+    *out = ctx->prof;
+    if (reset)
+        ctx->prof = blk_profile {};
+    return BLK_OK;
+}
+
 int blk_convert_rgba8_to_float_nchw(const void* rgba8, float* nchw, uint32_t batch, uint32_t width, uint32_t height,
     uintptr_t stream_handle)
 {
@@ -994,6 +1045,28 @@ int blk_convert_rgba8_to_float_nchw(const void* rgba8, float* nchw, uint32_t bat
 } // extern "C"
 
 namespace blk {
+
+int prof_begin(blk_ctx* ctx, int kind, cudaStream_t stream)
+{
+    if (!ctx->profiling)
+        return -1;
+    blk_ctx::Mark m {};
+    m.kind = kind;
+    for (cudaEvent_t& ev : m.e)
+        if (cudaEventCreate(&ev) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+    cudaEventRecord(m.e[0], stream);
+    ctx->marks.push_back(m);
+    return static_cast<int>(ctx->marks.size()) - 1;
+}
+
+void prof_mark(blk_ctx* ctx, int mark, int which, cudaStream_t stream)
+{
+    if (mark >= 0 && mark < static_cast<int>(ctx->marks.size()))
+        cudaEventRecord(ctx->marks[mark].e[which], stream);
+}
 
 int launch_relight(blk_ctx* ctx, cudaStream_t st)
 {

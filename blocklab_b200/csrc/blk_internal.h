@@ -8,6 +8,7 @@
 
 #include <cstdint>
 #include <string>
+#include <vector>
 
 struct blk_ctx {
     int device = 0;
@@ -43,6 +44,15 @@ struct blk_ctx {
 
     uint32_t* flags = nullptr;            // device error flag word
     uint32_t* h_flags = nullptr;          // pinned mirror
+
+    // Phase timing (blk_profile_*): event triples (start, mid, end) per call.
+    bool profiling = false;
+    struct Mark {
+        cudaEvent_t e[3];
+        int kind; // 0 generate, 1 edits
+    };
+    std::vector<Mark> marks;
+    blk_profile prof {};
 };
 
 namespace blk {
@@ -57,5 +67,9 @@ int stage_input(const void* src, size_t bytes, void* staging, cudaStream_t strea
 TerrainParams terrain_params(const blk_ctx* ctx);
 
 int launch_relight(blk_ctx* ctx, cudaStream_t stream);
+
+// Phase marks for blk_profile: begin() returns a mark index or -1 when off.
+int prof_begin(blk_ctx* ctx, int kind, cudaStream_t stream);
+void prof_mark(blk_ctx* ctx, int mark, int which, cudaStream_t stream);
 
 } // namespace blk

@@ -184,6 +184,15 @@ class WorldBatch:
         del keep
         return out
 
+    def profile(self, enable: bool) -> None:
+        """Turns per-phase CUDA-event timing on or off (events on the call's stream)."""
+        check(N.lib.blk_profile_enable(self._ctx, 1 if enable else 0))
+
+    def profile_read(self, reset: bool = True) -> dict:
+        p = N.ProfileC()
+        check(N.lib.blk_profile_read(self._ctx, ctypes.byref(p), 1 if reset else 0))
+        return {name: getattr(p, name) for name, _ in N.ProfileC._fields_}
+
     def sync(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         """Waits for the stream and raises if a kernel flagged an internal limit."""
         check(N.lib.blk_sync(self._ctx, _stream_handle(stream, self.device)))

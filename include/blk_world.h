@@ -166,6 +166,23 @@ int blk_readback(blk_ctx* ctx, uint32_t env_begin, uint32_t n_envs, uint8_t* ids
  * call (BLK_ERR_DEVICE_FLAG with a message). */
 int blk_sync(blk_ctx* ctx, uintptr_t stream);
 
+/* Per-phase device timing (CUDA events recorded on the call's own stream
+ * around each phase while enabled). The reference has no tracing of its own;
+ * this replaces ad-hoc timing of its benchmark (src/app/benchmark.cpp:341-377). */
+typedef struct blk_profile {
+    double generate_prep_ms;  /* override column-CSR build of blk_generate */
+    double generate_tiles_ms; /* fused generation + light tile kernel */
+    double edits_prep_ms;     /* edit grouping + setBlock application */
+    double relight_ms;        /* dirty-window compaction + relight tile kernel */
+    uint64_t generate_calls;
+    uint64_t edit_calls;
+} blk_profile;
+
+int blk_profile_enable(blk_ctx* ctx, int enable);
+/* Waits for the recorded events and returns the accumulated times; reset != 0
+ * clears the accumulators afterwards. */
+int blk_profile_read(blk_ctx* ctx, blk_profile* out, int reset);
+
 /* RGBA8 -> float32 NCHW with the alpha channel dropped, value * (1.0f/255.0f).
  * Same signature and meaning as the reference's convertRgba8ToFloatNchw
  * (src/environment/CudaObservation.h:7-8); both pointers are device memory.

@@ -22,6 +22,7 @@ import contextlib
 import ctypes
 import os
 from dataclasses import dataclass
+from typing import Optional
 
 import numpy as np
 
@@ -216,7 +217,8 @@ class Reference:
             self.lib = _load(os.path.join(HERE, "_ref", f"libref_{kind}.so"))
         self.kind = kind
 
-    def generate(self, seed: int, origin, size, ovr_xyz=None, ovr_block=None, runs: int = 2, max_voxels: int = 0):
+    def generate(self, seed: int, origin, size, ovr_xyz=None, ovr_block=None, runs: int = 2, max_voxels: int = 0,
+                 timing: Optional[list] = None):
         W, H, D = size
         xyz = np.ascontiguousarray(np.zeros((0, 3), np.int32) if ovr_xyz is None else ovr_xyz, np.int32)
         blk = np.ascontiguousarray(np.zeros(0, np.uint8) if ovr_block is None else ovr_block, np.uint8)
@@ -228,13 +230,17 @@ class Reference:
         vox = np.zeros(max(max_voxels, 1) * 3, np.uint32)
         cnt = np.zeros(1, np.uint32)
         hdr = np.zeros(3, np.int32)
+        last_ms = ctypes.c_double(0.0)
         rc = self.lib.ref_generate(ctypes.c_uint32(seed & 0xFFFFFFFF), ctypes.c_int32(origin[0]),
                                    ctypes.c_int32(origin[1]), ctypes.c_int32(origin[2]), ctypes.c_uint32(W),
                                    ctypes.c_uint32(H), ctypes.c_uint32(D), _ptr(xyz), _ptr(blk),
                                    ctypes.c_uint32(len(blk)), ctypes.c_int32(runs), _ptr(b), _ptr(bl), _ptr(sl),
-                                   _ptr(hm), _ptr(vox), ctypes.c_uint32(max_voxels), _ptr(cnt), _ptr(hdr))
+                                   _ptr(hm), _ptr(vox), ctypes.c_uint32(max_voxels), _ptr(cnt), _ptr(hdr),
+                                   ctypes.byref(last_ms))
         if rc != 0:
             raise RuntimeError(f"reference generate failed: {rc}")
+        if timing is not None:
+            timing.append(last_ms.value)
         sh = (D, H, W)
         n = int(min(cnt[0], max_voxels))
         return dict(blocks=b.reshape(sh), block_light=bl.reshape(sh), sky_light=sl.reshape(sh),

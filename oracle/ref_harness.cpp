@@ -21,6 +21,7 @@
 
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <memory>
@@ -57,6 +58,7 @@ extern "C" {
 //   out_block/out_block_light/out_sky_light: W*H*D bytes, index x + W*(y + H*z)
 //   out_height_map: W*D int8, index x + W*z
 //   out_voxels: max_voxels * 12 bytes (may be null when max_voxels == 0)
+//   out_last_ms: wall time of the last generation including its readback (may be null)
 // Returns 0 on success.
 int ref_generate(std::uint32_t seed, std::int32_t origin_x, std::int32_t origin_y, std::int32_t origin_z,
     std::uint32_t width, std::uint32_t height, std::uint32_t depth,
@@ -64,7 +66,8 @@ int ref_generate(std::uint32_t seed, std::int32_t origin_x, std::int32_t origin_
     std::int32_t runs,
     std::uint8_t* out_block, std::uint8_t* out_block_light, std::uint8_t* out_sky_light,
     std::int8_t* out_height_map,
-    void* out_voxels, std::uint32_t max_voxels, std::uint32_t* out_voxel_count, std::int32_t* out_header)
+    void* out_voxels, std::uint32_t max_voxels, std::uint32_t* out_voxel_count, std::int32_t* out_header,
+    double* out_last_ms)
 {
     using namespace blocklab;
     std::vector<BlockOverride> overrides(n_overrides);
@@ -90,6 +93,7 @@ int ref_generate(std::uint32_t seed, std::int32_t origin_x, std::int32_t origin_
     CPUCacheGenerationBuffers cache;
     std::uint32_t voxel_count = 0;
     for (std::int32_t r = 0; r < (runs < 1 ? 1 : runs); ++r) {
+        const auto t0 = std::chrono::steady_clock::now();
         WorldGenerationBuffers buffers {
             .terrain = {
                 .header = static_cast<TerrainHeader*>(header.ptr),
@@ -102,6 +106,8 @@ int ref_generate(std::uint32_t seed, std::int32_t origin_x, std::int32_t origin_
         WorldGenerationOutput& out = future.get();
         voxel_count = out.voxelCount;
         cache = std::move(out.buffers.cpuCache);
+        if (out_last_ms)
+            *out_last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     }
 
     for (std::size_t i = 0; i < volume; ++i) {

@@ -1,0 +1,433 @@
+"""GPU parity tests of the world-state path through the C ABI.
+
+Every comparison is bit-exact (integer block ids and 4-bit light levels; the
+observation conversion is compared as float bit patterns). The oracle is the
+C++ restatement pinned to the reference (tests/test_oracle.py); the committed
+golden fixture holds the reference's own output for its lighting tests.
+At full benchmark size the light field is checked through the fixed-point
+equations it uniquely satisfies (see _fixed_point_ok).
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle.oracle import TERRAIN_FBM, TERRAIN_FLAT, TERRAIN_REFERENCE, WorldSpec
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import scenarios as S  # noqa: E402
+
+GOLDEN = os.path.join(HERE, "golden", "lighting_scenarios.npz")
+
+
+@pytest.fixture(scope="module")
+def B():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import blocklab_b200
+
+    return blocklab_b200
+
+
+def _dev_world(wb, env):
+    """Device arrays of one env in the reference layout (D, H, W)."""
+    ids = wb.ids[env].cpu().numpy().transpose(0, 2, 1)
+    light = wb.light[env].cpu().numpy().transpose(0, 2, 1)
+    return ids, light & 15, light >> 4, wb.height_map[env].cpu().numpy()
+
+
+def _assert_world(wb, env, blocks, bl, sl, hm, label=""):
+    ids, gbl, gsl, ghm = _dev_world(wb, env)
+    assert np.array_equal(ids, blocks), f"{label} ids differ at {np.argwhere(ids != blocks)[:5].tolist()}"
+    assert np.array_equal(ghm, hm), f"{label} height map differs"
+    assert np.array_equal(gbl, bl), f"{label} block light differs at {np.argwhere(gbl != bl)[:5].tolist()}"
+    assert np.array_equal(gsl, sl), f"{label} sky light differs at {np.argwhere(gsl != sl)[:5].tolist()}"
+
+
+def _xyz(ovr):
+    return np.stack([ovr["x"], ovr["y"], ovr["z"]], 1)
+
+
+# ------------------------------------------------------------ conversion --
+@pytest.mark.parametrize("shape", [(128, 90, 160), (7, 84, 84), (3, 9, 13), (1, 1, 1), (2, 90, 160)])
+def test_convert_bit_exact(B, oracle, shape):
+    n, h, w = shape
+    rng = np.random.default_rng(n * 1000 + h)
+    rgba = rng.integers(0, 256, (n, h, w, 4), dtype=np.uint8)
+    out = B.convert_rgba8_to_float_nchw(torch.from_numpy(rgba).cuda()).cpu().numpy()
+    assert np.array_equal(out.view(np.uint32), oracle.convert_rgba8(rgba).view(np.uint32))
+
+
+def test_convert_every_byte_and_unaligned(B, oracle):
+    rgba = np.tile(np.arange(256, dtype=np.uint8)[None, None, :, None], (1, 3, 1, 4)).copy()
+    rgba[..., 1] = 255 - rgba[..., 1]
+    dev = torch.from_numpy(rgba).cuda()
+    out = B.convert_rgba8_to_float_nchw(dev).cpu().numpy()
+    assert np.array_equal(out.view(np.uint32), oracle.convert_rgba8(rgba).view(np.uint32))
+    # unaligned source (offset by one pixel) takes the scalar path
+    big = torch.from_numpy(np.concatenate([rgba.reshape(-1, 4)[:1], rgba.reshape(-1, 4)])).cuda()
+    view = big[1:].reshape(1, 3, 256, 4)
+    out2 = torch.empty((1, 3, 3, 256), dtype=torch.float32, device="cuda")
+    from blocklab_b200 import _native as N
+
+    N.check(N.lib.blk_convert_rgba8_to_float_nchw(view.data_ptr(), out2.data_ptr(), 1, 256, 3, 0))
+    torch.cuda.synchronize()
+    assert np.array_equal(out2.cpu().numpy().view(np.uint32), oracle.convert_rgba8(rgba).view(np.uint32))
+
+
+# ------------------------------------------------------------ generation --
+def test_config0_fbm_with_torches_matches_oracle(B, oracle):
+    """Config 0: 64 x 64 x 128, fBm seed 1, 200 surface torches (per-source oracle)."""
+    cfg = B.WorldConfig(num_envs=1, width=64, height=128, depth=64)
+    wb = B.WorldBatch(cfg)
+    spec = WorldSpec(1, 64, 128, 64)
+    t = oracle.place_torches(spec, 200, B.torch_key(1))
+    assert len(t) == 200
+    wb.generate([1], B.make_overrides(t, B.TORCH))
+    wb.sync()
+    blocks, bl, sl, hm = oracle.generate(spec, t, np.full(len(t), 4, np.uint8), method="per_source")
+    _assert_world(wb, 0, blocks, bl, sl, hm, "config0")
+    assert (bl > 0).sum() > 10000
+    wb.close()
+
+
+def test_device_torch_placement_matches_oracle(B, oracle):
+    cfg = B.WorldConfig(num_envs=3, width=96, height=128, depth=80)
+    wb = B.WorldBatch(cfg)
+    seeds = np.array([1, 2, 99], np.uint32)
+    dev = wb.place_torches(seeds, 300).cpu().numpy().view(B.OVERRIDE_DTYPE)
+    assert len(dev) == 900
+    for e, s in enumerate(seeds):
+        spec = WorldSpec(int(s), 96, 128, 80)
+        want = oracle.place_torches(spec, 300, B.torch_key(int(s)))
+        got = dev[(dev["env"] == e) & (dev["y"] > -(1 << 30))]
+        assert np.array_equal(_xyz(got), want)
+    wb.close()
+
+
+@pytest.mark.parametrize("terrain,base,amp", [(TERRAIN_FBM, 40, 50.0), (TERRAIN_FLAT, 20, 0.0),
+                                             (TERRAIN_FBM, 60, 120.0)])
+def test_random_overrides_match_oracle(B, oracle, terrain, base, amp):
+    """Caves, floating stone, torches everywhere; ragged tile edges (W, D not multiples of 32)."""
+    W, H, D, E = 77, 128, 45, 3
+    cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, origin=(-10, 0, 5), terrain=terrain, base=base,
+                        amplitude=amp)
+    wb = B.WorldBatch(cfg)
+    rng = np.random.default_rng(base)
+    seeds = rng.integers(1, 1 << 31, E).astype(np.uint32)
+    lists, per = [], []
+    for e in range(E):
+        n = 6000
+        cells = rng.choice(W * H * D, n, replace=False)
+        xyz = np.stack([cells % W - 10, (cells // W) % H, cells // (W * H) + 5], 1)
+        blk = rng.choice([0, 3, 4, 1, 2], n, p=[0.5, 0.3, 0.1, 0.05, 0.05]).astype(np.uint8)
+        per.append((xyz, blk))
+        lists.append(B.make_overrides(xyz, blk, env=e))
+    wb.generate(seeds, np.concatenate(lists))
+    wb.sync()
+    for e in range(E):
+        spec = WorldSpec(int(seeds[e]), W, H, D, origin=(-10, 0, 5), terrain=terrain, base=base, amplitude=amp)
+        blocks, bl, sl, hm = oracle.generate(spec, *per[e], method="multi")
+        _assert_world(wb, e, blocks, bl, sl, hm, f"env{e}")
+    wb.close()
+
+
+def test_duplicates_outside_and_invalid_overrides(B, oracle):
+    """Latest duplicate wins; overrides outside the region or with unknown ids are ignored."""
+    cfg = B.WorldConfig(num_envs=2, width=40, height=64, depth=33, terrain=TERRAIN_FLAT, base=20)
+    wb = B.WorldBatch(cfg)
+    o = B.make_overrides([[5, 21, 5], [5, 21, 5], [5, 21, 5], [-1, 21, 5], [5, 64, 5], [5, 25, 40], [6, 21, 6],
+                          [7, 21, 7], [1, 21, 1]],
+                         [3, 0, 4, 4, 4, 4, 9, 3, 4], env=[0, 0, 0, 0, 0, 0, 0, 5, 1])
+    wb.generate([3, 4], o)
+    wb.sync()
+    spec = WorldSpec(3, 40, 64, 33, terrain=TERRAIN_FLAT, base=20)
+    blocks, bl, sl, hm = oracle.generate(spec, [[5, 21, 5]], [4], method="multi")
+    _assert_world(wb, 0, blocks, bl, sl, hm, "env0")
+    spec = WorldSpec(4, 40, 64, 33, terrain=TERRAIN_FLAT, base=20)
+    blocks, bl, sl, hm = oracle.generate(spec, [[1, 21, 1]], [4], method="multi")
+    _assert_world(wb, 1, blocks, bl, sl, hm, "env1")
+    wb.close()
+
+
+@pytest.mark.parametrize("base", [-5, 200, 31])
+def test_empty_and_full_worlds(B, oracle, base):
+    cfg = B.WorldConfig(num_envs=1, width=33, height=32, depth=31, terrain=TERRAIN_FLAT, base=base)
+    wb = B.WorldBatch(cfg)
+    wb.generate([1], B.make_overrides([[0, 0, 0], [32, 31, 30]], B.TORCH))
+    wb.sync()
+    spec = WorldSpec(1, 33, 32, 31, terrain=TERRAIN_FLAT, base=base)
+    blocks, bl, sl, hm = oracle.generate(spec, [[0, 0, 0], [32, 31, 30]], [4, 4], method="per_source")
+    _assert_world(wb, 0, blocks, bl, sl, hm, f"base{base}")
+    wb.close()
+
+
+def test_tiny_world(B, oracle):
+    cfg = B.WorldConfig(num_envs=2, width=1, height=32, depth=1, terrain=TERRAIN_FLAT, base=3)
+    wb = B.WorldBatch(cfg)
+    wb.generate([1, 2], B.make_overrides([[0, 10, 0], [0, 2, 0]], [4, 0], env=[0, 1]))
+    wb.sync()
+    for e, (xyz, blk) in enumerate([([[0, 10, 0]], [4]), ([[0, 2, 0]], [0])]):
+        spec = WorldSpec(e + 1, 1, 32, 1, terrain=TERRAIN_FLAT, base=3)
+        _assert_world(wb, e, *oracle.generate(spec, xyz, blk, method="per_source"), f"env{e}")
+    wb.close()
+
+
+# ------------------------------------------------ reference golden fixture --
+def test_reference_lighting_scenarios(B):
+    """The 13 generations of the reference's lighting tests, against the
+    reference's own output (fixture made by tests/golden/make_golden.py)."""
+    if not os.path.exists(GOLDEN):
+        pytest.skip("golden fixture missing")
+    g = np.load(GOLDEN)
+    names = sorted({k[: -len("_xyz")] for k in g.files if k.endswith("_xyz")})
+    cfg = B.WorldConfig(num_envs=len(names), width=64, height=32, depth=64, origin=S.ORIGIN,
+                        terrain=B.TERRAIN_REFERENCE)
+    wb = B.WorldBatch(cfg)
+    lists = [B.make_overrides(g[n + "_xyz"], g[n + "_blk"], env=i) for i, n in enumerate(names)]
+    wb.generate(np.full(len(names), 23, np.uint32), np.concatenate(lists))
+    wb.sync()
+    for i, n in enumerate(names):
+        _assert_world(wb, i, g[n + "_blocks"], g[n + "_block_light"], g[n + "_sky_light"], g[n + "_height_map"], n)
+        vox, cnt, hdr = wb.render_voxels(i)
+        v = vox.cpu().numpy().view(np.uint32)
+        assert hdr == S.ORIGIN
+        assert np.array_equal(v[np.lexsort((v[:, 2], v[:, 1], v[:, 0]))], g[n + "_voxels"]), n
+    wb.close()
+
+
+def test_reference_terrain_matches_reference_cuda_build(B):
+    """Reference-terrain mode (fast __sinf/__cosf) against the reference's own sm_100a build."""
+    from oracle.oracle import Reference, ref_available
+
+    if not ref_available("cuda"):
+        pytest.skip("reference CUDA build not present")
+    R = Reference("cuda")
+    seeds = [1, 17, 23, 4242, 99991]
+    cfg = B.WorldConfig(num_envs=len(seeds), width=64, height=32, depth=64, origin=(-32, 0, -32),
+                        terrain=B.TERRAIN_REFERENCE)
+    wb = B.WorldBatch(cfg)
+    wb.generate(np.array(seeds, np.uint32))
+    wb.sync()
+    for e, s in enumerate(seeds):
+        r = R.generate(s, (-32, 0, -32), (64, 32, 64), max_voxels=64 * 32 * 64)
+        _assert_world(wb, e, r["blocks"], r["block_light"], r["sky_light"], r["height_map"], f"seed{s}")
+    wb.close()
+
+
+# ------------------------------------------------------ edits and relight --
+def _edit_batch(rng, E, W, H, D, n, origin, hm_list):
+    lists, local = [], []
+    for e in range(E):
+        x = rng.integers(0, W, n)
+        z = rng.integers(0, D, n)
+        y = np.clip(hm_list[e][z, x] - origin[1] + rng.integers(-8, 9, n), -2, H + 1)
+        kind = (rng.random(n) < 0.05).astype(np.uint8)
+        blk = rng.choice([0, 3, 4], n, p=[0.47, 0.47, 0.06]).astype(np.uint8)
+        xyz = np.stack([x, y, z], 1)
+        local.append((xyz, kind, blk))
+        lists.append(B_make(xyz + np.array(origin), blk, e, kind))
+    return np.concatenate(lists), local
+
+
+def B_make(xyz, blk, env, kind):
+    import blocklab_b200 as B
+
+    return B.make_overrides(xyz, blk, env=env, kind=kind)
+
+
+@pytest.mark.parametrize("W,H,D", [(64, 32, 64), (96, 128, 70)])
+def test_edit_sequences_relight_exactly(B, oracle, W, H, D):
+    """Dig / place / torch add / remove-torch edits near the surface, several
+    steps, World::setBlock semantics incl. torch support; relit light must equal
+    a full relight of the edited world."""
+    E = 3
+    origin = (-5, 0, 9)
+    cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, origin=origin, terrain=TERRAIN_FBM, base=H // 3,
+                        amplitude=H / 4)
+    wb = B.WorldBatch(cfg)
+    rng = np.random.default_rng(W + H)
+    seeds = rng.integers(1, 1 << 31, E).astype(np.uint32)
+    specs = [WorldSpec(int(s), W, H, D, origin=origin, terrain=TERRAIN_FBM, base=H // 3, amplitude=H / 4)
+             for s in seeds]
+    torches = [oracle.place_torches(sp, 40, B.torch_key(int(s))) for sp, s in zip(specs, seeds)]
+    wb.generate(seeds, np.concatenate([B.make_overrides(t, B.TORCH, env=e) for e, t in enumerate(torches)]))
+    state = []
+    for e in range(E):
+        blocks, hm = oracle.build_blocks(specs[e], torches[e], np.full(len(torches[e]), 4, np.uint8))
+        state.append([blocks, hm])
+    for step in range(4):
+        edits, local = _edit_batch(rng, E, W, H, D, 60, origin, [s[1] for s in state])
+        wb.apply_edits(edits)
+        wb.sync()
+        for e in range(E):
+            xyz, kind, blk = local[e]
+            oracle.apply_edits(state[e][0], state[e][1], xyz, kind, blk, origin_y=origin[1])
+            bl, sl = oracle.light(state[e][0], state[e][1], origin[1], "multi")
+            _assert_world(wb, e, state[e][0], bl, sl, state[e][1], f"step{step} env{e}")
+    wb.close()
+
+
+def test_edits_support_removal_and_heightmap(B, oracle):
+    """Digging the block under a torch removes the torch; digging the top block
+    lowers the height map (cells below become lit); placing above raises it."""
+    cfg = B.WorldConfig(num_envs=1, width=40, height=32, depth=40, terrain=TERRAIN_FLAT, base=10)
+    wb = B.WorldBatch(cfg)
+    wb.generate([1], B.make_overrides([[20, 11, 20]], B.TORCH))
+    blocks, hm = oracle.build_blocks(WorldSpec(1, 40, 32, 40, terrain=TERRAIN_FLAT, base=10), [[20, 11, 20]], [4])
+    steps = [
+        ([[20, 10, 20]], [0], [0]),                      # dig the support: torch goes too
+        ([[5, 10, 5], [5, 9, 5], [5, 8, 5]], [0, 0, 0], [0, 0, 0]),  # shaft, lowers the top
+        ([[30, 25, 30]], [3], [0]),                      # floating stone raises the top
+        ([[30, 25, 30], [31, 12, 31]], [0, 4], [1, 0]),  # remove-torch on stone is a no-op; new torch
+        ([[31, 12, 31]], [0], [1]),                      # remove the torch
+    ]
+    for xyz, blk, kind in steps:
+        xyz = np.array(xyz)
+        wb.apply_edits(B.make_overrides(xyz, np.array(blk, np.uint8), env=0, kind=np.array(kind, np.uint8)))
+        wb.sync()
+        oracle.apply_edits(blocks, hm, xyz, np.array(kind, np.uint8), np.array(blk, np.uint8))
+        bl, sl = oracle.light(blocks, hm, 0, "per_source")
+        _assert_world(wb, 0, blocks, bl, sl, hm, str(xyz.tolist()))
+    wb.close()
+
+
+def test_apply_edits_requires_generate_and_capacity(B):
+    cfg = B.WorldConfig(num_envs=1, width=32, height=32, depth=32, max_overrides=4, max_edits=2)
+    wb = B.WorldBatch(cfg)
+    with pytest.raises(B.BlkError) as ei:
+        wb.apply_edits(B.make_overrides([[1, 1, 1]], 0))
+    assert ei.value.status == 6
+    with pytest.raises(B.BlkError) as ei:
+        wb.generate([1], B.make_overrides(np.zeros((5, 3), np.int32), 0))
+    assert ei.value.status == 4
+    wb.generate([1], B.make_overrides(np.zeros((4, 3), np.int32), 0))
+    with pytest.raises(B.BlkError) as ei:
+        wb.apply_edits(B.make_overrides(np.zeros((3, 3), np.int32), 0))
+    assert ei.value.status == 4
+    wb.sync()
+    wb.close()
+
+
+# ------------------------------------------------ voxels and day/night --
+def test_render_voxels_match_oracle(B, oracle):
+    cfg = B.WorldConfig(num_envs=2, width=64, height=64, depth=48, terrain=TERRAIN_FBM, base=25, amplitude=15.0)
+    wb = B.WorldBatch(cfg)
+    rng = np.random.default_rng(11)
+    lists, per = [], []
+    for e in range(2):
+        n = 800
+        cells = rng.choice(64 * 64 * 48, n, replace=False)
+        xyz = np.stack([cells % 64, (cells // 64) % 64, cells // (64 * 64)], 1)
+        blk = rng.choice([0, 3, 4], n).astype(np.uint8)
+        per.append((xyz, blk))
+        lists.append(B.make_overrides(xyz, blk, env=e))
+    wb.generate([5, 6], np.concatenate(lists))
+    for e in range(2):
+        spec = WorldSpec(5 + e, 64, 64, 48, terrain=TERRAIN_FBM, base=25, amplitude=15.0)
+        blocks, bl, sl, hm = oracle.generate(spec, *per[e], method="multi")
+        want = oracle.render_voxels(blocks, bl, sl)
+        got, n, hdr = wb.render_voxels(e)
+        assert n == len(want) and hdr == (0, 0, 0)
+        assert np.array_equal(got.cpu().numpy().view(np.uint32), want)
+        # a too-small buffer reports the full count and writes a prefix
+        got2, n2, _ = wb.render_voxels(e, max_voxels=100)
+        assert n2 == n and np.array_equal(got2.cpu().numpy().view(np.uint32), want[:100])
+    wb.close()
+
+
+def test_effective_light(B):
+    cfg = B.WorldConfig(num_envs=12, width=32, height=64, depth=32)
+    wb = B.WorldBatch(cfg)
+    seeds = np.arange(12, dtype=np.uint32)
+    wb.generate(seeds, wb.place_torches(seeds, 20))
+    ticks = np.linspace(11000, 24000, 12).astype(int)
+    dim = np.array([B.sky_light_dimming(int(t)) for t in ticks], np.uint8)
+    out = wb.effective_light(dim).cpu().numpy()
+    light = wb.light.cpu().numpy()
+    sky = light >> 4
+    want = ((sky - np.minimum(sky, dim[:, None, None, None])) << 4) | (light & 15)
+    assert np.array_equal(out, want.astype(np.uint8))
+    assert set(dim.tolist()) >= {0, 11}
+    wb.close()
+
+
+# --------------------------------------------------- full benchmark size --
+def _fixed_point_ok(ids, light, hmap, origin_y=0):
+    """Light satisfies L = opaque ? 0 : max(src, max_N6 L - 1, 0) at every cell
+    (cells outside the region count as opaque). This equation has exactly one
+    solution: any positive level needs a neighbour one higher, so it is
+    supported by a chain to a source and cannot exceed 15 - distance, and the
+    equation forces at least 15 - distance. ids/light are (D, W, H) tensors."""
+    opaque = (ids != 0) & (ids != 4)
+
+    def nmax(L):
+        P = F.pad(L, (1, 1, 1, 1, 1, 1))
+        return torch.stack([P[:-2, 1:-1, 1:-1], P[2:, 1:-1, 1:-1], P[1:-1, :-2, 1:-1], P[1:-1, 2:, 1:-1],
+                            P[1:-1, 1:-1, :-2], P[1:-1, 1:-1, 2:]]).amax(0)
+
+    bl = (light & 15).to(torch.int16)
+    sl = (light >> 4).to(torch.int16)
+    zero = torch.zeros_like(bl)
+    src_b = (ids == 4).to(torch.int16) * 15
+    exp_b = torch.where(opaque, zero, torch.maximum(src_b, (nmax(bl) - 1).clamp(min=0)))
+    y = torch.arange(ids.shape[2], device=ids.device, dtype=torch.int16) + origin_y
+    lit = (y[None, None, :] > hmap[:, :, None]).to(torch.int16) * 15
+    exp_s = torch.where(opaque, zero, torch.maximum(lit, (nmax(sl) - 1).clamp(min=0)))
+    top = torch.where(opaque, y[None, None, :].expand_as(bl), torch.full_like(bl, -1)).amax(2)
+    return bool((exp_b == bl).all()) and bool((exp_s == sl).all()) and bool((top.clamp(min=-1) == hmap).all())
+
+
+def test_full_size_config1(B, oracle):
+    """Benchmark size: 128 envs of 256 x 256 x 128 with 1000 torches each.
+    Every env satisfies the light fixed point; two envs are compared
+    cell-for-cell with the oracle."""
+    cfg = B.WorldConfig(num_envs=128, width=256, height=128, depth=256, max_overrides=128 * 1000)
+    wb = B.WorldBatch(cfg)
+    seeds = np.arange(1, 129, dtype=np.uint32)
+    t = wb.place_torches(seeds, 1000)
+    wb.generate(seeds, t)
+    wb.sync()
+    for e in range(128):
+        assert _fixed_point_ok(wb.ids[e], wb.light[e], wb.height_map[e]), f"env {e}"
+    assert int((wb.ids == 4).sum()) == 128 * 1000
+    tn = t.cpu().numpy().view(B.OVERRIDE_DTYPE)
+    for e in (0, 77):
+        sel = tn[(tn["env"] == e) & (tn["y"] > -(1 << 30))]
+        spec = WorldSpec(int(seeds[e]), 256, 128, 256)
+        blocks, bl, sl, hm = oracle.generate(spec, _xyz(sel), sel["block"], method="multi")
+        _assert_world(wb, e, blocks, bl, sl, hm, f"env{e}")
+    wb.close()
+
+
+def test_full_size_incremental_steps_fixed_point(B):
+    """Config-2 shaped incremental steps (128^3 worlds, ~10 edits per env per
+    step) keep the light field at its fixed point."""
+    E = 64
+    cfg = B.WorldConfig(num_envs=E, width=128, height=128, depth=128, max_edits=1 << 14)
+    wb = B.WorldBatch(cfg)
+    seeds = np.arange(E, dtype=np.uint32) + 7
+    wb.generate(seeds, wb.place_torches(seeds, 200))
+    rng = np.random.default_rng(2)
+    hm = wb.height_map.cpu().numpy()
+    for step in range(5):
+        n = 10 * E
+        env = rng.integers(0, E, n)
+        x, z = rng.integers(0, 128, n), rng.integers(0, 128, n)
+        y = hm[env, z, x] + rng.integers(-8, 9, n)
+        r = rng.random(n)
+        blk = np.where(r < 0.45, 0, np.where(r < 0.9, 3, 4)).astype(np.uint8)
+        kind = (r >= 0.95).astype(np.uint8)
+        order = np.argsort(env, kind="stable")
+        wb.apply_edits(B.make_overrides(np.stack([x, y, z], 1)[order], blk[order], env=env[order],
+                                        kind=kind[order]))
+    wb.sync()
+    for e in range(E):
+        assert _fixed_point_ok(wb.ids[e], wb.light[e], wb.height_map[e]), f"env {e}"
+    wb.close()

@@ -1,0 +1,206 @@
+"""CPU tests: the oracle pinned to the reference and to the reference's own tests.
+
+- hash known-answer / determinism tests (reference tests/Hash.cpp:11-30);
+- golden light masks of tests/WorldLighting.cpp, through the committed
+  fixture produced by the reference itself and, where the reference sources
+  are present, re-parsed from the reference test file;
+- restatement vs the reference's own build (oracle/_ref) on random worlds;
+- the per-source restatement vs the independent multi-source formulation;
+- render voxel list, observation conversion and sky curve vs the reference.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from oracle.oracle import TERRAIN_FBM, TERRAIN_FLAT, TERRAIN_REFERENCE, WorldSpec
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import scenarios as S  # noqa: E402
+
+REFERENCE = "/root/reference"
+GOLDEN = os.path.join(HERE, "golden", "lighting_scenarios.npz")
+
+
+def test_hash_combine_deterministic_and_order_sensitive(oracle):
+    # reference tests/Hash.cpp:11-16
+    assert oracle.hash_combine(1, 2, 3) == oracle.hash_combine(1, 2, 3)
+    assert oracle.hash_combine(1, 2, 3) != oracle.hash_combine(1, 3, 2)
+    assert oracle.hash_combine(1, oracle.hash_combine(2, 3)) == oracle.hash_combine(1, 2, 3)
+
+
+def test_hash_known_values(oracle):
+    # reference tests/Hash.cpp:18-22 plus values of the src/utility/Hash.h formulas
+    assert oracle.hash(42) == oracle.hash(42) != 42
+    assert oracle.hash(0) == 0
+    a, b = 1, 2
+    a ^= (b + 0x9E3779B9 + ((a << 6) & 0xFFFFFFFF) + (a >> 2)) & 0xFFFFFFFF
+    assert oracle.hash_combine(1, 2) == a & 0xFFFFFFFF
+    for seed in (0, 1, 23, 0xFFFFFFFF):
+        off = oracle.seed_offset(seed, 0x4F1BBC21)
+        assert -4096 <= off <= 4096
+
+
+def test_sky_light_curve(oracle):
+    # src/world/Lighting.cpp:21-49 with src/world/WorldTime.h:10-18
+    assert oracle.sky_light_at_time(0) == 15
+    assert oracle.sky_light_at_time(11999) == 15
+    assert oracle.sky_light_at_time(12000) == 15
+    assert oracle.sky_light_at_time(13702) == 4
+    assert oracle.sky_light_at_time(20000) == 4
+    assert oracle.sky_light_at_time(22300) == 4
+    assert oracle.sky_light_at_time(23961) == 15
+    assert oracle.sky_light_at_time(23999) == 15
+    vals = [oracle.sky_light_at_time(t) for t in range(24000)]
+    assert min(vals) == 4 and max(vals) == 15
+    assert all(vals[t] >= vals[t + 1] for t in range(12000, 13702))
+    assert all(vals[t] <= vals[t + 1] for t in range(22300, 23961))
+
+
+def _golden():
+    if not os.path.exists(GOLDEN):
+        pytest.skip("golden fixture missing")
+    return np.load(GOLDEN)
+
+
+def _golden_keys(g):
+    return sorted({k.rsplit("_", 1)[0] if not k.endswith(("_block_light", "_sky_light", "_height_map"))
+                   else k.rsplit("_", 2)[0] for k in g.files})
+
+
+@pytest.mark.parametrize("method", ["per_source", "multi"])
+def test_oracle_matches_reference_lighting_scenarios(oracle, method):
+    """The restatement reproduces the reference's output on every generation of
+    the reference's lighting tests (fixture made by the reference itself)."""
+    g = _golden()
+    names = sorted({k[: -len("_xyz")] for k in g.files if k.endswith("_xyz")})
+    assert len(names) == 13
+    spec = WorldSpec(23, 64, 32, 64, origin=S.ORIGIN, terrain=TERRAIN_REFERENCE)
+    for n in names:
+        blocks, bl, sl, hm = oracle.generate(spec, g[n + "_xyz"], g[n + "_blk"], method=method)
+        assert np.array_equal(blocks, g[n + "_blocks"]), n
+        assert np.array_equal(hm, g[n + "_height_map"]), n
+        assert np.array_equal(bl, g[n + "_block_light"]), n
+        assert np.array_equal(sl, g[n + "_sky_light"]), n
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REFERENCE, "tests", "WorldLighting.cpp")),
+                    reason="reference sources not present")
+def test_oracle_matches_reference_masks(oracle):
+    """Masks parsed from the reference test file, checked on the restatement."""
+    masks = S.parse_masks(os.path.join(REFERENCE, "tests", "WorldLighting.cpp"))
+    spec = WorldSpec(23, 64, 32, 64, origin=S.ORIGIN, terrain=TERRAIN_REFERENCE)
+    base, _ = oracle.build_blocks(spec)
+    i = 0
+    for name, gen, xyz, blk, checks in S.scenarios(base):
+        blocks, bl, sl, hm = oracle.generate(spec, xyz, blk)
+        for origin, size in checks:
+            assert S.check_mask(blocks, bl, origin, size, masks[i]) == [], (name, gen)
+            i += 1
+    assert i == len(masks) == 15
+
+
+def test_golden_masks_spot_values():
+    """A few literal values of the reference masks (tests/WorldLighting.cpp:57-121)."""
+    g = _golden()
+    bl = g["explicit_torch_volume_0_block_light"]
+
+    def at(x, y, z):
+        return int(bl[z - S.ORIGIN[2], y - S.ORIGIN[1], x - S.ORIGIN[0]])
+
+    assert at(0, 16, 0) == 15
+    assert at(3, 16, 0) == 12
+    assert at(11, 16, 0) == 4
+    assert at(-3, 13, -3) == 6
+    assert at(15, 16, 0) == 0
+
+
+def _random_world(rng, W, H, D, n, origin=(0, 0, 0)):
+    cells = rng.choice(W * H * D, n, replace=False)
+    x, y, z = cells % W, (cells // W) % H, cells // (W * H)
+    xyz = np.stack([x + origin[0], y + origin[1], z + origin[2]], 1).astype(np.int32)
+    blk = rng.choice([0, 3, 4, 1, 2], n, p=[0.55, 0.25, 0.1, 0.05, 0.05]).astype(np.uint8)
+    return xyz, blk
+
+
+def test_restatement_matches_reference_build_random(oracle, ref_cpu):
+    """Cell-for-cell agreement with the reference's own code on random override worlds."""
+    rng = np.random.default_rng(7)
+    for trial in range(2):
+        W, H, D = 24, 32, 20
+        origin = (3, 0, -5)
+        seed = int(rng.integers(1, 1 << 31))
+        xyz, blk = _random_world(rng, W, H, D, 60, origin)
+        # Keep the reference's run bounded: its CPU path spends one 786-thread
+        # block per sky seed, and every floating block adds dozens of seeds.
+        high = (xyz[:, 1] > 14) & (blk != 0)
+        blk[high] = 0
+        spec = WorldSpec(seed, W, H, D, origin=origin, terrain=TERRAIN_REFERENCE)
+        blocks, bl, sl, hm = oracle.generate(spec, xyz, blk)
+        r = ref_cpu.generate(seed, origin, (W, H, D), xyz, blk, runs=2, max_voxels=W * H * D)
+        assert np.array_equal(blocks, r["blocks"])
+        assert np.array_equal(hm, r["height_map"])
+        assert np.array_equal(bl, r["block_light"])
+        assert np.array_equal(sl, r["sky_light"])
+        vox = oracle.render_voxels(blocks, bl, sl)
+        rv = r["voxels"]
+        assert len(vox) == r["voxel_count"]
+        key = lambda v: v[np.lexsort((v[:, 2], v[:, 1], v[:, 0]))]
+        assert np.array_equal(key(vox), key(rv))
+
+
+def test_per_source_equals_multi_source(oracle):
+    rng = np.random.default_rng(3)
+    for terrain in (TERRAIN_FBM, TERRAIN_FLAT, TERRAIN_REFERENCE):
+        spec = WorldSpec(11, 40, 64, 36, terrain=terrain, base=30, amplitude=20.0)
+        xyz, blk = _random_world(rng, 40, 64, 36, 3000)
+        blocks, hm = oracle.build_blocks(spec, xyz, blk)
+        a = oracle.light(blocks, hm, 0, "per_source")
+        b = oracle.light(blocks, hm, 0, "multi")
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+def test_conversion_matches_reference(oracle, ref_cpu):
+    rng = np.random.default_rng(5)
+    # At least as many 256-thread blocks as host threads: the reference's CPU
+    # launcher re-runs a worker's previous task when a launch has fewer blocks
+    # than workers (src/gpu/cuda/cpu_fallback/CpuKernelLauncher.h:35-49).
+    rgba = rng.integers(0, 256, (4, 90, 160, 4), dtype=np.uint8)
+    a = oracle.convert_rgba8(rgba)
+    b = ref_cpu.convert_rgba8(rgba)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    # multiply by the float reciprocal, not a division: differs from x/255 on some bytes
+    v = np.arange(256, dtype=np.float32)
+    mul = v * np.float32(1.0 / 255.0)
+    assert np.array_equal(oracle.convert_rgba8(np.tile(np.arange(256, dtype=np.uint8)[None, None, :, None],
+                                                       (1, 1, 1, 4)))[0, 0, 0], mul)
+    assert (mul != v / np.float32(255.0)).any()
+
+
+def test_torch_placement_distinct_columns(oracle):
+    spec = WorldSpec(1, 64, 128, 64)
+    t = oracle.place_torches(spec, 200, 12345)
+    assert len(t) == 200
+    cols = {(int(x), int(z)) for x, _, z in t}
+    assert len(cols) == 200
+    for x, y, z in t[:20]:
+        assert y == min(max(oracle.terrain_height(spec, int(x), int(z)), -1), 127) + 1
+    # a permutation of the whole column range
+    perm = sorted(oracle.permute(i, 100, 9) for i in range(100))
+    assert perm == list(range(100))
+
+
+def test_apply_edits_semantics(oracle):
+    """World::setBlock rules: y range, same-block no-op, torch drops with its support."""
+    spec = WorldSpec(1, 8, 32, 8, terrain=TERRAIN_FLAT, base=10)
+    blocks, hm = oracle.build_blocks(spec)
+    assert hm[0, 0] == 10
+    xyz = np.array([[2, 11, 2], [2, 10, 2], [3, 40, 3], [3, 10, 3]], np.int32)
+    kind = np.array([0, 0, 0, 0], np.uint8)
+    blk = np.array([4, 0, 3, 1], np.uint8)  # torch on top; dig its support; out of range; no-op (grass)
+    changed = oracle.apply_edits(blocks, hm, xyz, kind, blk)
+    assert changed == 3  # torch placed, support dug, torch removed
+    assert blocks[2, 11, 2] == 0 and blocks[2, 10, 2] == 0
+    assert hm[2, 2] == 9 and hm[3, 3] == 10
