@@ -10,7 +10,6 @@
 
 namespace blk {
 
-size_t tile_smem_bytes();
 int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream);
 
 namespace {
@@ -144,39 +143,39 @@ __global__ void ovr_count_kernel(const blk_override* ovr, uint32_t n, RegionDims
     }
 }
 
+// Scatters each override into its column segment. The override that takes
+// the segment's first slot is recorded as the segment's owner (owner[i] = 1),
+// so exactly one thread sorts each segment afterwards.
 __global__ void ovr_scatter_kernel(const blk_override* ovr, uint32_t n, RegionDims r, const uint32_t* col_offset,
-    uint32_t* cursor, uint64_t* entries)
+    uint32_t* cursor, uint64_t* entries, uint8_t* owner)
 {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const blk_override o = ovr[i];
         int32_t x, y, z;
-        if (!local_cell(r, o, x, y, z))
+        if (!local_cell(r, o, x, y, z)) {
+            owner[i] = 0;
             continue;
+        }
         const uint64_t col = static_cast<uint64_t>(o.env) * r.W * r.D + static_cast<uint64_t>(z) * r.W + x;
-        const uint32_t pos = col_offset[col] + atomicAdd(cursor + col, 1u);
-        entries[pos] = (static_cast<uint64_t>(y) << 40) | (static_cast<uint64_t>(i) << 8) | o.block;
+        const uint32_t slot = atomicAdd(cursor + col, 1u);
+        entries[col_offset[col] + slot] = (static_cast<uint64_t>(y) << 40) | (static_cast<uint64_t>(i) << 8) | o.block;
+        owner[i] = slot == 0 ? 1 : 0;
     }
 }
 
-// Sorts each column segment by (y, input order); the override with the
-// smallest input index in its column does the (insertion) sort.
+// Sorts each column segment by (y, input order); only the segment's owner
+// touches it.
 __global__ void ovr_sort_kernel(const blk_override* ovr, uint32_t n, RegionDims r, const uint32_t* col_offset,
-    uint64_t* entries)
+    uint64_t* entries, const uint8_t* owner)
 {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        if (!owner[i])
+            continue;
         const blk_override o = ovr[i];
         int32_t x, y, z;
-        if (!local_cell(r, o, x, y, z))
-            continue;
+        local_cell(r, o, x, y, z);
         const uint64_t col = static_cast<uint64_t>(o.env) * r.W * r.D + static_cast<uint64_t>(z) * r.W + x;
         const uint32_t beg = col_offset[col], end = col_offset[col + 1];
-        if (end - beg < 2)
-            continue;
-        uint32_t min_order = 0xFFFFFFFFu;
-        for (uint32_t k = beg; k < end; ++k)
-            min_order = min(min_order, static_cast<uint32_t>((entries[k] >> 8) & 0xFFFFFFFFu));
-        if (min_order != i)
-            continue;
         for (uint32_t k = beg + 1; k < end; ++k) {
             const uint64_t v = entries[k];
             uint32_t m = k;
@@ -643,10 +642,13 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->light, envs * ctx->env_stride, "light"));
     A(dalloc(&ctx->hmap, envs * ctx->columns_per_env, "height map"));
     A(dalloc(&ctx->seeds, envs, "seeds"));
+    A(dalloc(&ctx->terrain_top, envs * ctx->columns_per_env, "terrain heights"));
+    A(dalloc(&ctx->halo_order, static_cast<size_t>(halo_order_size()), "halo order"));
     A(dalloc(&ctx->ovr, ctx->cfg.max_overrides, "override staging"));
     A(dalloc(&ctx->col_count, n_cols, "column counts"));
     A(dalloc(&ctx->col_offset, n_cols, "column offsets"));
     A(dalloc(&ctx->entries, ctx->cfg.max_overrides, "override entries"));
+    A(dalloc(&ctx->ovr_owner, ctx->cfg.max_overrides, "override segment owners"));
     A(dalloc(&ctx->scan_partials, ctx->scan_blocks, "scan partials"));
     A(dalloc(&ctx->edits, ctx->cfg.max_edits, "edit staging"));
     A(dalloc(&ctx->edit_env_count, envs + 1, "edit counts"));
@@ -656,6 +658,15 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
     A(dalloc(&ctx->flags, 1, "flags"));
+    {
+        int sms = 148;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+            cudaGetLastError();
+            sms = 148;
+        }
+        ctx->park_ctas = static_cast<uint32_t>(sms);
+        A(dalloc(&ctx->park, static_cast<size_t>(sms) * 16 * 1024, "tile scratch"));
+    }
     if (rc == BLK_OK) {
         if (cudaMallocHost(reinterpret_cast<void**>(&ctx->h_flags), sizeof(uint32_t)) != cudaSuccess
             || cudaMallocHost(reinterpret_cast<void**>(&ctx->h_dirty_count), sizeof(uint32_t)) != cudaSuccess) {
@@ -663,6 +674,13 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
             set_error("cudaMallocHost failed");
             rc = BLK_ERR_OUT_OF_MEMORY;
         }
+    }
+    if (rc == BLK_OK) {
+        std::vector<uint16_t> order(static_cast<size_t>(halo_order_size()));
+        halo_order_table(order.data());
+        rc = cuda_fail(cudaMemcpy(ctx->halo_order, order.data(), order.size() * sizeof(uint16_t),
+                           cudaMemcpyHostToDevice),
+            "halo order upload");
     }
     if (rc == BLK_OK)
         rc = cuda_fail(cudaMemset(ctx->flags, 0, sizeof(uint32_t)), "cudaMemset flags");
@@ -689,9 +707,9 @@ int blk_ctx_destroy(blk_ctx* ctx)
     for (auto& m : ctx->marks)
         for (cudaEvent_t ev : m.e)
             cudaEventDestroy(ev);
-    void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->ovr, ctx->col_count, ctx->col_offset,
-        ctx->entries, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->flags };
+    void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
+        ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -747,6 +765,7 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
     const uint64_t n_cols = envs * ctx->columns_per_env;
     const RegionDims r = region(ctx);
     const int mark = prof_begin(ctx, 0, st);
+    BLK_CHECK(launch_terrain(ctx, st));
     BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
     if (n_overrides)
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
@@ -754,8 +773,9 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
     if (n_overrides) {
         BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset cursors");
         ovr_scatter_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset,
-            ctx->col_count, ctx->entries);
-        ovr_sort_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset, ctx->entries);
+            ctx->col_count, ctx->entries, ctx->ovr_owner);
+        ovr_sort_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset, ctx->entries,
+            ctx->ovr_owner);
         BLK_CUDA(cudaGetLastError(), "override kernels");
     }
     const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;

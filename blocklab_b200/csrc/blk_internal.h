@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <string>
 #include <vector>
@@ -22,6 +23,8 @@ struct blk_ctx {
     int16_t* hmap = nullptr;          // [env][z][x], world y
 
     uint32_t* seeds = nullptr;        // [env]
+    int16_t* terrain_top = nullptr;   // [env][z][x] local terrain surface, clamped to [-1, H+4]
+    uint16_t* halo_order = nullptr;   // halo columns of a tile by cone distance
     bool generated = false;
 
     // Override column CSR (generation input).
@@ -29,6 +32,7 @@ struct blk_ctx {
     uint32_t* col_count = nullptr;    // [env * columns + 1]
     uint32_t* col_offset = nullptr;   // [env * columns + 1]
     uint64_t* entries = nullptr;      // [max_overrides], key y<<40 | order<<8 | block
+    uint8_t* ovr_owner = nullptr;     // [max_overrides], 1 for the override owning its column segment
     uint32_t* scan_partials = nullptr;
     uint64_t scan_blocks = 0;
 
@@ -42,6 +46,8 @@ struct blk_ctx {
     uint32_t* dirty_count = nullptr;      // [1]
     uint32_t* h_dirty_count = nullptr;    // pinned [1]
 
+    uint32_t* park = nullptr;             // tile-kernel scratch: 16 words x 1024 threads per CTA
+    uint32_t park_ctas = 0;
     uint32_t* flags = nullptr;            // device error flag word
     uint32_t* h_flags = nullptr;          // pinned mirror
 
@@ -67,6 +73,9 @@ int stage_input(const void* src, size_t bytes, void* staging, cudaStream_t strea
 TerrainParams terrain_params(const blk_ctx* ctx);
 
 int launch_relight(blk_ctx* ctx, cudaStream_t stream);
+int launch_terrain(blk_ctx* ctx, cudaStream_t stream);
+void halo_order_table(uint16_t* out);
+int halo_order_size();
 
 // Phase marks for blk_profile: begin() returns a mark index or -1 when off.
 int prof_begin(blk_ctx* ctx, int kind, cudaStream_t stream);

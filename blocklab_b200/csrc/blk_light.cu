@@ -1,5 +1,5 @@
 // Fused world generation + exact sky/block light for one 32x32-column tile
-// per CTA, and the same kernel in relight mode over dirty tiles.
+// per CTA step, and the same kernel in relight mode over dirty tiles.
 //
 // Light model (reference: src/world/WorldGenerator.cu:364-588). The reference
 // runs one breadth-first search per light source over a 29^3 cube and
@@ -13,20 +13,30 @@
 // This kernel computes that fixed point with bit-sliced level sets: with
 // S_k = {v : L(v) >= k}, S_15 = sources and
 //     S_k = S_{k+1} | (open & dilate6(S_{k+1}))        k = 14 .. 1,
-// one bit per cell, 32 consecutive y cells of a column per 32-bit word. The
-// y neighbours are in-register shifts, the x/z neighbours are the adjacent
-// columns' words in shared memory. L(v) is accumulated into four bit planes
-// (bit0 = xor of all S_k, bit1 = xor of even k, bit2 = xor of k % 4 == 0,
-// bit3 = S_8), exact because the sets are nested.
+// one bit per cell, 32 consecutive y cells of a column per 32-bit word. A
+// thread keeps its own columns' level-set words and open masks in registers;
+// the y neighbours are shifts across a column's words, the x/z neighbours are
+// the adjacent columns' words read from a shared plane. The planes ping-pong
+// between two buffers, one barrier per level. L(v) is accumulated into four
+// bit planes (bit0 = xor of all S_k, bit1 = xor of even k, bit2 = xor of
+// k % 4 == 0, bit3 = S_8), exact because the sets are nested.
 //
 // A tile is 32x32 output columns plus a 14-column halo (60x60 columns): light
 // reaches 14 cells, so the halo holds every source and obstacle that can
 // affect the tile. At level step s only columns within L1 distance 14 - s of
 // the tile interior are updated (the "cone"), which is all the interior needs.
-// In y only the band of rows that can hold non-trivial light is processed:
-// torch rows +-14 for block light, dark open rows +-14 for sky light; every
-// other row is 0 block light and trivial sky light (15 above the height map,
-// 0 at or below it).
+// Each thread owns its interior column plus up to two halo columns (the 1976
+// halo columns with cone distance <= 13), handed out in order of cone distance
+// so that whole warps drop out of later steps. In y only the band of rows that
+// can hold non-trivial light is processed (torch rows +-14 for block light,
+// dark open rows +-14 for sky light), in words that start at the band's first
+// row; every other row has block light 0 and trivial sky light (15 above the
+// height map, 0 at or below it).
+//
+// The kernel is persistent (one CTA per SM walking the tiles) so one tile's
+// output stores drain while the next tile computes, and every warp writes its
+// 32 finished columns (contiguous in memory) with coalesced 16-byte stores
+// from a shared staging area.
 #include "blk_internal.h"
 
 namespace blk {
@@ -37,37 +47,48 @@ constexpr int kExt = kTile + 2 * kHalo;             // 60
 constexpr int kExtCols = kExt * kExt;               // 3600
 constexpr int kHaloCols = kExtCols - kTile * kTile; // 2576
 constexpr int kThreads = 1024;
-constexpr int kMaxWords = 4;                        // H <= 128
-constexpr int kSlots = 4;                           // interior + up to 3 halo columns per thread
+constexpr int kWarps = kThreads / 32;
+constexpr int kSlots = 3;                           // interior + up to 2 halo columns per thread
+constexpr int kColIters = (kExtCols + kThreads - 1) / kThreads;
+constexpr uint32_t kCntSat = 31;                    // packed override count saturates here
 
 struct TileArgs {
     uint8_t* ids;
     uint8_t* light;
     int16_t* hmap;
-    const uint32_t* seeds;
+    const int16_t* terrain_top;     // [env][z][x] local terrain surface clamped to [-1, H+4]
+    const uint16_t* halo_order;     // halo ext columns sorted by cone distance
     const uint32_t* col_offset;
     const uint64_t* entries;
     const uint32_t* dirty_list;
     const uint32_t* dirty_window;
     const uint32_t* dirty_count;
     uint32_t* flags;
-    TerrainParams terrain;
-    int32_t W, H, D;
+    uint32_t* park;                 // per-CTA scratch for block planes during a sky flood
+    uint32_t n_tiles;
+    int32_t origin_y;
+    int32_t W, D;
     int32_t tiles_x, tiles_z;
     uint64_t env_stride;
     uint64_t columns;
     int32_t mode; // 0 = generate, 1 = relight dirty tiles from the resident ids
 };
 
+template <int NW>
 struct Smem {
-    uint32_t O[kMaxWords * kExtCols];
-    uint32_t B[kMaxWords * kExtCols];
+    static constexpr int kPlane = NW * kExtCols;                      // words per plane
+    static constexpr int kPitch = 32 * NW + 16;                       // staging bytes per column
+    static constexpr int kStageWords = (kWarps / 2) * kTile * kPitch / 4; // half the warps at a time
+    static constexpr int kPoolWords = 3 * kPlane > kStageWords ? 3 * kPlane : kStageWords;
+    // O | B0 | B1 during the floods; output staging afterwards.
+    uint32_t pool[kPoolWords];
     int16_t top_t[kExtCols];   // terrain surface (local, clamped to [-1, H+4]); unused in relight mode
     int16_t top_f[kExtCols];   // final highest opaque local y, -1 none, -2 outside the world
-    uint32_t beg[kExtCols];
-    uint16_t cnt[kExtCols];
+    uint32_t ovr[kExtCols];    // override list: begin << 5 | min(count, 31)
     int32_t tmin, tmax, dmin, dmax;
-    int32_t any_torch, any_dark;
+
+    __device__ uint32_t* O() { return pool; }
+    __device__ uint32_t* B(int i) { return pool + (1 + i) * kPlane; }
 };
 
 __device__ inline uint32_t spread4(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
@@ -86,6 +107,17 @@ __device__ inline uint32_t above_mask(int32_t ybase, int32_t top)
     return 0xFFFFFFFFu << k;
 }
 
+// Bits j of the word starting at row ybase with ybase + j < H.
+__device__ inline uint32_t inside_mask(int32_t ybase, int32_t H)
+{
+    const int32_t k = H - ybase;
+    if (k >= 32)
+        return 0xFFFFFFFFu;
+    if (k <= 0)
+        return 0u;
+    return (1u << k) - 1u;
+}
+
 // Rows [lo, hi] of the word starting at ybase.
 __device__ inline uint32_t rows_mask(int32_t ybase, int32_t lo, int32_t hi)
 {
@@ -101,519 +133,794 @@ __device__ inline uint32_t bytes_eq(uint32_t x, uint32_t v) { return __vcmpeq4(x
 // Low bit of each byte -> 4 packed bits.
 __device__ inline uint32_t pack4(uint32_t m) { return ((m & 0x01010101u) * 0x10204080u) >> 28; }
 
-__device__ inline void halo_coords(int h, int& ex, int& ez)
+__device__ inline int cone_distance(int c)
 {
-    if (h < kHalo * kExt) {
-        ez = h / kExt;
-        ex = h % kExt;
-    } else if (h < 2 * kHalo * kExt) {
-        const int h2 = h - kHalo * kExt;
-        ez = kHalo + kTile + h2 / kExt;
-        ex = h2 % kExt;
-    } else {
-        const int h3 = h - 2 * kHalo * kExt;
-        const int r = h3 / (2 * kHalo), k = h3 % (2 * kHalo);
-        ez = kHalo + r;
-        ex = k < kHalo ? k : k + kTile;
-    }
-}
-
-__device__ inline int cone_distance(int ex, int ez)
-{
+    const int ex = c % kExt, ez = c / kExt;
     const int dx = max(0, max(kHalo - ex, ex - (kHalo + kTile - 1)));
     const int dz = max(0, max(kHalo - ez, ez - (kHalo + kTile - 1)));
     return dx + dz;
 }
 
-// 14 dilation steps of S over the band words; accumulates the level bit
-// planes of the thread's interior column into cnt[w][p].
-__device__ void flood(Smem& s, int nwb, const int (&slot_col)[kSlots], const int (&slot_dist)[kSlots],
-    uint32_t (&cnt)[kMaxWords][4])
+__device__ inline bool in_world(const TileArgs& a, int gx, int gz) { return gx >= 0 && gz >= 0 && gx < a.W && gz < a.D; }
+
+// Open-cell and torch bits of the 32 rows starting at `ybase` (any row, not
+// necessarily aligned) of a resident id column; rows outside [0, H) are 0.
+template <int H>
+__device__ inline void id_bits(const uint8_t* column, int ybase, uint32_t& open, uint32_t& torch)
 {
-    const int tid = threadIdx.x;
-    // Level 15 = the sources themselves.
+    open = 0u;
+    torch = 0u;
+    const int a0 = ybase & ~15;
+    uint32_t ob[3] = { 0u, 0u, 0u }, tb[3] = { 0u, 0u, 0u };
 #pragma unroll
-    for (int w = 0; w < kMaxWords; ++w) {
-        const uint32_t v = w < nwb ? s.B[w * kExtCols + slot_col[0]] : 0u;
-        cnt[w][0] = v;
+    for (int q = 0; q < 3; ++q) {
+        const int r = a0 + 16 * q;
+        if (r < 0 || r >= H)
+            continue;
+        const uint4 v4 = *reinterpret_cast<const uint4*>(column + r);
+        const uint32_t v[4] = { v4.x, v4.y, v4.z, v4.w };
+        uint32_t o16 = 0u, t16 = 0u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t t = bytes_eq(v[j], Torch);
+            o16 |= pack4(bytes_eq(v[j], Air) | t) << (4 * j);
+            t16 |= pack4(t) << (4 * j);
+        }
+        ob[q] = o16;
+        tb[q] = t16;
+    }
+    // 48 bits starting at row a0; take 32 starting at row ybase.
+    const int sh = ybase - a0; // 0..15
+    const uint64_t o48 = static_cast<uint64_t>(ob[0]) | (static_cast<uint64_t>(ob[1]) << 16) | (static_cast<uint64_t>(ob[2]) << 32);
+    const uint64_t t48 = static_cast<uint64_t>(tb[0]) | (static_cast<uint64_t>(tb[1]) << 16) | (static_cast<uint64_t>(tb[2]) << 32);
+    open = static_cast<uint32_t>(o48 >> sh);
+    torch = static_cast<uint32_t>(t48 >> sh);
+}
+
+// 14 dilation steps of S over NB band words. Plane O holds the open cells and
+// plane B0 the level-15 sources of every ext column. A thread keeps its slot
+// columns' words in registers for the whole flood. Accumulates the level bit
+// planes of the interior column (slot 0) into cnt[w][p]. slot[k] packs the
+// ext column (low 16 bits) and its cone distance (high bits); -1 = unused.
+template <int NW, int NB>
+__device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[NW][4])
+{
+    constexpr int P = Smem<NW>::kPlane;
+    const uint32_t* O = s.O();
+    uint32_t own[kSlots][NB];
+#pragma unroll
+    for (int k = 0; k < kSlots; ++k)
+#pragma unroll
+        for (int w = 0; w < NB; ++w)
+            own[k][w] = slot[k] >= 0 ? s.B(0)[w * kExtCols + (slot[k] & 0xFFFF)] : 0u;
+    // The interior column is updated at every step: its open mask stays in registers.
+    uint32_t open0[NB];
+#pragma unroll
+    for (int w = 0; w < NB; ++w)
+        open0[w] = O[w * kExtCols + (slot[0] & 0xFFFF)];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        cnt[w][0] = w < NB ? own[0][w < NB ? w : 0] : 0u;
         cnt[w][1] = 0;
         cnt[w][2] = 0;
         cnt[w][3] = 0;
     }
-    (void)tid;
     for (int step = 1; step <= kMaxDistance; ++step) {
+        const uint32_t* cur = s.pool + (1 + ((step - 1) & 1)) * P;
+        uint32_t* nxt = s.pool + (1 + (step & 1)) * P;
+        const int reach = kMaxDistance - step;
         const int level = 15 - step;
-        uint32_t nxt[kSlots][kMaxWords];
 #pragma unroll
         for (int k = 0; k < kSlots; ++k) {
-            const int c = slot_col[k];
-            const bool active = c >= 0 && slot_dist[k] <= kMaxDistance - step;
+            const bool act = k == 0 || (slot[k] >= 0 && (slot[k] >> 16) <= reach);
+            if (k > 0 && !__any_sync(0xFFFFFFFFu, act))
+                continue; // the whole warp skips this slot
+            if (!act)
+                continue;
+            const int c = slot[k] & 0xFFFF;
+            uint32_t v[NB];
 #pragma unroll
-            for (int w = 0; w < kMaxWords; ++w) {
-                nxt[k][w] = 0u;
-                if (active && w < nwb) {
-                    const uint32_t* Bw = s.B + w * kExtCols;
-                    const uint32_t cur = Bw[c];
-                    const uint32_t below = w > 0 ? s.B[(w - 1) * kExtCols + c] : 0u;
-                    const uint32_t above = w + 1 < nwb ? s.B[(w + 1) * kExtCols + c] : 0u;
-                    const uint32_t up = __funnelshift_l(below, cur, 1);   // cell y takes y-1
-                    const uint32_t dn = __funnelshift_r(cur, above, 1);   // cell y takes y+1
-                    const uint32_t n = up | dn | Bw[c - 1] | Bw[c + 1] | Bw[c - kExt] | Bw[c + kExt];
-                    nxt[k][w] = cur | (s.O[w * kExtCols + c] & n);
+            for (int w = 0; w < NB; ++w) {
+                const uint32_t* Bw = cur + w * kExtCols + c;
+                const uint32_t below = w > 0 ? own[k][w > 0 ? w - 1 : 0] : 0u;
+                const uint32_t above = w + 1 < NB ? own[k][w + 1 < NB ? w + 1 : w] : 0u;
+                const uint32_t up = __funnelshift_l(below, own[k][w], 1); // cell y takes y-1
+                const uint32_t dn = __funnelshift_r(own[k][w], above, 1); // cell y takes y+1
+                const uint32_t n = up | dn | Bw[-1] | Bw[1] | Bw[-kExt] | Bw[kExt];
+                v[w] = own[k][w] | ((k == 0 ? open0[w] : O[w * kExtCols + c]) & n);
+            }
+#pragma unroll
+            for (int w = 0; w < NB; ++w) {
+                own[k][w] = v[w];
+                nxt[w * kExtCols + c] = v[w];
+            }
+            if (k == 0) {
+#pragma unroll
+                for (int w = 0; w < NB; ++w) {
+                    cnt[w][0] ^= v[w];
+                    if ((level & 1) == 0)
+                        cnt[w][1] ^= v[w];
+                    if ((level & 3) == 0)
+                        cnt[w][2] ^= v[w];
+                    if (level == 8)
+                        cnt[w][3] = v[w];
                 }
             }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int k = 0; k < kSlots; ++k) {
-            const int c = slot_col[k];
-            const bool active = c >= 0 && slot_dist[k] <= kMaxDistance - step;
-#pragma unroll
-            for (int w = 0; w < kMaxWords; ++w)
-                if (active && w < nwb)
-                    s.B[w * kExtCols + c] = nxt[k][w];
-        }
-#pragma unroll
-        for (int w = 0; w < kMaxWords; ++w) {
-            const uint32_t v = nxt[0][w];
-            cnt[w][0] ^= v;
-            if ((level & 1) == 0)
-                cnt[w][1] ^= v;
-            if ((level & 3) == 0)
-                cnt[w][2] ^= v;
-            if (level == 8)
-                cnt[w][3] = v;
         }
         __syncthreads();
     }
 }
 
-__device__ inline bool in_world(const TileArgs& a, int gx, int gz) { return gx >= 0 && gz >= 0 && gx < a.W && gz < a.D; }
-
-__global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
+template <int NW>
+__device__ void flood_any(int nb, Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[NW][4])
 {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    Smem& s = *reinterpret_cast<Smem*>(smem_raw);
-    const int tid = threadIdx.x;
-
-    // ---- which tile ----------------------------------------------------
-    uint32_t tile_id;
-    int32_t wlo_rows = 0, whi_rows = a.H - 1; // output rows
-    if (a.mode == 0) {
-        tile_id = blockIdx.x;
-    } else {
-        if (blockIdx.x >= *a.dirty_count)
-            return;
-        tile_id = a.dirty_list[blockIdx.x];
-        const uint32_t win = a.dirty_window[tile_id];
-        wlo_rows = static_cast<int32_t>(win & 0xFFFFu) & ~15;
-        whi_rows = min(static_cast<int32_t>(win >> 16) | 15, a.H - 1);
+    switch (nb) {
+    case 1:
+        flood<NW, 1>(s, slot, cnt);
+        break;
+    case 2:
+        if constexpr (NW >= 2)
+            flood<NW, 2 <= NW ? 2 : NW>(s, slot, cnt);
+        break;
+    case 3:
+        if constexpr (NW >= 3)
+            flood<NW, 3 <= NW ? 3 : NW>(s, slot, cnt);
+        break;
+    default:
+        if constexpr (NW >= 4)
+            flood<NW, NW>(s, slot, cnt);
+        break;
     }
+}
+
+// Re-indexes counter planes from band words (word w holds rows lo + 32w ..)
+// to absolute words (word w holds rows 32w ..); rows outside the band are 0.
+template <int NW>
+__device__ inline void realign(uint32_t (&cnt)[NW][4], int lo, int nb)
+{
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        uint32_t out[NW];
+#pragma unroll
+        for (int aw = 0; aw < NW; ++aw) {
+            const int b = 32 * aw - lo; // band offset of the absolute word's first row
+            uint32_t v = 0u;
+            if (b > -32 && b < 32 * nb) {
+                if (b < 0) {
+                    v = cnt[0][p] << (-b);
+                } else {
+                    const int w0 = b >> 5, sh = b & 31;
+                    uint32_t lo_w = 0u, hi_w = 0u;
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) {
+                        if (w == w0)
+                            lo_w = cnt[w][p];
+                        if (w == w0 + 1 && w < nb)
+                            hi_w = cnt[w][p];
+                    }
+                    v = __funnelshift_r(lo_w, hi_w, sh);
+                }
+            }
+            out[aw] = v;
+        }
+#pragma unroll
+        for (int aw = 0; aw < NW; ++aw)
+            cnt[aw][p] = out[aw];
+    }
+}
+
+template <int NW>
+__device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, int32_t wlo_rows, int32_t whi_rows)
+{
+    constexpr int H = 32 * NW;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const uint32_t tiles_per_env = static_cast<uint32_t>(a.tiles_x * a.tiles_z);
     const uint32_t env = tile_id / tiles_per_env;
     const uint32_t t_in_env = tile_id % tiles_per_env;
     const int x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
     const int z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
-    const uint32_t seed = a.seeds[env];
     const uint64_t env_col0 = static_cast<uint64_t>(env) * a.columns;
     uint8_t* env_ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
-    uint8_t* env_light = a.light + static_cast<uint64_t>(env) * a.env_stride;
-    const int H = a.H;
 
     if (tid == 0) {
         s.tmin = 1 << 20;
         s.tmax = -(1 << 20);
         s.dmin = 1 << 20;
         s.dmax = -(1 << 20);
-        s.any_torch = 0;
-        s.any_dark = 0;
     }
-    __syncthreads();
 
     // ---- phase A: per-column summary -----------------------------------
-    for (int c = tid; c < kExtCols; c += kThreads) {
+    // All global loads of the thread's columns are issued before any is used.
+    int32_t pa_top[kColIters];
+    uint32_t pa_beg[kColIters], pa_end[kColIters];
+#pragma unroll
+    for (int it = 0; it < kColIters; ++it) {
+        const int c = tid + it * kThreads;
+        pa_top[it] = -1;
+        pa_beg[it] = 0;
+        pa_end[it] = 0;
+        if (c < kExtCols) {
+            const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
+            if (in_world(a, gx, gz)) {
+                const uint64_t col = env_col0 + static_cast<uint64_t>(gz) * a.W + gx;
+                if (a.mode == 0) {
+                    pa_top[it] = __ldg(a.terrain_top + col);
+                    pa_beg[it] = __ldg(a.col_offset + col);
+                    pa_end[it] = __ldg(a.col_offset + col + 1);
+                } else {
+                    pa_top[it] = __ldg(a.hmap + col);
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < kColIters; ++it) {
+        const int c = tid + it * kThreads;
+        if (c >= kExtCols)
+            break;
         const int ex = c % kExt, ez = c / kExt;
         const int gx = x0 - kHalo + ex, gz = z0 - kHalo + ez;
         const bool interior = ex >= kHalo && ex < kHalo + kTile && ez >= kHalo && ez < kHalo + kTile;
         if (!in_world(a, gx, gz)) {
             s.top_t[c] = -1;
             s.top_f[c] = -2;
-            s.beg[c] = 0;
-            s.cnt[c] = 0;
+            s.ovr[c] = 0;
             continue;
         }
-        const uint64_t col = env_col0 + static_cast<uint64_t>(gz) * a.W + gx;
         if (a.mode == 0) {
-            int32_t top = terrain_top_local(a.terrain, seed, a.terrain.origin_x + gx, a.terrain.origin_z + gz);
-            top = top < -1 ? -1 : (top > H + 4 ? H + 4 : top);
+            const int32_t top = pa_top[it];
             const int32_t tc = min(top, H - 1);
-            const uint32_t beg = a.col_offset[col], end = a.col_offset[col + 1];
-            uint32_t n = end - beg;
-            if (n > 0xFFFFu) {
-                atomicOr(a.flags, kFlagOverrideList);
-                n = 0xFFFFu;
-            }
-            int32_t hi_opaque = -1;
-            int32_t dlo = 1 << 20, dhi = -(1 << 20);
-            // Winners: the last entry of each y run (entries sorted by y, then input order).
-            for (uint32_t i = 0; i < n; ++i) {
-                const uint64_t e = a.entries[beg + i];
-                const int32_t y = static_cast<int32_t>(entry_y(e));
-                if (i + 1 < n && static_cast<int32_t>(entry_y(a.entries[beg + i + 1])) == y)
-                    continue;
-                const uint8_t b = entry_block(e);
-                if (is_opaque(b))
-                    hi_opaque = max(hi_opaque, y);
-                if (b == Torch) {
-                    atomicMin(&s.tmin, y);
-                    atomicMax(&s.tmax, y);
-                }
-            }
-            // Terrain part of the height map: walk down through cells whose
-            // winning override is non-opaque.
-            int32_t yt = tc;
-            int32_t i = static_cast<int32_t>(n) - 1;
-            while (yt >= 0) {
-                while (i >= 0 && static_cast<int32_t>(entry_y(a.entries[beg + i])) > yt)
-                    --i;
-                if (i >= 0 && static_cast<int32_t>(entry_y(a.entries[beg + i])) == yt
-                    && !is_opaque(entry_block(a.entries[beg + i]))) {
-                    --yt;
-                    continue;
-                }
-                break;
-            }
-            const int32_t topf = max(hi_opaque, yt);
-            if (interior) {
-                // Open cells below the final top: non-opaque overrides there, and
-                // terrain air between the terrain surface and a higher opaque override.
-                for (uint32_t k = 0; k < n; ++k) {
-                    const uint64_t e = a.entries[beg + k];
-                    const int32_t y = static_cast<int32_t>(entry_y(e));
-                    if (k + 1 < n && static_cast<int32_t>(entry_y(a.entries[beg + k + 1])) == y)
+            const uint32_t beg = pa_beg[it];
+            const uint32_t n = pa_end[it] - beg;
+            int32_t topf = tc;
+            if (n > 0) {
+                const uint64_t* e = a.entries + beg;
+                int32_t hi_opaque = -1;
+                int32_t dlo = 1 << 20, dhi = -(1 << 20);
+                // Winners: the last entry of each y run (entries sorted by y, then input order).
+                for (uint32_t i = 0; i < n; ++i) {
+                    const uint64_t v = __ldg(e + i);
+                    const int32_t y = static_cast<int32_t>(entry_y(v));
+                    if (i + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + i + 1))) == y)
                         continue;
-                    if (!is_opaque(entry_block(e)) && y < topf) {
-                        dlo = min(dlo, y);
-                        dhi = max(dhi, y);
+                    const uint8_t b = entry_block(v);
+                    if (is_opaque(b))
+                        hi_opaque = max(hi_opaque, y);
+                    if (b == Torch) {
+                        atomicMin(&s.tmin, y);
+                        atomicMax(&s.tmax, y);
                     }
                 }
-                if (tc + 1 < topf) {
-                    dlo = min(dlo, tc + 1);
-                    dhi = max(dhi, topf - 1);
+                // Terrain part of the height map: walk down through cells whose
+                // winning override is non-opaque.
+                int32_t yt = tc;
+                int32_t i = static_cast<int32_t>(n) - 1;
+                while (yt >= 0) {
+                    while (i >= 0 && static_cast<int32_t>(entry_y(__ldg(e + i))) > yt)
+                        --i;
+                    if (i >= 0 && static_cast<int32_t>(entry_y(__ldg(e + i))) == yt
+                        && !is_opaque(entry_block(__ldg(e + i)))) {
+                        --yt;
+                        continue;
+                    }
+                    break;
                 }
-                if (dlo <= dhi) {
-                    atomicMin(&s.dmin, dlo);
-                    atomicMax(&s.dmax, dhi);
+                topf = max(hi_opaque, yt);
+                if (interior) {
+                    // Open cells below the final top: non-opaque overrides there, and
+                    // terrain air between the terrain surface and a higher opaque override.
+                    for (uint32_t k = 0; k < n; ++k) {
+                        const uint64_t v = __ldg(e + k);
+                        const int32_t y = static_cast<int32_t>(entry_y(v));
+                        if (k + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + k + 1))) == y)
+                            continue;
+                        if (!is_opaque(entry_block(v)) && y < topf) {
+                            dlo = min(dlo, y);
+                            dhi = max(dhi, y);
+                        }
+                    }
+                    if (tc + 1 < topf) {
+                        dlo = min(dlo, tc + 1);
+                        dhi = max(dhi, topf - 1);
+                    }
+                    if (dlo <= dhi) {
+                        atomicMin(&s.dmin, dlo);
+                        atomicMax(&s.dmax, dhi);
+                    }
                 }
             }
             s.top_t[c] = static_cast<int16_t>(top);
             s.top_f[c] = static_cast<int16_t>(topf);
-            s.beg[c] = beg;
-            s.cnt[c] = static_cast<uint16_t>(n);
+            s.ovr[c] = (beg << 5) | (n < kCntSat ? n : kCntSat);
         } else {
-            const int32_t topf = clamp_top(static_cast<int32_t>(a.hmap[col]) - a.terrain.origin_y, H);
             s.top_t[c] = -1;
-            s.top_f[c] = static_cast<int16_t>(topf);
-            s.beg[c] = 0;
-            s.cnt[c] = 0;
+            s.top_f[c] = static_cast<int16_t>(clamp_top(pa_top[it] - a.origin_y, H));
+            s.ovr[c] = 0;
         }
     }
     __syncthreads();
 
     // ---- slot ownership for the flood ------------------------------------
-    int slot_col[kSlots], slot_dist[kSlots];
-    slot_col[0] = (kHalo + tid / kTile) * kExt + kHalo + tid % kTile;
-    slot_dist[0] = 0;
+    // Slot 0: the thread's interior column. Slots 1..2: halo columns in order
+    // of cone distance; slot 2 runs the warps in reverse so every warp gets a
+    // similar amount of work at each step.
+    int slot[kSlots];
+    slot[0] = (kHalo + tid / kTile) * kExt + kHalo + tid % kTile;
 #pragma unroll
     for (int k = 1; k < kSlots; ++k) {
-        const int h = tid + (k - 1) * kThreads;
-        if (h < kHaloCols) {
-            int ex, ez;
-            halo_coords(h, ex, ez);
-            slot_col[k] = ez * kExt + ex;
-            slot_dist[k] = cone_distance(ex, ez);
-        } else {
-            slot_col[k] = -1;
-            slot_dist[k] = 1 << 20;
+        const int wk = (k == 2) ? (kWarps - 1 - warp) : warp;
+        const int r = (k - 1) * kThreads + wk * 32 + lane;
+        slot[k] = -1;
+        if (r < kHaloCols) {
+            const int c = __ldg(a.halo_order + r);
+            const int d = cone_distance(c);
+            if (d < kMaxDistance)
+                slot[k] = c | (d << 16);
         }
     }
 
-    uint32_t cb[kMaxWords][4], cs[kMaxWords][4];
-    int b_wlo = 0, b_nwb = 0, s_wlo = 0, s_nwb = 0;
-
-    // ---- band planes -----------------------------------------------------
-    // Builds s.O (open cells) and s.B (level-15 sources) over `nwb` words
-    // starting at word `wlo`. source: 0 = torches, 1 = lit cells.
-    auto build = [&](int wlo, int nwb, int source) {
-        for (int idx = tid; idx < nwb * kExtCols; idx += kThreads) {
-            const int w = idx / kExtCols, c = idx - w * kExtCols;
-            const int ybase = (wlo + w) * 32;
-            const int32_t topf = s.top_f[c];
-            uint32_t o = 0u, src = 0u;
-            if (topf >= -1) {
-                if (a.mode == 0) {
-                    o = above_mask(ybase, min(static_cast<int32_t>(s.top_t[c]), H - 1));
-                    const uint32_t beg = s.beg[c], n = s.cnt[c];
-                    for (uint32_t i = 0; i < n; ++i) {
-                        const uint64_t e = a.entries[beg + i];
-                        const int32_t y = static_cast<int32_t>(entry_y(e));
-                        if (y < ybase || y >= ybase + 32)
-                            continue;
-                        if (i + 1 < n && static_cast<int32_t>(entry_y(a.entries[beg + i + 1])) == y)
-                            continue;
-                        const uint8_t b = entry_block(e);
-                        const uint32_t bit = 1u << (y - ybase);
-                        o = is_opaque(b) ? (o & ~bit) : (o | bit);
-                        if (source == 0 && b == Torch)
-                            src |= bit;
-                    }
-                } else {
-                    const int ex = c % kExt, ez = c / kExt;
-                    const int gx = x0 - kHalo + ex, gz = z0 - kHalo + ez;
-                    const uint4* p = reinterpret_cast<const uint4*>(
-                        env_ids + (static_cast<uint64_t>(gz) * a.W + gx) * H + ybase);
-                    const uint4 q0 = p[0], q1 = p[1];
-                    const uint32_t v[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t t = bytes_eq(v[j], Torch);
-                        const uint32_t op = bytes_eq(v[j], Air) | t;
-                        o |= pack4(op) << (4 * j);
-                        if (source == 0)
-                            src |= pack4(t) << (4 * j);
-                    }
-                }
-                if (source == 1)
-                    src = above_mask(ybase, topf);
-            }
-            s.O[w * kExtCols + c] = o;
-            s.B[w * kExtCols + c] = src & (source == 1 ? 0xFFFFFFFFu : o);
+    // Override list of ext column c: pointer and count.
+    auto overrides_of = [&](int c, const uint64_t*& e, uint32_t& n) {
+        const uint32_t packed = s.ovr[c];
+        n = packed & kCntSat;
+        uint32_t beg = packed >> 5;
+        if (n == kCntSat) {
+            // Long list: reread its bounds.
+            const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
+            const uint64_t col = env_col0 + static_cast<uint64_t>(gz) * a.W + gx;
+            beg = __ldg(a.col_offset + col);
+            n = __ldg(a.col_offset + col + 1) - beg;
         }
+        e = a.entries + beg;
     };
 
-    auto band_words = [&](int32_t rlo, int32_t rhi, int& wlo, int& nwb) {
+    // Open-cell and source bits of ext column c for the 32 rows from ybase.
+    // source: 0 = torches, 1 = lit cells (above the final top).
+    auto column_bits = [&](int c, int ybase, int source, uint32_t& open, uint32_t& src) {
+        const int32_t topf = s.top_f[c];
+        open = 0u;
+        src = 0u;
+        if (topf < -1)
+            return; // outside the world
+        const uint32_t inside = inside_mask(ybase, H); // bands start at row >= 0
+        if (a.mode == 0) {
+            open = above_mask(ybase, min(static_cast<int32_t>(s.top_t[c]), H - 1));
+            const uint64_t* e;
+            uint32_t n;
+            overrides_of(c, e, n);
+            for (uint32_t i = 0; i < n; ++i) {
+                const uint64_t v = __ldg(e + i);
+                const int32_t y = static_cast<int32_t>(entry_y(v));
+                if (y < ybase || y >= ybase + 32)
+                    continue;
+                if (i + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + i + 1))) == y)
+                    continue;
+                const uint8_t b = entry_block(v);
+                const uint32_t bit = 1u << (y - ybase);
+                open = is_opaque(b) ? (open & ~bit) : (open | bit);
+                if (source == 0 && b == Torch)
+                    src |= bit;
+            }
+        } else {
+            const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
+            uint32_t t;
+            id_bits<H>(env_ids + (static_cast<uint64_t>(gz) * a.W + gx) * H, ybase, open, t);
+            if (source == 0)
+                src = t;
+        }
+        if (source == 1)
+            src = above_mask(ybase, topf);
+        open &= inside;
+        src &= inside & open;
+    };
+
+    // Builds planes O (open cells) and B0 (level-15 sources) of every ext
+    // column over nb words from row blo.
+    auto build = [&](int blo, int nb, int source) {
+        uint32_t* O = s.O();
+        uint32_t* B0 = s.B(0);
+        for (int w = 0; w < nb; ++w)
+            for (int c = tid; c < kExtCols; c += kThreads) {
+                uint32_t o, src;
+                column_bits(c, blo + 32 * w, source, o, src);
+                O[w * kExtCols + c] = o;
+                B0[w * kExtCols + c] = src;
+            }
+    };
+
+    // Band of rows [rlo, rhi] clipped to the region: first row and word count.
+    auto band = [&](int32_t rlo, int32_t rhi, int& blo, int& nb) {
         rlo = max(rlo, 0);
         rhi = min(rhi, H - 1);
         if (rlo > rhi) {
-            nwb = 0;
+            nb = 0;
             return;
         }
-        wlo = rlo >> 5;
-        nwb = (rhi >> 5) - wlo + 1;
+        blo = rlo;
+        nb = (rhi - rlo) / 32 + 1;
     };
+
+    uint32_t cb[NW][4], cs[NW][4];
+    int b_lo = 0, b_nb = 0, s_lo = 0, s_nb = 0;
 
     // ---- block light -------------------------------------------------------
     if (a.mode == 0) {
         if (s.tmin <= s.tmax)
-            band_words(s.tmin - kMaxDistance, s.tmax + kMaxDistance, b_wlo, b_nwb);
+            band(s.tmin - kMaxDistance, s.tmax + kMaxDistance, b_lo, b_nb);
     } else {
-        band_words(wlo_rows - kMaxDistance, whi_rows + kMaxDistance, b_wlo, b_nwb);
+        band(wlo_rows - kMaxDistance, whi_rows + kMaxDistance, b_lo, b_nb);
     }
-    if (b_nwb > kMaxWords) {
-        if (tid == 0)
-            atomicOr(a.flags, kFlagBandTooWide);
-        b_nwb = kMaxWords;
-    }
-    if (b_nwb > 0) {
-        build(b_wlo, b_nwb, 0);
+    if (b_nb > 0) {
+        build(b_lo, b_nb, 0);
         __syncthreads();
         if (a.mode == 1) {
-            // Any torch in the band? (mode 0 knows from the override lists.)
+            // Any torch in the band? (generation knows from the override lists.)
             bool any = false;
-            for (int idx = tid; idx < b_nwb * kExtCols; idx += kThreads)
-                any |= s.B[idx] != 0u;
+            for (int idx = tid; idx < b_nb * kExtCols; idx += kThreads)
+                any |= s.B(0)[idx] != 0u;
             if (__syncthreads_or(any) == 0)
-                b_nwb = 0;
+                b_nb = 0;
         }
     }
-    if (b_nwb > 0)
-        flood(s, b_nwb, slot_col, slot_dist, cb);
+    if (b_nb > 0) {
+        flood_any<NW>(b_nb, s, slot, cb);
+        realign<NW>(cb, b_lo, b_nb);
+    }
 
     // ---- sky light -----------------------------------------------------------
     if (a.mode == 0) {
         if (s.dmin <= s.dmax)
-            band_words(s.dmin - kMaxDistance, s.dmax + kMaxDistance, s_wlo, s_nwb);
-        if (s_nwb > kMaxWords) {
-            if (tid == 0)
-                atomicOr(a.flags, kFlagBandTooWide);
-            s_nwb = kMaxWords;
-        }
-        if (s_nwb > 0) {
+            band(s.dmin - kMaxDistance, s.dmax + kMaxDistance, s_lo, s_nb);
+        if (s_nb > 0) {
             __syncthreads();
-            build(s_wlo, s_nwb, 1);
+            build(s_lo, s_nb, 1);
             __syncthreads();
         }
     } else {
-        // Same band as block light; the open plane is still valid, only the
-        // sources change. Sky BFS is needed if an interior column has an open
-        // cell at or below its top inside the output rows.
-        s_wlo = b_wlo;
-        band_words(wlo_rows - kMaxDistance, whi_rows + kMaxDistance, s_wlo, s_nwb);
-        if (s_nwb > kMaxWords)
-            s_nwb = kMaxWords;
-        if (b_nwb == 0 && s_nwb > 0) {
-            // The block pass skipped its flood but built O already.
-        }
+        // Same rows as block light. The sky flood is needed if an interior
+        // column has an open cell at or below its top inside the output rows.
+        band(wlo_rows - kMaxDistance, whi_rows + kMaxDistance, s_lo, s_nb);
+        __syncthreads();
+        if (s_nb > 0)
+            build(s_lo, s_nb, 1);
+        __syncthreads();
         bool dark = false;
-        {
-            const int c = slot_col[0];
-            const int32_t topf = s.top_f[c];
-            if (topf >= 0) {
+        const int c = slot[0];
+        const int32_t topf0 = s.top_f[c];
+        if (topf0 >= 0) {
 #pragma unroll
-                for (int w = 0; w < kMaxWords; ++w)
-                    if (w < s_nwb) {
-                        const int ybase = (s_wlo + w) * 32;
-                        const uint32_t below_top = ~above_mask(ybase, topf);
-                        dark |= (s.O[w * kExtCols + c] & below_top & rows_mask(ybase, wlo_rows, whi_rows)) != 0u;
+            for (int w = 0; w < NW; ++w)
+                if (w < s_nb) {
+                    const int ybase = s_lo + 32 * w;
+                    dark |= (s.O()[w * kExtCols + c] & ~above_mask(ybase, topf0) & rows_mask(ybase, wlo_rows, whi_rows))
+                        != 0u;
+                }
+        }
+        if (__syncthreads_or(dark) == 0)
+            s_nb = 0;
+    }
+    uint32_t* park = a.park + static_cast<uint64_t>(blockIdx.x) * (NW * 4 * kThreads);
+    if (s_nb > 0) {
+        // The block planes wait in this CTA's global scratch slice while the
+        // sky flood uses the registers (rare: needs dark open cells); the
+        // output reads them back from there.
+#pragma unroll
+        for (int w = 0; w < NW; ++w)
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+                park[(w * 4 + p) * kThreads + tid] = b_nb > 0 ? cb[w][p] : 0u;
+        flood_any<NW>(s_nb, s, slot, cs);
+        realign<NW>(cs, s_lo, s_nb);
+    }
+
+    // ---- outputs for the interior columns -------------------------------------
+    // Each warp owns one z row of 32 columns, contiguous in memory. A lane
+    // builds its column's bytes in the warp's staging area (the flood planes
+    // are free now), then the warp stores the row with coalesced 16-byte
+    // stores. Half of the warps stage at a time.
+    constexpr int kPitch = Smem<NW>::kPitch;
+    constexpr int kChunks = H / 16;
+    const int c0 = slot[0];
+    const int32_t topf = s.top_f[c0];
+    const int32_t top = s.top_t[c0];
+    const uint64_t* obeg;
+    uint32_t ocnt;
+    if (a.mode == 0)
+        overrides_of(c0, obeg, ocnt);
+    const int gx = x0 + lane, gz = z0 + warp;
+    const bool valid = in_world(a, gx, gz);
+    const bool row_ok = gz < a.D;
+    const int ncols = min(kTile, a.W - x0);
+    uint8_t* stage = reinterpret_cast<uint8_t*>(s.pool) + (warp & (kWarps / 2 - 1)) * (kTile * kPitch);
+    uint8_t* my = stage + lane * kPitch;
+    const uint64_t row_off = (static_cast<uint64_t>(gz) * a.W + x0) * H;
+
+    auto copy_out = [&](uint8_t* dst, int rlo, int rhi) {
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int idx = i * 32 + lane;
+            const int col = idx / kChunks, ch = idx - col * kChunks;
+            const int r0 = ch * 16;
+            if (col < ncols && r0 >= rlo && r0 <= rhi)
+                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(col) * H + r0)
+                    = *reinterpret_cast<const uint4*>(stage + col * kPitch + r0);
+        }
+    };
+
+    for (int round = 0; round < 2; ++round) {
+        __syncthreads();
+        if ((warp >> 4) != round)
+            continue;
+        if (a.mode == 0) {
+            if (valid) {
+                a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(topf + a.origin_y);
+                // Layer rule branch-free: id = [y <= top] + [y <= top-1] + [y <= top-4].
+                const uint32_t t0 = static_cast<uint32_t>(min(max(top, -1), 127) & 0xFF) * 0x01010101u;
+                const uint32_t t1 = static_cast<uint32_t>(min(max(top - 1, -1), 127) & 0xFF) * 0x01010101u;
+                const uint32_t t4 = static_cast<uint32_t>(min(max(top - 4, -1), 127) & 0xFF) * 0x01010101u;
+#pragma unroll
+                for (int ch = 0; ch < kChunks; ++ch) {
+                    const int r0 = ch * 16;
+                    uint32_t wv[4];
+                    if (r0 > top) {
+                        wv[0] = wv[1] = wv[2] = wv[3] = 0u;
+                    } else if (r0 + 15 <= top - 4) {
+                        wv[0] = wv[1] = wv[2] = wv[3] = 0x03030303u;
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint32_t y4 = static_cast<uint32_t>(r0 + 4 * q) * 0x01010101u + 0x03020100u;
+                            wv[q] = (__vcmples4(y4, t0) & 0x01010101u) + (__vcmples4(y4, t1) & 0x01010101u)
+                                + (__vcmples4(y4, t4) & 0x01010101u);
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                }
+                // Winning overrides (latest of each y) replace the terrain bytes.
+                for (uint32_t i = 0; i < ocnt; ++i) {
+                    const uint64_t v = __ldg(obeg + i);
+                    const int32_t y = static_cast<int32_t>(entry_y(v));
+                    if (i + 1 < ocnt && static_cast<int32_t>(entry_y(__ldg(obeg + i + 1))) == y)
+                        continue;
+                    my[y] = entry_block(v);
+                }
+            }
+            __syncwarp();
+            if (row_ok)
+                copy_out(env_ids + row_off, 0, H - 1);
+            __syncwarp();
+        }
+
+        if (valid) {
+            // One 16-row chunk of light bytes: block bits bn, sky bits sn for
+            // the chunk rows in sky_rows, trivial sky light elsewhere.
+            auto emit = [&](int r0, uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3, uint32_t s0, uint32_t s1,
+                            uint32_t s2, uint32_t s3, uint32_t sky_rows) {
+                const bool block_any = (b0 | b1 | b2 | b3) != 0u;
+                uint32_t wv[4];
+                if (!block_any && sky_rows == 0u && (r0 > topf || r0 + 15 <= topf)) {
+                    const uint32_t v = r0 > topf ? 0xF0F0F0F0u : 0u;
+                    wv[0] = wv[1] = wv[2] = wv[3] = v;
+                } else {
+                    const uint32_t lit = above_mask(r0, topf) & ~sky_rows;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int j = 4 * q;
+                        uint32_t v = spread4((b0 >> j) & 0xFu) | (spread4((b1 >> j) & 0xFu) << 1)
+                            | (spread4((b2 >> j) & 0xFu) << 2) | (spread4((b3 >> j) & 0xFu) << 3);
+                        if (sky_rows != 0u)
+                            v |= (spread4((s0 >> j) & 0xFu) << 4) | (spread4((s1 >> j) & 0xFu) << 5)
+                                | (spread4((s2 >> j) & 0xFu) << 6) | (spread4((s3 >> j) & 0xFu) << 7);
+                        v |= spread4((lit >> j) & 0xFu) * 0xF0u;
+                        wv[q] = v;
+                    }
+                }
+                *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            };
+            if (s_nb == 0) {
+                // Block planes in registers, sky light trivial.
+#pragma unroll
+                for (int w = 0; w < NW; ++w)
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int r0 = 32 * w + 16 * half;
+                        if (r0 < wlo_rows || r0 > whi_rows)
+                            continue;
+                        const int sh = 16 * half;
+                        if (b_nb > 0)
+                            emit(r0, (cb[w][0] >> sh) & 0xFFFFu, (cb[w][1] >> sh) & 0xFFFFu, (cb[w][2] >> sh) & 0xFFFFu,
+                                (cb[w][3] >> sh) & 0xFFFFu, 0u, 0u, 0u, 0u, 0u);
+                        else
+                            emit(r0, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u);
+                    }
+            } else {
+                // Block planes from the parked slice, sky planes in registers.
+#pragma unroll
+                for (int w = 0; w < NW; ++w)
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int r0 = 32 * w + 16 * half;
+                        if (r0 < wlo_rows || r0 > whi_rows)
+                            continue;
+                        const int sh = 16 * half;
+                        const uint32_t* pk = park + w * 4 * kThreads + tid;
+                        emit(r0, (pk[0] >> sh) & 0xFFFFu, (pk[kThreads] >> sh) & 0xFFFFu,
+                            (pk[2 * kThreads] >> sh) & 0xFFFFu, (pk[3 * kThreads] >> sh) & 0xFFFFu,
+                            (cs[w][0] >> sh) & 0xFFFFu, (cs[w][1] >> sh) & 0xFFFFu, (cs[w][2] >> sh) & 0xFFFFu,
+                            (cs[w][3] >> sh) & 0xFFFFu, rows_mask(r0, s_lo, s_lo + 32 * s_nb - 1) & 0xFFFFu);
                     }
             }
         }
-        __syncthreads();
-        if (__syncthreads_or(dark) == 0)
-            s_nwb = 0;
-        if (s_nwb > 0) {
-            for (int idx = tid; idx < s_nwb * kExtCols; idx += kThreads) {
-                const int w = idx / kExtCols, c = idx - w * kExtCols;
-                const int32_t topf = s.top_f[c];
-                s.B[idx] = topf >= -1 ? above_mask((s_wlo + w) * 32, topf) : 0u;
-            }
-            __syncthreads();
-        }
-    }
-    if (s_nwb > 0)
-        flood(s, s_nwb, slot_col, slot_dist, cs);
-
-    // ---- outputs for the interior column -------------------------------------
-    const int lx = tid % kTile, lz = tid / kTile;
-    const int gx = x0 + lx, gz = z0 + lz;
-    if (!in_world(a, gx, gz))
-        return;
-    const int c0 = slot_col[0];
-    const int32_t topf = s.top_f[c0];
-    const uint64_t col_off = (static_cast<uint64_t>(gz) * a.W + gx) * H;
-    uint4* light_col = reinterpret_cast<uint4*>(env_light + col_off);
-
-    if (a.mode == 0) {
-        a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(topf + a.terrain.origin_y);
-        const int32_t top = s.top_t[c0];
-        uint4* id_col = reinterpret_cast<uint4*>(env_ids + col_off);
-        for (int r0 = 0; r0 < H; r0 += 16) {
-            uint32_t wv[4];
-            if (r0 > top) {
-                wv[0] = wv[1] = wv[2] = wv[3] = 0u;
-            } else if (r0 + 15 <= top - 4) {
-                wv[0] = wv[1] = wv[2] = wv[3] = 0x03030303u;
-            } else {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint32_t v = 0;
-#pragma unroll
-                    for (int b = 0; b < 4; ++b)
-                        v |= static_cast<uint32_t>(layer_block(r0 + 4 * q + b, top)) << (8 * b);
-                    wv[q] = v;
-                }
-            }
-            id_col[r0 >> 4] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-        }
-        // Overrides (same thread, program order: these bytes land last).
-        const uint32_t beg = s.beg[c0], n = s.cnt[c0];
-        for (uint32_t i = 0; i < n; ++i) {
-            const uint64_t e = a.entries[beg + i];
-            const int32_t y = static_cast<int32_t>(entry_y(e));
-            if (i + 1 < n && static_cast<int32_t>(entry_y(a.entries[beg + i + 1])) == y)
-                continue;
-            env_ids[col_off + y] = entry_block(e);
-        }
-    }
-
-    for (int r0 = wlo_rows; r0 <= whi_rows; r0 += 16) {
-        const int word = r0 >> 5;
-        const int j0 = r0 & 31;
-        const int bw = word - b_wlo, sw = word - s_wlo;
-        uint32_t bn[4] = { 0u, 0u, 0u, 0u }, sn[4] = { 0u, 0u, 0u, 0u };
-        bool block_any = false;
-        if (b_nwb > 0 && bw >= 0 && bw < b_nwb) {
-#pragma unroll
-            for (int w = 0; w < kMaxWords; ++w)
-                if (w == bw) {
-#pragma unroll
-                    for (int p = 0; p < 4; ++p)
-                        bn[p] = cb[w][p] >> j0;
-                }
-            block_any = ((bn[0] | bn[1] | bn[2] | bn[3]) & 0xFFFFu) != 0u;
-        }
-        const bool sky_bfs = s_nwb > 0 && sw >= 0 && sw < s_nwb;
-        if (sky_bfs) {
-#pragma unroll
-            for (int w = 0; w < kMaxWords; ++w)
-                if (w == sw) {
-#pragma unroll
-                    for (int p = 0; p < 4; ++p)
-                        sn[p] = cs[w][p] >> j0;
-                }
-        }
-        uint32_t wv[4];
-        if (!block_any && !sky_bfs && (r0 > topf || r0 + 15 <= topf)) {
-            const uint32_t v = r0 > topf ? 0xF0F0F0F0u : 0u;
-            wv[0] = wv[1] = wv[2] = wv[3] = v;
-        } else {
-            const uint32_t lit = sky_bfs ? 0u : above_mask(r0, topf);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int j = 4 * q;
-                uint32_t v = spread4((bn[0] >> j) & 0xFu) | (spread4((bn[1] >> j) & 0xFu) << 1)
-                    | (spread4((bn[2] >> j) & 0xFu) << 2) | (spread4((bn[3] >> j) & 0xFu) << 3);
-                if (sky_bfs)
-                    v |= (spread4((sn[0] >> j) & 0xFu) << 4) | (spread4((sn[1] >> j) & 0xFu) << 5)
-                        | (spread4((sn[2] >> j) & 0xFu) << 6) | (spread4((sn[3] >> j) & 0xFu) << 7);
-                else
-                    v |= spread4((lit >> j) & 0xFu) * 0xF0u;
-                wv[q] = v;
-            }
-        }
-        light_col[r0 >> 4] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        __syncwarp();
+        if (row_ok)
+            copy_out(a.light + static_cast<uint64_t>(env) * a.env_stride + row_off, wlo_rows, whi_rows);
     }
 }
 
-} // namespace
+// Persistent: one CTA per SM walks the tiles.
+template <int NW>
+__global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Smem<NW>& s = *reinterpret_cast<Smem<NW>*>(smem_raw);
+    const uint32_t n = a.mode == 0 ? a.n_tiles : *a.dirty_count;
+    for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
+        uint32_t tile_id = i;
+        int32_t wlo_rows = 0, whi_rows = 32 * NW - 1;
+        if (a.mode != 0) {
+            tile_id = a.dirty_list[i];
+            const uint32_t win = a.dirty_window[tile_id];
+            wlo_rows = static_cast<int32_t>(win & 0xFFFFu) & ~15;
+            whi_rows = min(static_cast<int32_t>(win >> 16) | 15, 32 * NW - 1);
+        }
+        process_tile<NW>(a, s, tile_id, wlo_rows, whi_rows);
+        __syncthreads();
+    }
+}
 
-size_t tile_smem_bytes() { return sizeof(Smem); }
+// Terrain surface of every column of every env (local y, clamped to
+// [-1, H+4], which preserves the layer rule inside the region).
+__global__ void terrain_kernel(const uint32_t* seeds, TerrainParams t, int32_t W, int32_t D, uint64_t total,
+    int16_t* out)
+{
+    const uint64_t columns = static_cast<uint64_t>(W) * D;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t env = static_cast<uint32_t>(i / columns);
+        const uint64_t col = i - env * columns;
+        const int32_t x = static_cast<int32_t>(col % W), z = static_cast<int32_t>(col / W);
+        int32_t top = terrain_top_local(t, seeds[env], t.origin_x + x, t.origin_z + z);
+        top = top < -1 ? -1 : (top > t.height + 4 ? t.height + 4 : top);
+        out[i] = static_cast<int16_t>(top);
+    }
+}
 
-int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream)
+template <int NW>
+int launch_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
 {
     static bool attr_set[64] = {};
-    int dev = ctx->device;
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-            static_cast<int>(sizeof(Smem)));
+    static int sm_count[64] = {};
+    const int dev = ctx->device;
+    if (dev < 0 || dev >= 64) {
+        set_error("device index out of range");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(tile_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            static_cast<int>(sizeof(Smem<NW>)));
         if (e != cudaSuccess)
             return cuda_fail(e, "cudaFuncSetAttribute(tile_kernel)");
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute(multiprocessor count)");
         attr_set[dev] = true;
     }
     if (n_tiles == 0)
         return BLK_OK;
+    uint32_t grid = n_tiles < static_cast<uint32_t>(sm_count[dev]) ? n_tiles : static_cast<uint32_t>(sm_count[dev]);
+    if (grid > ctx->park_ctas)
+        grid = ctx->park_ctas;
+    tile_kernel<NW><<<grid, kThreads, sizeof(Smem<NW>), stream>>>(a);
+    return cuda_fail(cudaGetLastError(), "tile_kernel launch");
+}
+
+} // namespace
+
+// Halo columns of the extended tile in the order threads take them: nearest
+// cone distance first, 32 at a time (one warp), each group of 32 using 32
+// distinct shared-memory banks (ext column index mod 32) so that a warp's
+// plane accesses, and those of its +-1 / +-60 neighbours, are conflict-free.
+void halo_order_table(uint16_t* out)
+{
+    std::vector<int> rest;
+    for (int d = 1; d <= 2 * kHalo; ++d)
+        for (int c = 0; c < kExtCols; ++c) {
+            const int ex = c % kExt, ez = c / kExt;
+            const int dx = std::max(0, std::max(kHalo - ex, ex - (kHalo + kTile - 1)));
+            const int dz = std::max(0, std::max(kHalo - ez, ez - (kHalo + kTile - 1)));
+            if (dx + dz == d)
+                rest.push_back(c);
+        }
+    int n = 0;
+    std::vector<char> taken(rest.size(), 0);
+    size_t first = 0;
+    while (n < kHaloCols) {
+        uint32_t banks = 0;
+        int got = 0;
+        for (size_t i = first; i < rest.size() && got < 32; ++i) {
+            if (taken[i])
+                continue;
+            const uint32_t bit = 1u << (rest[i] & 31);
+            if (banks & bit)
+                continue;
+            banks |= bit;
+            taken[i] = 1;
+            out[n++] = static_cast<uint16_t>(rest[i]);
+            ++got;
+        }
+        for (size_t i = first; i < rest.size() && got < 32; ++i) // fewer than 32 banks left
+            if (!taken[i]) {
+                taken[i] = 1;
+                out[n++] = static_cast<uint16_t>(rest[i]);
+                ++got;
+            }
+        while (first < rest.size() && taken[first])
+            ++first;
+    }
+}
+
+int halo_order_size() { return kHaloCols; }
+
+int launch_terrain(blk_ctx* ctx, cudaStream_t stream)
+{
+    const uint64_t total = static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->columns_per_env;
+    uint64_t blocks = (total + 255) / 256;
+    if (blocks > 148ull * 32)
+        blocks = 148ull * 32;
+    terrain_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
+        static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), total, ctx->terrain_top);
+    return cuda_fail(cudaGetLastError(), "terrain_kernel launch");
+}
+
+int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream)
+{
     TileArgs a {};
     a.ids = ctx->ids;
     a.light = ctx->light;
     a.hmap = ctx->hmap;
-    a.seeds = ctx->seeds;
+    a.terrain_top = ctx->terrain_top;
+    a.halo_order = ctx->halo_order;
     a.col_offset = ctx->col_offset;
     a.entries = ctx->entries;
     a.dirty_list = ctx->dirty_list;
     a.dirty_window = ctx->dirty_window;
     a.dirty_count = ctx->dirty_count;
     a.flags = ctx->flags;
-    a.terrain = terrain_params(ctx);
+    a.park = ctx->park;
+    a.n_tiles = n_tiles;
+    a.origin_y = ctx->cfg.origin_y;
     a.W = static_cast<int32_t>(ctx->cfg.width);
-    a.H = static_cast<int32_t>(ctx->cfg.height);
     a.D = static_cast<int32_t>(ctx->cfg.depth);
     a.tiles_x = static_cast<int32_t>(ctx->tiles_x);
     a.tiles_z = static_cast<int32_t>(ctx->tiles_z);
     a.env_stride = ctx->env_stride;
     a.columns = ctx->columns_per_env;
     a.mode = mode;
-    tile_kernel<<<n_tiles, kThreads, sizeof(Smem), stream>>>(a);
-    return cuda_fail(cudaGetLastError(), "tile_kernel launch");
+    switch (ctx->cfg.height / 32) {
+    case 1:
+        return launch_nw<1>(ctx, a, n_tiles, stream);
+    case 2:
+        return launch_nw<2>(ctx, a, n_tiles, stream);
+    case 3:
+        return launch_nw<3>(ctx, a, n_tiles, stream);
+    case 4:
+        return launch_nw<4>(ctx, a, n_tiles, stream);
+    default:
+        set_error("unsupported height");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
 }
 
 } // namespace blk

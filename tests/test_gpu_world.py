@@ -156,6 +156,34 @@ def test_duplicates_outside_and_invalid_overrides(B, oracle):
     wb.close()
 
 
+def test_dense_column_overrides_deterministic(B, oracle):
+    """Many overrides per column, duplicates included (latest wins), several
+    runs: the per-column sort must be race-free and the result deterministic."""
+    W, H, D = 40, 64, 40
+    cfg = B.WorldConfig(num_envs=2, width=W, height=H, depth=D, terrain=TERRAIN_FBM, base=30, amplitude=10.0)
+    wb = B.WorldBatch(cfg)
+    rng = np.random.default_rng(99)
+    n = 20000
+    cols = rng.integers(0, 400, n)
+    x, z = (cols % 20) * 2, (cols // 20) * 2
+    y = rng.integers(0, H, n)
+    blk = rng.choice([0, 3, 4, 2], n).astype(np.uint8)
+    env = rng.integers(0, 2, n).astype(np.uint16)
+    xyz = np.stack([x, y, z], 1)
+    o = B.make_overrides(xyz, blk, env=env)
+    want = []
+    for e in range(2):
+        sel = env == e
+        spec = WorldSpec(e + 1, W, H, D, terrain=TERRAIN_FBM, base=30, amplitude=10.0)
+        want.append(oracle.generate(spec, xyz[sel], blk[sel], method="multi"))
+    for run in range(3):
+        wb.generate([1, 2], o)
+        wb.sync()
+        for e in range(2):
+            _assert_world(wb, e, *want[e], f"run{run} env{e}")
+    wb.close()
+
+
 @pytest.mark.parametrize("base", [-5, 200, 31])
 def test_empty_and_full_worlds(B, oracle, base):
     cfg = B.WorldConfig(num_envs=1, width=33, height=32, depth=31, terrain=TERRAIN_FLAT, base=base)
