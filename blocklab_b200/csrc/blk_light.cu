@@ -76,11 +76,12 @@ struct TileArgs {
 
 template <int NW>
 struct Smem {
-    static constexpr int kPlane = NW * kExtCols;                      // words per plane
+    static constexpr int kBand = NW < 4 ? NW : 4;                     // max words of one flood band
+    static constexpr int kPlane = kBand * kExtCols;                   // words per plane
     static constexpr int kPitch = 32 * NW + 16;                       // staging bytes per column
     static constexpr int kStageWords = (kWarps / 2) * kTile * kPitch / 4; // half the warps at a time
     static constexpr int kPoolWords = 3 * kPlane > kStageWords ? 3 * kPlane : kStageWords;
-    // O | B0 | B1 during the floods; output staging afterwards.
+    // O | B0 | B1 during the floods; output staging otherwise.
     uint32_t pool[kPoolWords];
     int16_t top_t[kExtCols];   // terrain surface (local, clamped to [-1, H+4]); unused in relight mode
     int16_t top_f[kExtCols];   // final highest opaque local y, -1 none, -2 outside the world
@@ -183,8 +184,9 @@ __device__ inline void id_bits(const uint8_t* column, int ybase, uint32_t& open,
 // planes of the interior column (slot 0) into cnt[w][p]. slot[k] packs the
 // ext column (low 16 bits) and its cone distance (high bits); -1 = unused.
 template <int NW, int NB>
-__device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[NW][4])
+__device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Smem<NW>::kBand][4])
 {
+    constexpr int KB = Smem<NW>::kBand;
     constexpr int P = Smem<NW>::kPlane;
     const uint32_t* O = s.O();
     uint32_t own[kSlots][NB];
@@ -199,7 +201,7 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[NW
     for (int w = 0; w < NB; ++w)
         open0[w] = O[w * kExtCols + (slot[0] & 0xFFFF)];
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
+    for (int w = 0; w < KB; ++w) {
         cnt[w][0] = w < NB ? own[0][w < NB ? w : 0] : 0u;
         cnt[w][1] = 0;
         cnt[w][2] = 0;
@@ -252,60 +254,25 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[NW
 }
 
 template <int NW>
-__device__ void flood_any(int nb, Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[NW][4])
+__device__ void flood_any(int nb, Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Smem<NW>::kBand][4])
 {
+    constexpr int KB = Smem<NW>::kBand;
     switch (nb) {
     case 1:
         flood<NW, 1>(s, slot, cnt);
         break;
     case 2:
-        if constexpr (NW >= 2)
-            flood<NW, 2 <= NW ? 2 : NW>(s, slot, cnt);
+        if constexpr (KB >= 2)
+            flood<NW, KB >= 2 ? 2 : 1>(s, slot, cnt);
         break;
     case 3:
-        if constexpr (NW >= 3)
-            flood<NW, 3 <= NW ? 3 : NW>(s, slot, cnt);
+        if constexpr (KB >= 3)
+            flood<NW, KB >= 3 ? 3 : 1>(s, slot, cnt);
         break;
     default:
-        if constexpr (NW >= 4)
-            flood<NW, NW>(s, slot, cnt);
+        if constexpr (KB >= 4)
+            flood<NW, KB>(s, slot, cnt);
         break;
-    }
-}
-
-// Re-indexes counter planes from band words (word w holds rows lo + 32w ..)
-// to absolute words (word w holds rows 32w ..); rows outside the band are 0.
-template <int NW>
-__device__ inline void realign(uint32_t (&cnt)[NW][4], int lo, int nb)
-{
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        uint32_t out[NW];
-#pragma unroll
-        for (int aw = 0; aw < NW; ++aw) {
-            const int b = 32 * aw - lo; // band offset of the absolute word's first row
-            uint32_t v = 0u;
-            if (b > -32 && b < 32 * nb) {
-                if (b < 0) {
-                    v = cnt[0][p] << (-b);
-                } else {
-                    const int w0 = b >> 5, sh = b & 31;
-                    uint32_t lo_w = 0u, hi_w = 0u;
-#pragma unroll
-                    for (int w = 0; w < NW; ++w) {
-                        if (w == w0)
-                            lo_w = cnt[w][p];
-                        if (w == w0 + 1 && w < nb)
-                            hi_w = cnt[w][p];
-                    }
-                    v = __funnelshift_r(lo_w, hi_w, sh);
-                }
-            }
-            out[aw] = v;
-        }
-#pragma unroll
-        for (int aw = 0; aw < NW; ++aw)
-            cnt[aw][p] = out[aw];
     }
 }
 
@@ -530,136 +497,74 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
             }
     };
 
-    // Band of rows [rlo, rhi] clipped to the region: first row and word count.
-    auto band = [&](int32_t rlo, int32_t rhi, int& blo, int& nb) {
-        rlo = max(rlo, 0);
-        rhi = min(rhi, H - 1);
-        if (rlo > rhi) {
-            nb = 0;
-            return;
-        }
-        blo = rlo;
-        nb = (rhi - rlo) / 32 + 1;
-    };
-
-    uint32_t cb[NW][4], cs[NW][4];
-    int b_lo = 0, b_nb = 0, s_lo = 0, s_nb = 0;
-
-    // ---- block light -------------------------------------------------------
-    if (a.mode == 0) {
-        if (s.tmin <= s.tmax)
-            band(s.tmin - kMaxDistance, s.tmax + kMaxDistance, b_lo, b_nb);
-    } else {
-        band(wlo_rows - kMaxDistance, whi_rows + kMaxDistance, b_lo, b_nb);
-    }
-    if (b_nb > 0) {
-        build(b_lo, b_nb, 0);
-        __syncthreads();
-        if (a.mode == 1) {
-            // Any torch in the band? (generation knows from the override lists.)
-            bool any = false;
-            for (int idx = tid; idx < b_nb * kExtCols; idx += kThreads)
-                any |= s.B(0)[idx] != 0u;
-            if (__syncthreads_or(any) == 0)
-                b_nb = 0;
-        }
-    }
-    if (b_nb > 0) {
-        flood_any<NW>(b_nb, s, slot, cb);
-        realign<NW>(cb, b_lo, b_nb);
-    }
-
-    // ---- sky light -----------------------------------------------------------
-    if (a.mode == 0) {
-        if (s.dmin <= s.dmax)
-            band(s.dmin - kMaxDistance, s.dmax + kMaxDistance, s_lo, s_nb);
-        if (s_nb > 0) {
-            __syncthreads();
-            build(s_lo, s_nb, 1);
-            __syncthreads();
-        }
-    } else {
-        // Same rows as block light. The sky flood is needed if an interior
-        // column has an open cell at or below its top inside the output rows.
-        band(wlo_rows - kMaxDistance, whi_rows + kMaxDistance, s_lo, s_nb);
-        __syncthreads();
-        if (s_nb > 0)
-            build(s_lo, s_nb, 1);
-        __syncthreads();
-        bool dark = false;
-        const int c = slot[0];
-        const int32_t topf0 = s.top_f[c];
-        if (topf0 >= 0) {
-#pragma unroll
-            for (int w = 0; w < NW; ++w)
-                if (w < s_nb) {
-                    const int ybase = s_lo + 32 * w;
-                    dark |= (s.O()[w * kExtCols + c] & ~above_mask(ybase, topf0) & rows_mask(ybase, wlo_rows, whi_rows))
-                        != 0u;
-                }
-        }
-        if (__syncthreads_or(dark) == 0)
-            s_nb = 0;
-    }
-    uint32_t* park = a.park + static_cast<uint64_t>(blockIdx.x) * (NW * 4 * kThreads);
-    if (s_nb > 0) {
-        // The block planes wait in this CTA's global scratch slice while the
-        // sky flood uses the registers (rare: needs dark open cells); the
-        // output reads them back from there.
-#pragma unroll
-        for (int w = 0; w < NW; ++w)
-#pragma unroll
-            for (int p = 0; p < 4; ++p)
-                park[(w * 4 + p) * kThreads + tid] = b_nb > 0 ? cb[w][p] : 0u;
-        flood_any<NW>(s_nb, s, slot, cs);
-        realign<NW>(cs, s_lo, s_nb);
-    }
-
-    // ---- outputs for the interior columns -------------------------------------
+    // ---- output staging helpers ----------------------------------------------
     // Each warp owns one z row of 32 columns, contiguous in memory. A lane
-    // builds its column's bytes in the warp's staging area (the flood planes
-    // are free now), then the warp stores the row with coalesced 16-byte
-    // stores. Half of the warps stage at a time.
+    // builds its column's bytes in the warp's staging area (the flood planes),
+    // then the warp stores the row with coalesced 16-byte stores. Half of the
+    // warps stage at a time. The helpers derive everything from tid, the tile
+    // origin and shared memory, so nothing of theirs stays live across a flood.
     constexpr int kPitch = Smem<NW>::kPitch;
     constexpr int kChunks = H / 16;
-    const int c0 = slot[0];
-    const int32_t topf = s.top_f[c0];
-    const int32_t top = s.top_t[c0];
-    const uint64_t* obeg;
-    uint32_t ocnt;
-    if (a.mode == 0)
-        overrides_of(c0, obeg, ocnt);
-    const int gx = x0 + lane, gz = z0 + warp;
-    const bool valid = in_world(a, gx, gz);
-    const bool row_ok = gz < a.D;
-    const int ncols = min(kTile, a.W - x0);
-    uint8_t* stage = reinterpret_cast<uint8_t*>(s.pool) + (warp & (kWarps / 2 - 1)) * (kTile * kPitch);
-    uint8_t* my = stage + lane * kPitch;
-    const uint64_t row_off = (static_cast<uint64_t>(gz) * a.W + x0) * H;
+    constexpr int KB = Smem<NW>::kBand;
+    auto stage_of = [&]() {
+        return reinterpret_cast<uint8_t*>(s.pool) + (warp & (kWarps / 2 - 1)) * (kTile * kPitch) + lane * kPitch;
+    };
+    auto row_offset = [&]() { return (static_cast<uint64_t>(z0 + warp) * a.W + x0) * H; };
 
-    auto copy_out = [&](uint8_t* dst, int rlo, int rhi) {
+    // Copies the staged 16-row chunks selected by `mask` (bit ch = rows 16ch..).
+    auto copy_out = [&](uint8_t* dst, uint32_t mask) {
+        const uint8_t* stage = reinterpret_cast<const uint8_t*>(s.pool) + (warp & (kWarps / 2 - 1)) * (kTile * kPitch);
+        const int ncols = min(kTile, a.W - x0);
 #pragma unroll
         for (int i = 0; i < kChunks; ++i) {
             const int idx = i * 32 + lane;
             const int col = idx / kChunks, ch = idx - col * kChunks;
-            const int r0 = ch * 16;
-            if (col < ncols && r0 >= rlo && r0 <= rhi)
-                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(col) * H + r0)
-                    = *reinterpret_cast<const uint4*>(stage + col * kPitch + r0);
+            if (col < ncols && ((mask >> ch) & 1u))
+                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(col) * H + ch * 16)
+                    = *reinterpret_cast<const uint4*>(stage + col * kPitch + ch * 16);
         }
     };
 
-    for (int round = 0; round < 2; ++round) {
-        __syncthreads();
-        if ((warp >> 4) != round)
-            continue;
-        if (a.mode == 0) {
-            if (valid) {
-                a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(topf + a.origin_y);
-                // Layer rule branch-free: id = [y <= top] + [y <= top-1] + [y <= top-4].
-                const uint32_t t0 = static_cast<uint32_t>(min(max(top, -1), 127) & 0xFF) * 0x01010101u;
-                const uint32_t t1 = static_cast<uint32_t>(min(max(top - 1, -1), 127) & 0xFF) * 0x01010101u;
-                const uint32_t t4 = static_cast<uint32_t>(min(max(top - 4, -1), 127) & 0xFF) * 0x01010101u;
+    // One 16-row chunk of light bytes: block bits, sky bits for the chunk rows
+    // in sky_rows, trivial sky light (15 above the final top) elsewhere.
+    auto emit = [&](uint8_t* my, int32_t topf, int r0, uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3, uint32_t s0,
+                    uint32_t s1, uint32_t s2, uint32_t s3, uint32_t sky_rows) {
+        const bool block_any = (b0 | b1 | b2 | b3) != 0u;
+        uint32_t wv[4];
+        if (!block_any && sky_rows == 0u && (r0 > topf || r0 + 15 <= topf)) {
+            const uint32_t v = r0 > topf ? 0xF0F0F0F0u : 0u;
+            wv[0] = wv[1] = wv[2] = wv[3] = v;
+        } else {
+            const uint32_t lit = above_mask(r0, topf) & ~sky_rows;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int j = 4 * q;
+                uint32_t v = spread4((b0 >> j) & 0xFu) | (spread4((b1 >> j) & 0xFu) << 1)
+                    | (spread4((b2 >> j) & 0xFu) << 2) | (spread4((b3 >> j) & 0xFu) << 3);
+                if (sky_rows != 0u)
+                    v |= (spread4((s0 >> j) & 0xFu) << 4) | (spread4((s1 >> j) & 0xFu) << 5)
+                        | (spread4((s2 >> j) & 0xFu) << 6) | (spread4((s3 >> j) & 0xFu) << 7);
+                v |= spread4((lit >> j) & 0xFu) * 0xF0u;
+                wv[q] = v;
+            }
+        }
+        *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    };
+
+    // ---- block ids and height map (generation) -------------------------------
+    if (a.mode == 0) {
+        for (int round = 0; round < 2; ++round) {
+            __syncthreads();
+            if ((warp >> 4) != round)
+                continue;
+            const int gx = x0 + lane, gz = z0 + warp;
+            if (in_world(a, gx, gz)) {
+                const int c0 = slot[0];
+                const int32_t top = s.top_t[c0];
+                uint8_t* my = stage_of();
+                a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(s.top_f[c0] + a.origin_y);
+                // Layer rule branch-free: id = [y <= top] + [y <= top-1] + [y <= top-4],
+                // compared chunk-relative in signed bytes (y - r0 is 0..15).
 #pragma unroll
                 for (int ch = 0; ch < kChunks; ++ch) {
                     const int r0 = ch * 16;
@@ -669,9 +574,13 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
                     } else if (r0 + 15 <= top - 4) {
                         wv[0] = wv[1] = wv[2] = wv[3] = 0x03030303u;
                     } else {
+                        const int d = top - r0; // -4 .. 15 here
+                        const uint32_t t0 = static_cast<uint32_t>(d & 0xFF) * 0x01010101u;
+                        const uint32_t t1 = static_cast<uint32_t>((d - 1) & 0xFF) * 0x01010101u;
+                        const uint32_t t4 = static_cast<uint32_t>((d - 4) & 0xFF) * 0x01010101u;
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            const uint32_t y4 = static_cast<uint32_t>(r0 + 4 * q) * 0x01010101u + 0x03020100u;
+                            const uint32_t y4 = static_cast<uint32_t>(4 * q) * 0x01010101u + 0x03020100u;
                             wv[q] = (__vcmples4(y4, t0) & 0x01010101u) + (__vcmples4(y4, t1) & 0x01010101u)
                                 + (__vcmples4(y4, t4) & 0x01010101u);
                         }
@@ -679,6 +588,9 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
                     *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
                 // Winning overrides (latest of each y) replace the terrain bytes.
+                const uint64_t* obeg;
+                uint32_t ocnt;
+                overrides_of(c0, obeg, ocnt);
                 for (uint32_t i = 0; i < ocnt; ++i) {
                     const uint64_t v = __ldg(obeg + i);
                     const int32_t y = static_cast<int32_t>(entry_y(v));
@@ -688,74 +600,239 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
                 }
             }
             __syncwarp();
-            if (row_ok)
-                copy_out(env_ids + row_off, 0, H - 1);
-            __syncwarp();
+            if (z0 + warp < a.D)
+                copy_out(env_ids + row_offset(), 0xFFFFFFFFu);
         }
+    }
 
-        if (valid) {
-            // One 16-row chunk of light bytes: block bits bn, sky bits sn for
-            // the chunk rows in sky_rows, trivial sky light elsewhere.
-            auto emit = [&](int r0, uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3, uint32_t s0, uint32_t s1,
-                            uint32_t s2, uint32_t s3, uint32_t sky_rows) {
-                const bool block_any = (b0 | b1 | b2 | b3) != 0u;
-                uint32_t wv[4];
-                if (!block_any && sky_rows == 0u && (r0 > topf || r0 + 15 <= topf)) {
-                    const uint32_t v = r0 > topf ? 0xF0F0F0F0u : 0u;
-                    wv[0] = wv[1] = wv[2] = wv[3] = v;
-                } else {
-                    const uint32_t lit = above_mask(r0, topf) & ~sky_rows;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int j = 4 * q;
-                        uint32_t v = spread4((b0 >> j) & 0xFu) | (spread4((b1 >> j) & 0xFu) << 1)
-                            | (spread4((b2 >> j) & 0xFu) << 2) | (spread4((b3 >> j) & 0xFu) << 3);
-                        if (sky_rows != 0u)
-                            v |= (spread4((s0 >> j) & 0xFu) << 4) | (spread4((s1 >> j) & 0xFu) << 5)
-                                | (spread4((s2 >> j) & 0xFu) << 6) | (spread4((s3 >> j) & 0xFu) << 7);
-                        v |= spread4((lit >> j) & 0xFu) * 0xF0u;
-                        wv[q] = v;
-                    }
+    // ---- light: rows that can hold non-trivial light ---------------------------
+    // Block band: torch rows +-14; sky band: rows of dark open cells +-14.
+    // Output rows o = the bands' hull rounded to 16-row chunks (relight: the
+    // dirty window). They are lit in windows of at most KB words: a window's
+    // flood covers its output rows +-14 so that every path of length <= 14
+    // that ends in them stays inside. Mode 0 bands already carry that margin:
+    // one window of the output rows when they fit. Otherwise windows of 96
+    // output rows with a margin of 16 rows below (every window starts on a
+    // 16-row chunk, so its band words split into whole chunks) and 14 above.
+    // The plan reads shared memory only, so it is recomputed after each flood
+    // instead of being held in registers across it.
+    struct Plan {
+        int32_t r_lo, r_hi, w_lo, nb;
+        int32_t b_lo, b_hi, s_lo, s_hi;
+        uint32_t o_chunks;
+        int n_win;
+        bool whole;
+    };
+    auto plan_tile = [&](Plan& p) {
+        int32_t o_lo = 0, o_hi = -1;
+        p.b_lo = H;
+        p.b_hi = -1;
+        p.s_lo = H;
+        p.s_hi = -1;
+        if (a.mode == 0) {
+            const int32_t tmin = s.tmin, tmax = s.tmax, dmin = s.dmin, dmax = s.dmax;
+            if (tmin <= tmax) {
+                p.b_lo = max(tmin - kMaxDistance, 0);
+                p.b_hi = min(tmax + kMaxDistance, H - 1);
+            }
+            if (dmin <= dmax) {
+                p.s_lo = max(dmin - kMaxDistance, 0);
+                p.s_hi = min(dmax + kMaxDistance, H - 1);
+            }
+            const int32_t u_lo = min(p.b_lo, p.s_lo), u_hi = max(p.b_hi, p.s_hi);
+            if (u_lo <= u_hi) {
+                o_lo = u_lo & ~15;
+                o_hi = min(u_hi | 15, H - 1);
+            }
+        } else {
+            o_lo = wlo_rows;
+            o_hi = whi_rows;
+            p.b_lo = p.s_lo = max(o_lo - kMaxDistance, 0);
+            p.b_hi = p.s_hi = min(o_hi + kMaxDistance, H - 1);
+        }
+        p.whole = o_lo <= o_hi
+            && ((a.mode == 0 && o_hi - o_lo + 1 <= 32 * KB)
+                || (min(o_hi + kMaxDistance, H - 1) - max(o_lo - 16, 0) + 1 <= 32 * KB));
+        p.n_win = o_lo > o_hi ? 0 : (p.whole ? 1 : (o_hi - o_lo + 96) / 96);
+        p.o_chunks = o_lo > o_hi ? 0u : (((2u << (o_hi >> 4)) - 1u) & ~((1u << (o_lo >> 4)) - 1u));
+        p.r_lo = o_lo;
+        p.r_hi = o_hi;
+    };
+    auto plan_window = [&](Plan& p, int wi) {
+        plan_tile(p);
+        const int32_t o_lo = p.r_lo, o_hi = p.r_hi;
+        int32_t w_hi;
+        if (p.whole) {
+            p.w_lo = a.mode == 0 ? o_lo : max(o_lo - 16, 0);
+            w_hi = a.mode == 0 ? o_hi : min(o_hi + kMaxDistance, H - 1);
+        } else {
+            p.r_lo = o_lo + 96 * wi;
+            p.r_hi = min(p.r_lo + 95, o_hi);
+            p.w_lo = max(p.r_lo - 16, 0);
+            w_hi = min(p.r_hi + kMaxDistance, H - 1);
+        }
+        p.nb = (w_hi - p.w_lo) / 32 + 1;
+    };
+
+    uint32_t* park = a.park + static_cast<uint64_t>(blockIdx.x) * (KB * 4 * kThreads);
+    constexpr uint32_t kAllChunks = (1u << kChunks) - 1u;
+    int n_win;
+    {
+        Plan p;
+        plan_tile(p);
+        n_win = p.n_win;
+    }
+    // Pass wi < n_win lights window wi. When one window covers the output
+    // rows (always for H <= 128) its pass also writes the trivial chunks;
+    // otherwise a last pass writes them (generation only).
+    for (int wi = 0; wi < max(n_win, 1); ++wi) {
+        uint32_t cb[KB][4], cs[KB][4];
+        bool have_block = false, have_sky = false;
+        if (n_win > 0) {
+            Plan p;
+            plan_window(p, wi);
+            const bool do_block = p.b_lo <= p.b_hi && p.b_lo <= p.r_hi && p.b_hi >= p.r_lo;
+            const bool do_sky = p.s_lo <= p.s_hi && p.s_lo <= p.r_hi && p.s_hi >= p.r_lo;
+            if (do_block) {
+                __syncthreads();
+                build(p.w_lo, p.nb, 0);
+                __syncthreads();
+                bool go = true;
+                if (a.mode == 1) {
+                    // Any torch in the window? (generation knows from the override lists.)
+                    bool any = false;
+                    for (int idx = tid; idx < p.nb * kExtCols; idx += kThreads)
+                        any |= s.B(0)[idx] != 0u;
+                    go = __syncthreads_or(any) != 0;
                 }
-                *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-            };
-            if (s_nb == 0) {
-                // Block planes in registers, sky light trivial.
+                if (go) {
+                    flood_any<NW>(p.nb, s, slot, cb);
+                    have_block = true;
+                }
+            }
+            if (do_sky) {
+                plan_window(p, wi);
+                __syncthreads();
+                build(p.w_lo, p.nb, 1);
+                __syncthreads();
+                bool go = true;
+                if (a.mode == 1) {
+                    // Needed if an interior column has an open cell at or below
+                    // its top inside the output rows.
+                    bool dark = false;
+                    const int32_t topf = s.top_f[slot[0]];
+                    if (topf >= 0) {
 #pragma unroll
-                for (int w = 0; w < NW; ++w)
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const int r0 = 32 * w + 16 * half;
-                        if (r0 < wlo_rows || r0 > whi_rows)
-                            continue;
-                        const int sh = 16 * half;
-                        if (b_nb > 0)
-                            emit(r0, (cb[w][0] >> sh) & 0xFFFFu, (cb[w][1] >> sh) & 0xFFFFu, (cb[w][2] >> sh) & 0xFFFFu,
-                                (cb[w][3] >> sh) & 0xFFFFu, 0u, 0u, 0u, 0u, 0u);
-                        else
-                            emit(r0, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u);
+                        for (int w = 0; w < KB; ++w)
+                            if (w < p.nb) {
+                                const int ybase = p.w_lo + 32 * w;
+                                dark |= (s.O()[w * kExtCols + slot[0]] & ~above_mask(ybase, topf)
+                                            & rows_mask(ybase, p.r_lo, p.r_hi))
+                                    != 0u;
+                            }
                     }
-            } else {
-                // Block planes from the parked slice, sky planes in registers.
+                    go = __syncthreads_or(dark) != 0;
+                }
+                if (go) {
+                    // The block planes wait in this CTA's global scratch slice while
+                    // the sky flood uses the registers (rare: needs dark open cells).
 #pragma unroll
-                for (int w = 0; w < NW; ++w)
+                    for (int j = 0; j < KB; ++j)
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const int r0 = 32 * w + 16 * half;
-                        if (r0 < wlo_rows || r0 > whi_rows)
-                            continue;
-                        const int sh = 16 * half;
-                        const uint32_t* pk = park + w * 4 * kThreads + tid;
-                        emit(r0, (pk[0] >> sh) & 0xFFFFu, (pk[kThreads] >> sh) & 0xFFFFu,
-                            (pk[2 * kThreads] >> sh) & 0xFFFFu, (pk[3 * kThreads] >> sh) & 0xFFFFu,
-                            (cs[w][0] >> sh) & 0xFFFFu, (cs[w][1] >> sh) & 0xFFFFu, (cs[w][2] >> sh) & 0xFFFFu,
-                            (cs[w][3] >> sh) & 0xFFFFu, rows_mask(r0, s_lo, s_lo + 32 * s_nb - 1) & 0xFFFFu);
-                    }
+                        for (int q = 0; q < 4; ++q) {
+                            park[(j * 4 + q) * kThreads + tid] = have_block ? cb[j][q] : 0u;
+                            cb[j][q] = 0u; // the sky path reads the parked copy
+                        }
+                    flood_any<NW>(p.nb, s, slot, cs);
+                    have_sky = true;
+                }
             }
         }
-        __syncwarp();
-        if (row_ok)
-            copy_out(a.light + static_cast<uint64_t>(env) * a.env_stride + row_off, wlo_rows, whi_rows);
+
+        // Stage and store the pass's light chunks. Band word j, half h holds
+        // the 16-row chunk from row w_lo + 32j + 16h (w_lo is chunk aligned).
+        for (int round = 0; round < 2; ++round) {
+            __syncthreads();
+            if ((warp >> 4) != round)
+                continue;
+            Plan p;
+            uint32_t mask = kAllChunks, band_chunks = 0u;
+            if (n_win > 0) {
+                plan_window(p, wi);
+                const uint32_t r_chunks = ((2u << (p.r_hi >> 4)) - 1u) & ~((1u << (p.r_lo >> 4)) - 1u);
+                mask = p.whole ? (a.mode == 0 ? kAllChunks : r_chunks) : r_chunks;
+                band_chunks = (have_block || have_sky) ? r_chunks : 0u;
+            } else {
+                p.w_lo = 0;
+            }
+            const int gx = x0 + lane, gz = z0 + warp;
+            if (in_world(a, gx, gz)) {
+                uint8_t* my = stage_of();
+                const int32_t topf = s.top_f[slot[0]];
+                const uint32_t trivial = mask & ~band_chunks;
+#pragma unroll
+                for (int ch = 0; ch < kChunks; ++ch)
+                    if ((trivial >> ch) & 1u)
+                        emit(my, topf, ch * 16, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u);
+                if (band_chunks != 0u) {
+                    if (!have_sky) {
+#pragma unroll
+                        for (int j = 0; j < KB; ++j)
+#pragma unroll
+                            for (int half = 0; half < 2; ++half) {
+                                const int r0 = p.w_lo + 32 * j + 16 * half;
+                                if (r0 >= H || !((band_chunks >> (r0 >> 4)) & 1u))
+                                    continue;
+                                const int sh = 16 * half;
+                                emit(my, topf, r0, (cb[j][0] >> sh) & 0xFFFFu, (cb[j][1] >> sh) & 0xFFFFu,
+                                    (cb[j][2] >> sh) & 0xFFFFu, (cb[j][3] >> sh) & 0xFFFFu, 0u, 0u, 0u, 0u, 0u);
+                            }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < KB; ++j)
+#pragma unroll
+                            for (int half = 0; half < 2; ++half) {
+                                const int r0 = p.w_lo + 32 * j + 16 * half;
+                                if (r0 >= H || !((band_chunks >> (r0 >> 4)) & 1u))
+                                    continue;
+                                const int sh = 16 * half;
+                                const uint32_t* pk = park + j * 4 * kThreads + tid;
+                                emit(my, topf, r0, (pk[0] >> sh) & 0xFFFFu, (pk[kThreads] >> sh) & 0xFFFFu,
+                                    (pk[2 * kThreads] >> sh) & 0xFFFFu, (pk[3 * kThreads] >> sh) & 0xFFFFu,
+                                    (cs[j][0] >> sh) & 0xFFFFu, (cs[j][1] >> sh) & 0xFFFFu, (cs[j][2] >> sh) & 0xFFFFu,
+                                    (cs[j][3] >> sh) & 0xFFFFu, 0xFFFFu);
+                            }
+                    }
+                }
+            }
+            __syncwarp();
+            if (gz < a.D)
+                copy_out(a.light + static_cast<uint64_t>(env) * a.env_stride + row_offset(), mask);
+        }
+    }
+
+    // Several windows: the chunks outside the output rows (generation only).
+    if (a.mode == 0 && n_win > 1) {
+        for (int round = 0; round < 2; ++round) {
+            __syncthreads();
+            if ((warp >> 4) != round)
+                continue;
+            Plan p;
+            plan_tile(p);
+            const uint32_t mask = kAllChunks & ~p.o_chunks;
+            const int gx = x0 + lane, gz = z0 + warp;
+            if (in_world(a, gx, gz)) {
+                uint8_t* my = stage_of();
+                const int32_t topf = s.top_f[slot[0]];
+#pragma unroll
+                for (int ch = 0; ch < kChunks; ++ch)
+                    if ((mask >> ch) & 1u)
+                        emit(my, topf, ch * 16, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u);
+            }
+            __syncwarp();
+            if (gz < a.D)
+                copy_out(a.light + static_cast<uint64_t>(env) * a.env_stride + row_offset(), mask);
+        }
     }
 }
 
@@ -917,6 +994,14 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream)
         return launch_nw<3>(ctx, a, n_tiles, stream);
     case 4:
         return launch_nw<4>(ctx, a, n_tiles, stream);
+    case 5:
+        return launch_nw<5>(ctx, a, n_tiles, stream);
+    case 6:
+        return launch_nw<6>(ctx, a, n_tiles, stream);
+    case 7:
+        return launch_nw<7>(ctx, a, n_tiles, stream);
+    case 8:
+        return launch_nw<8>(ctx, a, n_tiles, stream);
     default:
         set_error("unsupported height");
         return BLK_ERR_INVALID_ARGUMENT;

@@ -73,7 +73,7 @@ enum blk_edit_kind {
 typedef struct blk_world_config {
     uint32_t num_envs;
     uint32_t width;    /* W: x extent, 1..4096 */
-    uint32_t height;   /* H: y extent, multiple of 32, 32..128 */
+    uint32_t height;   /* H: y extent, multiple of 32, 32..256 */
     uint32_t depth;    /* D: z extent, 1..4096 */
     int32_t origin_x;  /* world coordinate of local (0, 0, 0), shared by all envs */
     int32_t origin_y;

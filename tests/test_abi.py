@@ -38,7 +38,7 @@ def test_sky_light_at_time_matches_oracle(oracle):
 def test_invalid_config_rejected_without_device():
     from blocklab_b200 import _native as N
 
-    for bad in [dict(num_envs=0), dict(height=48), dict(height=256), dict(width=0), dict(terrain_mode=7)]:
+    for bad in [dict(num_envs=0), dict(height=48), dict(height=288), dict(width=0), dict(terrain_mode=7)]:
         c = dict(num_envs=1, width=8, height=32, depth=8, terrain_mode=1)
         c.update(bad)
         cfg = N.WorldConfigC(c["num_envs"], c["width"], c["height"], c["depth"], 0, 0, 0, c["terrain_mode"], 40, 50.0,

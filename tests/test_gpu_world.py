@@ -138,6 +138,41 @@ def test_random_overrides_match_oracle(B, oracle, terrain, base, amp):
     wb.close()
 
 
+@pytest.mark.parametrize("W,H,D,terrain,base,amp", [(70, 256, 40, TERRAIN_FBM, 40, 50.0),
+                                                     (45, 160, 33, TERRAIN_FLAT, 150, 0.0),
+                                                     (64, 224, 64, TERRAIN_FBM, 120, 100.0)])
+def test_tall_worlds_match_oracle(B, oracle, W, H, D, terrain, base, amp):
+    """Heights above 128: the layer rule over the upper rows, and tiles whose
+    torch rows are far apart, so their light is computed in several row windows."""
+    E = 2
+    origin = (3, 0, -7)
+    cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, origin=origin, terrain=terrain, base=base,
+                        amplitude=amp)
+    wb = B.WorldBatch(cfg)
+    rng = np.random.default_rng(H + base)
+    seeds = rng.integers(1, 1 << 31, E).astype(np.uint32)
+    lists, per = [], []
+    for e in range(E):
+        n = 4000
+        cells = rng.choice(W * H * D, n, replace=False)
+        xyz = np.stack([cells % W, (cells // W) % H, cells // (W * H)], 1) + np.array(origin)
+        blk = rng.choice([0, 3, 4, 1, 2], n, p=[0.5, 0.3, 0.1, 0.05, 0.05]).astype(np.uint8)
+        # torch columns spanning the whole height inside one tile
+        ty = np.arange(2, H - 1, 23)
+        txyz = np.stack([np.full_like(ty, 5), ty, np.full_like(ty, 6)], 1) + np.array(origin)
+        xyz = np.concatenate([xyz, txyz])
+        blk = np.concatenate([blk, np.full(len(ty), 4, np.uint8)])
+        per.append((xyz, blk))
+        lists.append(B.make_overrides(xyz, blk, env=e))
+    wb.generate(seeds, np.concatenate(lists))
+    wb.sync()
+    for e in range(E):
+        spec = WorldSpec(int(seeds[e]), W, H, D, origin=origin, terrain=terrain, base=base, amplitude=amp)
+        blocks, bl, sl, hm = oracle.generate(spec, *per[e], method="multi")
+        _assert_world(wb, e, blocks, bl, sl, hm, f"env{e}")
+    wb.close()
+
+
 def test_duplicates_outside_and_invalid_overrides(B, oracle):
     """Latest duplicate wins; overrides outside the region or with unknown ids are ignored."""
     cfg = B.WorldConfig(num_envs=2, width=40, height=64, depth=33, terrain=TERRAIN_FLAT, base=20)
@@ -270,7 +305,7 @@ def B_make(xyz, blk, env, kind):
     return B.make_overrides(xyz, blk, env=env, kind=kind)
 
 
-@pytest.mark.parametrize("W,H,D", [(64, 32, 64), (96, 128, 70)])
+@pytest.mark.parametrize("W,H,D", [(64, 32, 64), (96, 128, 70), (50, 256, 40)])
 def test_edit_sequences_relight_exactly(B, oracle, W, H, D):
     """Dig / place / torch add / remove-torch edits near the surface, several
     steps, World::setBlock semantics incl. torch support; relit light must equal
@@ -458,4 +493,40 @@ def test_full_size_incremental_steps_fixed_point(B):
     wb.sync()
     for e in range(E):
         assert _fixed_point_ok(wb.ids[e], wb.light[e], wb.height_map[e]), f"env {e}"
+    wb.close()
+
+
+def test_full_size_tall_worlds_fixed_point(B, oracle):
+    """Scale-out shaped worlds: 256 x 256 x 256 with terrain amplitude 120 and
+    2000 torches each (a slice of the env batch). Every env satisfies the light
+    fixed point, one env matches the oracle cell for cell, then a step of
+    edits keeps the fixed point."""
+    E = 8
+    cfg = B.WorldConfig(num_envs=E, width=256, height=256, depth=256, amplitude=120.0, max_overrides=E * 2000,
+                        max_edits=E * 5000)
+    wb = B.WorldBatch(cfg)
+    seeds = np.arange(100, 100 + E, dtype=np.uint32)
+    t = wb.place_torches(seeds, 2000)
+    wb.generate(seeds, t)
+    wb.sync()
+    for e in range(E):
+        assert _fixed_point_ok(wb.ids[e], wb.light[e], wb.height_map[e]), f"env {e}"
+    tn = t.cpu().numpy().view(B.OVERRIDE_DTYPE)
+    sel = tn[(tn["env"] == 3) & (tn["y"] > -(1 << 30))]
+    spec = WorldSpec(int(seeds[3]), 256, 256, 256, amplitude=120.0)
+    blocks, bl, sl, hm = oracle.generate(spec, _xyz(sel), sel["block"], method="multi")
+    _assert_world(wb, 3, blocks, bl, sl, hm, "env3")
+    rng = np.random.default_rng(4)
+    hmn = wb.height_map.cpu().numpy()
+    n = 5000 * E
+    env = np.repeat(np.arange(E), 5000)
+    x, z = rng.integers(0, 256, n), rng.integers(0, 256, n)
+    y = hmn[env, z, x] + rng.integers(-8, 9, n)
+    r = rng.random(n)
+    blk = np.where(r < 0.45, 0, np.where(r < 0.9, 3, 4)).astype(np.uint8)
+    kind = (r >= 0.95).astype(np.uint8)
+    wb.apply_edits(B.make_overrides(np.stack([x, y, z], 1), blk, env=env, kind=kind))
+    wb.sync()
+    for e in range(E):
+        assert _fixed_point_ok(wb.ids[e], wb.light[e], wb.height_map[e]), f"env {e} after edits"
     wb.close()
