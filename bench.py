@@ -38,8 +38,8 @@ BASE_SEED = 1
 # reference's torch density (1000 per 256 x 256 columns).
 SAMPLE_W, SAMPLE_H, SAMPLE_D, SAMPLE_TORCHES = 128, 128, 128, 250
 # Our kernel launches per step: place_torches, override count/scan(3)/scatter/sort,
-# tile kernel, conversion.
-LAUNCHES_PER_STEP = 9
+# terrain surface, tile kernel, conversion.
+LAUNCHES_PER_STEP = 10
 
 
 def parse_args():
@@ -117,6 +117,15 @@ class ClockSampler:
                 "samples": len(self.samples), "source": "nvml"}
 
 
+def workload_config(world: int) -> dict:
+    return {"workload": "world reset: generation + full sky/block light + RGBA8->NCHW conversion",
+            "envs_per_gpu": ENVS_PER_GPU, "world": [W, H, D], "torches_per_env": TORCHES,
+            "terrain": "fBm 40+round(50*fbm)", "frames": [ENVS_PER_GPU, 3, FRAME_H, FRAME_W],
+            "l2": f"outputs {2 * ENVS_PER_GPU * W * H * D / 1e9:.2f} GB per step per GPU rewritten every step "
+                  f"(> 126 MB L2)",
+            "parallelism": f"env shards x{world}"}
+
+
 # ------------------------------------------------------------ CPU samples --
 def cpu_sample(kind_pref: str = "reference"):
     """Times one bounded sample of the workload on the host cores.
@@ -166,8 +175,7 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": f"world reset sample {SAMPLE_W}x{SAMPLE_H}x{SAMPLE_D}, {SAMPLE_TORCHES} torches",
-                   "envs_per_gpu": ENVS_PER_GPU, "world": [W, H, D], "torches_per_env": TORCHES},
+        "config": workload_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -176,10 +184,14 @@ def run_reference(args) -> None:
 
 # ------------------------------------------------------------------- ours --
 def load_traffic():
-    path = os.path.join(ROOT, "profiles", "tile_kernel_traffic.json")
+    """DRAM read+write bytes of one benchmark launch of the tile kernel, from
+    the committed ncu summary (a 16-env capture scaled to the launch)."""
+    path = os.path.join(ROOT, "profiles", "tile_kernel_reset_16envs_256x128x256.md")
     if os.path.exists(path):
         with open(path) as f:
-            return json.load(f)
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch_scaled:"):
+                    return int(line.split(":", 1)[1])
     return None
 
 
@@ -299,16 +311,12 @@ def run_ours(args) -> None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": "world reset: generation + full sky/block light + RGBA8->NCHW conversion",
-                   "envs_per_gpu": ENVS_PER_GPU, "world": [W, H, D], "torches_per_env": TORCHES,
-                   "terrain": "fBm 40+round(50*fbm)", "frames": [ENVS_PER_GPU, 3, FRAME_H, FRAME_W],
-                   "l2": "outputs 2.15 GB per step per GPU rewritten every step (> 126 MB L2)",
-                   "parallelism": f"env shards x{world}"},
+        "config": workload_config(world),
         "env_resets_per_s": ENVS_PER_GPU * world * args.steps / (ms / 1e3),
         "roofline": {"bound": "hbm", "kernel": "tile_kernel", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "algorithmic_bytes_per_launch": algo_bytes, "kernel_ms": tile_ms,
-                     "traffic": None if traffic is None else traffic["dram_bytes_per_launch_scaled"]},
+                     "traffic": traffic if ENVS_PER_GPU == 128 else None},
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": seeds.numel() * 4 + frames.numel(),
                 "d2h_bytes_per_step": hm_host.numel() * 2},
