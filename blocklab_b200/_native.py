@@ -101,6 +101,8 @@ SIGNATURES = {
     "blk_place_torches": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _UP]),
     "blk_apply_edits": (ctypes.c_int, [_VP, _VP, _U32, _UP]),
     "blk_build_render_voxels": (ctypes.c_int, [_VP, _U32, _VP, _U32, _VP, _VP, _UP]),
+    "blk_build_render_voxels_static": (ctypes.c_int, [_VP, _VP, _U32, _U32, _U32, ctypes.c_int32, ctypes.c_int32,
+                                                      ctypes.c_int32, _VP, _U32, _VP, _VP, _UP]),
     "blk_effective_light": (ctypes.c_int, [_VP, _VP, _VP, _UP]),
     "blk_sky_light_at_time": (ctypes.c_uint8, [_U32]),
     "blk_readback": (ctypes.c_int, [_VP, _U32, _U32, _VP, _VP, _VP, _UP]),

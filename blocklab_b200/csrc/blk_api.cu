@@ -6,6 +6,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 namespace blk {
@@ -482,6 +483,53 @@ __global__ void voxel_write_kernel(VoxelArgs a, const uint32_t* row_offset, uint
                 voxels[3 * static_cast<uint64_t>(pos) + 2] = v[2];
             }
             ++pos;
+        }
+}
+
+// Render voxels without allocation: the per-row counts and offsets live in a
+// fixed device array. depth * height rows at most; the reference's packing
+// (z < 64, y < 512) never needs more.
+constexpr uint32_t kStaticVoxelRows = 64u * 512u;
+static __device__ __align__(256) uint32_t g_voxel_rows[2 * kStaticVoxelRows]; // counts | offsets
+
+// Exclusive scan of n <= 32768 row counts by one block of 1024 threads, each
+// owning a run of consecutive rows.
+__global__ void __launch_bounds__(1024) row_scan_one_block(const uint32_t* in, uint32_t* out, uint32_t n)
+{
+    __shared__ uint32_t warp_sums[32];
+    const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+    const uint32_t per = (n + 1023u) / 1024u;
+    const uint32_t b = t * per;
+    uint32_t sum = 0;
+    for (uint32_t i = 0; i < per; ++i)
+        if (b + i < n)
+            sum += in[b + i];
+    uint32_t v = sum; // inclusive scan over the warp
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t u = __shfl_up_sync(0xFFFFFFFFu, v, d);
+        if (lane >= static_cast<uint32_t>(d))
+            v += u;
+    }
+    if (lane == 31u)
+        warp_sums[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = warp_sums[lane];
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t u = __shfl_up_sync(0xFFFFFFFFu, w, d);
+            if (lane >= static_cast<uint32_t>(d))
+                w += u;
+        }
+        warp_sums[lane] = w;
+    }
+    __syncthreads();
+    uint32_t run = v - sum + (warp ? warp_sums[warp - 1] : 0u);
+    for (uint32_t i = 0; i < per; ++i)
+        if (b + i < n) {
+            out[b + i] = run;
+            run += in[b + i];
         }
 }
 
@@ -1060,6 +1108,60 @@ int blk_convert_rgba8_to_float_nchw(const void* rgba8, float* nchw, uint32_t bat
             static_cast<uint32_t>(ppi), total);
     }
     return cuda_fail(cudaGetLastError(), "rgba8 conversion launch");
+}
+
+int blk_build_render_voxels_static(const uint8_t* ids, const uint8_t* light, uint32_t width, uint32_t height,
+    uint32_t depth, int32_t origin_x, int32_t origin_y, int32_t origin_z, void* voxels, uint32_t max_voxels,
+    uint32_t* count, int32_t* header, uintptr_t stream_handle)
+{
+    if (!ids || !light || !count || !header || (max_voxels && !voxels) || width == 0 || height == 0 || depth == 0) {
+        set_error("blk_build_render_voxels_static: invalid argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (width > 64 || depth > 64 || height > 512
+        || static_cast<uint64_t>(depth) * height > static_cast<uint64_t>(kStaticVoxelRows)) {
+        set_error("blk_build_render_voxels_static: region exceeds the static scratch (width, depth <= 64, "
+                  "height <= 512, depth * height <= 32768 rows)");
+        return BLK_ERR_CAPACITY;
+    }
+    // Set-up, once per device, with that device current: the scratch array's
+    // device address. Later calls only read the cached pointer.
+    constexpr int kMaxDevices = 64;
+    static std::mutex setup_mutex;
+    static uint32_t* scratch_of[kMaxDevices] = {};
+    int dev = 0;
+    BLK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("blk_build_render_voxels_static: device ordinal out of range");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    uint32_t* scratch;
+    {
+        std::lock_guard<std::mutex> lock(setup_mutex);
+        if (!scratch_of[dev]) {
+            void* addr = nullptr;
+            BLK_CUDA(cudaGetSymbolAddress(&addr, g_voxel_rows), "cudaGetSymbolAddress (render voxel scratch)");
+            scratch_of[dev] = static_cast<uint32_t*>(addr);
+        }
+        scratch = scratch_of[dev];
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    VoxelArgs a;
+    a.ids = ids;
+    a.light = light;
+    a.W = static_cast<int32_t>(width);
+    a.H = static_cast<int32_t>(height);
+    a.D = static_cast<int32_t>(depth);
+    a.row_count = scratch; // every entry is written before it is read: nothing has to start at zero
+    uint32_t* row_offset = scratch + kStaticVoxelRows;
+    const uint32_t rows = depth * height;
+    voxel_count_kernel<<<(rows + 127) / 128, 128, 0, st>>>(a);
+    BLK_CUDA(cudaGetLastError(), "render voxel count launch");
+    row_scan_one_block<<<1, 1024, 0, st>>>(a.row_count, row_offset, rows);
+    BLK_CUDA(cudaGetLastError(), "render voxel scan launch");
+    voxel_write_kernel<<<(rows + 127) / 128, 128, 0, st>>>(a, row_offset, static_cast<uint32_t*>(voxels), max_voxels,
+        count, header, make_int3(origin_x, origin_y, origin_z));
+    return cuda_fail(cudaGetLastError(), "render voxel launch");
 }
 
 } // extern "C"

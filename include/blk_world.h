@@ -147,6 +147,24 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
 int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t max_voxels, uint32_t* count,
     int32_t* header, uintptr_t stream);
 
+/* No counterpart in the reference (an addition of this library). The render
+ * voxel list of blk_build_render_voxels for one world held in caller-owned
+ * device memory (ids and light of one env in this library's layout,
+ * [depth][width][height] with height fastest, e.g. a blk_views env slice),
+ * without allocating anything: the row scratch is a fixed device array of
+ * 2 x 32768 words inside the library. For callers that cannot allocate
+ * device memory at call time, e.g. a renderer recording its frame work.
+ * Limits: width, depth <= 64 and height <= 512 (the reference packing) and
+ * depth * height <= 32768 rows; larger regions return BLK_ERR_CAPACITY.
+ * The first call on a device does the set-up (looks up the scratch array's
+ * device address with that device current) and should come before any
+ * stream capture. Nothing has to start at zero. All calls on a device share
+ * the scratch: calls that overlap in time (other streams or host threads)
+ * race, so order them. `voxels`, `count` and `header` are device memory. */
+int blk_build_render_voxels_static(const uint8_t* ids, const uint8_t* light, uint32_t width, uint32_t height,
+    uint32_t depth, int32_t origin_x, int32_t origin_y, int32_t origin_z, void* voxels, uint32_t max_voxels,
+    uint32_t* count, int32_t* header, uintptr_t stream);
+
 /* Day/night effective light: out[i] = (sky - min(sky, dimming[env])) << 4 | block
  * for every cell, dimming = 15 - skyLightAtTime(t) as the reference renderer
  * applies it per face (src/graphics/Renderer.cpp:803, shaders/voxel.vert.hlsl:151).
