@@ -79,7 +79,11 @@ struct Smem {
     static constexpr int kBand = NW < 4 ? NW : 4;                     // max words of one flood band
     static constexpr int kPlane = kBand * kExtCols;                   // words per plane
     static constexpr int kPitch = 32 * NW + 16;                       // staging bytes per column
-    static constexpr int kStageWords = (kWarps / 2) * kTile * kPitch / 4; // half the warps at a time
+    // Output staging: every warp at once when its rows fit in 198 KB (with the
+    // column summaries the CTA stays within 227 KB), else half of the warps per round.
+    static constexpr int kStageWarps = kWarps * kTile * kPitch <= 198 * 1024 ? kWarps : kWarps / 2;
+    static constexpr int kRounds = kWarps / kStageWarps;
+    static constexpr int kStageWords = kStageWarps * kTile * kPitch / 4;
     static constexpr int kPoolWords = 3 * kPlane > kStageWords ? 3 * kPlane : kStageWords;
     // O | B0 | B1 during the floods; output staging otherwise.
     uint32_t pool[kPoolWords];
@@ -500,20 +504,21 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
     // ---- output staging helpers ----------------------------------------------
     // Each warp owns one z row of 32 columns, contiguous in memory. A lane
     // builds its column's bytes in the warp's staging area (the flood planes),
-    // then the warp stores the row with coalesced 16-byte stores. Half of the
-    // warps stage at a time. The helpers derive everything from tid, the tile
+    // then the warp stores the row with coalesced 16-byte stores. All warps
+    // stage at once up to H = 160, half of them per round above. The helpers
+    // derive everything from tid, the tile
     // origin and shared memory, so nothing of theirs stays live across a flood.
     constexpr int kPitch = Smem<NW>::kPitch;
     constexpr int kChunks = H / 16;
     constexpr int KB = Smem<NW>::kBand;
     auto stage_of = [&]() {
-        return reinterpret_cast<uint8_t*>(s.pool) + (warp & (kWarps / 2 - 1)) * (kTile * kPitch) + lane * kPitch;
+        return reinterpret_cast<uint8_t*>(s.pool) + (warp % Smem<NW>::kStageWarps) * (kTile * kPitch) + lane * kPitch;
     };
     auto row_offset = [&]() { return (static_cast<uint64_t>(z0 + warp) * a.W + x0) * H; };
 
     // Copies the staged 16-row chunks selected by `mask` (bit ch = rows 16ch..).
     auto copy_out = [&](uint8_t* dst, uint32_t mask) {
-        const uint8_t* stage = reinterpret_cast<const uint8_t*>(s.pool) + (warp & (kWarps / 2 - 1)) * (kTile * kPitch);
+        const uint8_t* stage = reinterpret_cast<const uint8_t*>(s.pool) + (warp % Smem<NW>::kStageWarps) * (kTile * kPitch);
         const int ncols = min(kTile, a.W - x0);
 #pragma unroll
         for (int i = 0; i < kChunks; ++i) {
@@ -553,9 +558,9 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
 
     // ---- block ids and height map (generation) -------------------------------
     if (a.mode == 0) {
-        for (int round = 0; round < 2; ++round) {
+        for (int round = 0; round < Smem<NW>::kRounds; ++round) {
             __syncthreads();
-            if ((warp >> 4) != round)
+            if (warp / Smem<NW>::kStageWarps != round)
                 continue;
             const int gx = x0 + lane, gz = z0 + warp;
             if (in_world(a, gx, gz)) {
@@ -751,9 +756,9 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
 
         // Stage and store the pass's light chunks. Band word j, half h holds
         // the 16-row chunk from row w_lo + 32j + 16h (w_lo is chunk aligned).
-        for (int round = 0; round < 2; ++round) {
+        for (int round = 0; round < Smem<NW>::kRounds; ++round) {
             __syncthreads();
-            if ((warp >> 4) != round)
+            if (warp / Smem<NW>::kStageWarps != round)
                 continue;
             Plan p;
             uint32_t mask = kAllChunks, band_chunks = 0u;
@@ -813,9 +818,9 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
 
     // Several windows: the chunks outside the output rows (generation only).
     if (a.mode == 0 && n_win > 1) {
-        for (int round = 0; round < 2; ++round) {
+        for (int round = 0; round < Smem<NW>::kRounds; ++round) {
             __syncthreads();
-            if ((warp >> 4) != round)
+            if (warp / Smem<NW>::kStageWarps != round)
                 continue;
             Plan p;
             plan_tile(p);
