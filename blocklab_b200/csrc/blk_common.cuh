@@ -69,25 +69,28 @@ __device__ inline float ref_terrain_height(uint32_t seed, int32_t x, int32_t z)
     return 9.0f + low + high + diagonal + rough;
 }
 
-// Lattice value of the fBm terrain: the reference's value noise, evaluated
+// Lattice value of the fBm terrain in [-1, 1]: the reference's hash finalizer
+// (src/utility/Hash.h:26-34) over hash_combine(octave seed, x, z), evaluated
 // with explicitly rounded single operations (no contraction) so the CPU
-// oracle reproduces it bit for bit.
+// oracle reproduces it bit for bit. Without the finalizer hash_combine of
+// small lattice coordinates changes only low bits and the terrain is flat.
 __device__ inline float fbm_lattice(uint32_t seed, int32_t x, int32_t z)
 {
-    const uint32_t h = hash_combine3(seed, static_cast<uint32_t>(x), static_cast<uint32_t>(z));
+    const uint32_t h = hash32(hash_combine3(seed, static_cast<uint32_t>(x), static_cast<uint32_t>(z)));
     const float q = __fdiv_rn(static_cast<float>(h & 0x00ffffffU), 16777215.0f);
     return __fsub_rn(__fmul_rn(q, 2.0f), 1.0f);
 }
 
 // 4-octave value-noise fBm in [-1, 1]: lattice spacing 64 >> o, lacunarity 2,
-// gain 0.5, smoothstep-weighted bilinear interpolation, normalised by 1.875.
+// gain 0.5, smoothstep-weighted bilinear interpolation, normalised by 1.875;
+// octave o uses the seed hash(hash_combine(seed, o)).
 __device__ inline float fbm(uint32_t seed, int32_t x, int32_t z)
 {
     float acc = 0.0f;
     float amp = 1.0f;
 #pragma unroll
     for (int o = 0; o < 4; ++o) {
-        const uint32_t s = hash_combine2(seed, static_cast<uint32_t>(o));
+        const uint32_t s = hash32(hash_combine2(seed, static_cast<uint32_t>(o)));
         const float scale = 1.0f / static_cast<float>(64 >> o);
         const float fx = __fmul_rn(static_cast<float>(x), scale);
         const float fz = __fmul_rn(static_cast<float>(z), scale);

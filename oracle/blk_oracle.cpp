@@ -54,16 +54,26 @@ float terrain_height_reference(uint32_t seed, int32_t x, int32_t z)
     return 9.0f + low + high + diagonal + rough;
 }
 
+// Lattice value of the fBm terrain in [-1, 1]: the reference's hash finalizer
+// (src/utility/Hash.h:26-34) over hash_combine(octave seed, x, z). Without the
+// finalizer hash_combine of small lattice coordinates changes only low bits
+// and the terrain comes out flat.
+float fbm_lattice(uint32_t seed, int32_t x, int32_t z)
+{
+    const uint32_t h = orc_hash(orc_hash_combine3(seed, static_cast<uint32_t>(x), static_cast<uint32_t>(z)));
+    return static_cast<float>(h & 0x00ffffffU) / static_cast<float>(0x00ffffffU) * 2.0f - 1.0f;
+}
+
 // fBm terrain of the benchmark worlds (this project's spec; the reference has
 // none). Four octaves of bilinear value noise with smoothstep weights on a
 // lattice of spacing 64 >> o, lacunarity 2, gain 0.5, normalised by 1.875.
-// Lattice values are the reference's value_noise on a per-octave seed.
+// Octave o uses the seed hash(hash_combine(seed, o)).
 float fbm(uint32_t seed, int32_t x, int32_t z)
 {
     float acc = 0.0f;
     float amp = 1.0f;
     for (int o = 0; o < 4; ++o) {
-        const uint32_t s = orc_hash_combine2(seed, static_cast<uint32_t>(o));
+        const uint32_t s = orc_hash(orc_hash_combine2(seed, static_cast<uint32_t>(o)));
         const float scale = 1.0f / static_cast<float>(64 >> o); // exact power of two
         const float fx = static_cast<float>(x) * scale;
         const float fz = static_cast<float>(z) * scale;
@@ -75,10 +85,10 @@ float fbm(uint32_t seed, int32_t x, int32_t z)
         const float tz = fz - flz;
         const float wx = (tx * tx) * (3.0f - 2.0f * tx);
         const float wz = (tz * tz) * (3.0f - 2.0f * tz);
-        const float v00 = value_noise(s, ix, iz);
-        const float v10 = value_noise(s, ix + 1, iz);
-        const float v01 = value_noise(s, ix, iz + 1);
-        const float v11 = value_noise(s, ix + 1, iz + 1);
+        const float v00 = fbm_lattice(s, ix, iz);
+        const float v10 = fbm_lattice(s, ix + 1, iz);
+        const float v01 = fbm_lattice(s, ix, iz + 1);
+        const float v11 = fbm_lattice(s, ix + 1, iz + 1);
         const float a = v00 + (v10 - v00) * wx;
         const float b = v01 + (v11 - v01) * wx;
         const float n = a + (b - a) * wz;
