@@ -49,8 +49,16 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--envs", type=int, default=ENVS_PER_GPU,
-                    help="envs per GPU (default 128; smaller batches are for profiler captures)")
+    ap.add_argument("--envs", type=int, default=None,
+                    help="envs per GPU (default: the workload's; smaller batches are for profiler captures)")
+    ap.add_argument("--workload", choices=["reset", "relight", "daynight", "scaleout"], default="reset",
+                    help="reset (default): 128 worlds 256x256x128 regenerated + lit + frames converted per step; "
+                         "relight: 1024 worlds 128^3, 10k edits per step + exact relight; daynight: 4096 worlds "
+                         "128x128x96, sky sweep + 84x84 frame conversion per step; scaleout: 1024 worlds 256^3 per "
+                         "GPU, 5000x1024/8192 edits per GPU per step + 90x160 frames, optional NCCL gather")
+    ap.add_argument("--gather", action="store_true", help="scaleout: gather observations to rank 0 every step")
+    ap.add_argument("--materialize", action="store_true",
+                    help="daynight: also materialise the effective light of every cell each step")
     return ap.parse_args()
 
 
@@ -208,7 +216,7 @@ def run_ours(args) -> None:
     import torch
 
     global ENVS_PER_GPU
-    ENVS_PER_GPU = args.envs
+    ENVS_PER_GPU = args.envs or ENVS_PER_GPU
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -336,9 +344,321 @@ def run_ours(args) -> None:
         pg.destroy_process_group()
 
 
+# --------------------------------------------------- secondary workloads --
+# The relight, day/night and scale-out configurations. Each prints its own
+# JSON line; the default invocation (reset) is the headline.
+RELIGHT = dict(envs=1024, W=128, H=128, D=128, torches=200, edits=10000)
+DAYNIGHT = dict(envs=4096, W=128, H=96, D=128, torches=300, frame=84, steps_per_sweep=256)
+SCALEOUT = dict(envs=1024, W=256, H=256, D=256, torches=2000, amplitude=120.0, edits_total=5000, envs_total=8192)
+
+
+def init_dist():
+    import datetime
+
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    return rank, world, local, dev, pg
+
+
+def time_steps(fn, steps, warmup, dev, pg, clock_gpu):
+    """Runs warmup untimed steps, then times `steps` calls of fn(k) with CUDA
+    events on the current stream between barriers; returns (ms, clocks)."""
+    import torch
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+
+    for k in range(warmup):
+        fn(k)
+    barrier()
+    clocks = ClockSampler(clock_gpu)
+    clocks.start()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(steps):
+        fn(warmup + k)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    info = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if pg is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, info
+
+
+def surface_edits(rng, hm, envs, n, W, D, torch_xyz):
+    """n edits over `envs` worlds: 45% dig, 45% place stone, 5% torch, 5%
+    remove an existing torch; cells uniform within 8 voxels of the surface."""
+    import numpy as np
+
+    import blocklab_b200 as B
+
+    env = rng.integers(0, envs, n)
+    x, z = rng.integers(0, W, n), rng.integers(0, D, n)
+    y = hm[env, z, x].astype(np.int64) + rng.integers(-8, 9, n)
+    r = rng.random(n)
+    blk = np.where(r < 0.45, B.AIR, np.where(r < 0.9, B.STONE, B.TORCH)).astype(np.uint8)
+    kind = np.zeros(n, np.uint8)
+    rm = r >= 0.95
+    if rm.any() and torch_xyz is not None:
+        pick = rng.integers(0, torch_xyz.shape[1], int(rm.sum()))
+        t = torch_xyz[env[rm], pick]
+        x[rm], y[rm], z[rm] = t[:, 0], t[:, 1], t[:, 2]
+        blk[rm] = B.AIR
+        kind[rm] = 1
+    return B.make_overrides(np.stack([x, y, z], 1), blk, env=env, kind=kind)
+
+
+def dirty_voxels(before, after, W, H, D):
+    """Voxels within L-inf distance 14 (clipped to the world) of a changed cell,
+    summed over envs: the cells whose light an exact relight must revisit."""
+    import numpy as np
+
+    changed = (before != after).nonzero().cpu().numpy()  # (env, z, x, y)
+    total = 0
+    for e in np.unique(changed[:, 0]):
+        m = np.zeros((D, W, H), bool)
+        for _, z, x, y in changed[changed[:, 0] == e]:
+            m[max(z - 14, 0):z + 15, max(x - 14, 0):x + 15, max(y - 14, 0):y + 15] = True
+        total += int(m.sum())
+    return total, len(changed)
+
+
+def run_workload(args) -> None:
+    import numpy as np
+    import torch
+
+    if args.impl == "reference":
+        run_workload_reference(args)
+        return
+    import blocklab_b200 as B
+
+    rank, world, local, dev, pg = init_dist()
+    peaks, peak_kind = measured_peaks()
+    line = {"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+    rng = np.random.default_rng(4242 + rank)
+
+    if args.workload == "relight":
+        c = dict(RELIGHT)
+        c["envs"] = args.envs or c["envs"]
+        E, Wd, Hd, Dd = c["envs"], c["W"], c["H"], c["D"]
+        n_edits = c["edits"] * E // RELIGHT["envs"]
+        cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, max_overrides=E * c["torches"],
+                            max_edits=n_edits)
+        wb = B.WorldBatch(cfg, device=local)
+        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+        torches = wb.place_torches(seeds, c["torches"])
+        wb.generate(seeds, torches)
+        wb.sync()
+        hm = wb.height_map.cpu().numpy()
+        tl = torches.cpu().numpy().view(B.OVERRIDE_DTYPE).reshape(E, c["torches"])
+        txyz = np.stack([tl["x"], tl["y"], tl["z"]], 2)
+        batches = [surface_edits(rng, hm, E, n_edits, Wd, Dd, txyz) for _ in range(args.warmup + args.steps)]
+        dev_batches = [torch.from_numpy(b.view(np.uint8).copy()).to(dev) for b in batches]
+        # Dirty volume of the first timed step, measured outside the timed region.
+        for k in range(args.warmup):
+            wb.apply_edits(dev_batches[k])
+        before = wb.ids.clone()
+        wb.apply_edits(dev_batches[args.warmup])
+        dirty, n_changed = dirty_voxels(before, wb.ids, Wd, Hd, Dd)
+        del before
+        # Timed run on a fresh copy of the same worlds and edit sequence.
+        wb.generate(seeds, torches)
+        wb.profile(True)
+        ms, clocks = time_steps(lambda k: wb.apply_edits(dev_batches[k]), args.steps, args.warmup, dev, pg, local)
+        prof = wb.profile_read()
+        wb.profile(False)
+        relight_ms = prof["relight_ms"] / max(prof["edit_calls"], 1)
+        pinned = [torch.from_numpy(b.view(np.uint8).copy()).pin_memory() for b in batches]
+        stage = torch.empty_like(dev_batches[0])
+        wb.generate(seeds, torches)
+
+        def e2e(k):
+            stage.copy_(pinned[k], non_blocking=True)
+            wb.apply_edits(stage)
+
+        e2e_ms, _ = time_steps(e2e, args.steps, args.warmup, dev, pg, local)
+        env_steps = E * world * args.steps
+        algo = 3 * dirty
+        line.update({
+            "metric": "env-steps/s (incremental relight)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
+            "ms_per_step": ms / args.steps, "dtype": "u8",
+            "config": {"workload": "relight: edits with World::setBlock semantics + exact incremental relight",
+                       "envs_per_gpu": E, "world": [Wd, Hd, Dd], "torches_per_env": c["torches"],
+                       "edits_per_step_per_gpu": n_edits, "mix": "45% dig, 45% stone, 5% torch, 5% remove torch",
+                       "l2": "edits touch scattered tiles of a 4.3 GB world; no flush needed (L2 126 MB)",
+                       "parallelism": f"env shards x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "tile_kernel (relight) + apply_edits",
+                         "achieved": algo / (relight_ms / 1e3) / 1e9 if relight_ms > 0 else None,
+                         "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": (algo / (relight_ms / 1e3) / 1e9) / peaks["hbm_gbs"] if relight_ms > 0 else None,
+                         "algorithmic_bytes_per_step": algo, "dirty_voxels_per_step": dirty,
+                         "changed_cells_per_step": n_changed, "relight_ms": relight_ms, "traffic": None},
+            "e2e": {"value": env_steps / (e2e_ms / 1e3), "unit": "env-steps/s",
+                    "h2d_bytes_per_step": int(dev_batches[0].numel()), "d2h_bytes_per_step": 0},
+            "gpu_launches": None, "clocks": clocks})
+        wb.close()
+    elif args.workload == "daynight":
+        c = dict(DAYNIGHT)
+        c["envs"] = args.envs or c["envs"]
+        E, Wd, Hd, Dd, F = c["envs"], c["W"], c["H"], c["D"], c["frame"]
+        cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, max_overrides=E * c["torches"])
+        wb = B.WorldBatch(cfg, device=local)
+        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+        wb.generate(seeds, wb.place_torches(seeds, c["torches"]))
+        gen = torch.Generator().manual_seed(99 + rank)
+        frames = torch.randint(0, 256, (E, F, F, 4), dtype=torch.uint8, generator=gen).to(dev)
+        obs = torch.empty((E, 3, F, F), dtype=torch.float32, device=dev)
+        eff = torch.empty_like(wb.light) if args.materialize else None
+        half = c["steps_per_sweep"] // 2
+        # Tick of sweep step k: across the sunset ramp, then the sunrise ramp.
+        ticks = [12000 + (13702 - 12000) * k // (half - 1) for k in range(half)] + \
+                [22300 + (23961 - 22300) * k // (half - 1) for k in range(half)]
+        dims = torch.tensor([[B.sky_light_dimming(t)] * E for t in ticks], dtype=torch.uint8).pin_memory()
+        dim_dev = torch.empty(E, dtype=torch.uint8, device=dev)
+
+        def step(k):
+            dim_dev.copy_(dims[k % len(ticks)], non_blocking=True)
+            B.convert_rgba8_to_float_nchw(frames, out=obs)
+            if eff is not None:
+                wb.effective_light(dim_dev, out=eff)
+
+        ms, clocks = time_steps(step, args.steps, args.warmup, dev, pg, local)
+        env_steps = E * world * args.steps
+        conv_bytes = 16 * E * F * F + (2 * wb.light.numel() if eff is not None else 0)
+        achieved = conv_bytes * args.steps / (ms / 1e3) / 1e9
+        line.update({
+            "metric": "env-steps/s (day/night sweep)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
+            "ms_per_step": ms / args.steps, "dtype": "u8 -> f32",
+            "config": {"workload": "daynight: sky level by tick (sunset then sunrise ramps), dimming upload, "
+                                   "RGBA8 84x84 -> float32 NCHW" + (", effective light of every cell"
+                                                                     if eff is not None else ""),
+                       "envs_per_gpu": E, "world": [Wd, Hd, Dd], "torches_per_env": c["torches"],
+                       "frames": [E, 3, F, F], "l2": f"{conv_bytes / 1e9:.2f} GB moved per step (> 126 MB L2)",
+                       "parallelism": f"env shards x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "rgba_to_nchw_vec_kernel" + (
+                " + effective_light_kernel" if eff is not None else ""), "achieved": achieved,
+                "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_step": conv_bytes, "traffic": None},
+            "gpu_launches": (2 if eff is not None else 1) * args.steps, "clocks": clocks})
+        wb.close()
+    else:  # scaleout
+        c = dict(SCALEOUT)
+        c["envs"] = args.envs or c["envs"]
+        E, Wd, Hd, Dd = c["envs"], c["W"], c["H"], c["D"]
+        n_edits = c["edits_total"] * E // c["envs_total"]
+        cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, amplitude=c["amplitude"],
+                            max_overrides=E * c["torches"], max_edits=max(n_edits, 1))
+        wb = B.WorldBatch(cfg, device=local)
+        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+        seeds_dev = torch.from_numpy(seeds.view(np.int32)).to(dev)
+        reset_torches = {}
+
+        def reset(k):
+            reset_torches["t"] = wb.place_torches(seeds_dev, c["torches"])
+            wb.generate(seeds_dev, reset_torches["t"])
+
+        reset_ms, reset_clocks = time_steps(reset, 1, 1, dev, pg, local)
+        hm = wb.height_map.cpu().numpy()
+        tl = reset_torches["t"].cpu().numpy().view(B.OVERRIDE_DTYPE).reshape(E, c["torches"])
+        txyz = np.stack([tl["x"], tl["y"], tl["z"]], 2)
+        batches = [torch.from_numpy(surface_edits(rng, hm, E, n_edits, Wd, Dd, txyz).view(np.uint8).copy()).to(dev)
+                   for _ in range(args.warmup + args.steps)]
+        gen = torch.Generator().manual_seed(7 + rank)
+        frames = torch.randint(0, 256, (E, FRAME_H, FRAME_W, 4), dtype=torch.uint8, generator=gen).to(dev)
+        obs = torch.empty((E, 3, FRAME_H, FRAME_W), dtype=torch.float32, device=dev)
+        gathered = None
+        if args.gather and pg is not None and rank == 0:
+            gathered = [torch.empty_like(obs) for _ in range(world)]
+
+        def step(k):
+            wb.apply_edits(batches[k])
+            B.convert_rgba8_to_float_nchw(frames, out=obs)
+            if args.gather and pg is not None:
+                pg.gather(obs, gathered if rank == 0 else None, dst=0)
+
+        ms, clocks = time_steps(step, args.steps, args.warmup, dev, pg, local)
+        env_steps = E * world * args.steps
+        line.update({
+            "metric": "env-steps/s (scale-out)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
+            "ms_per_step": ms / args.steps, "dtype": "u8",
+            "config": {"workload": "scaleout: per step edits + exact relight + 90x160 frame conversion"
+                                   + (" + NCCL gather of observations to rank 0" if args.gather else ""),
+                       "envs_per_gpu": E, "world": [Wd, Hd, Dd], "terrain": "fBm 40+round(120*fbm)",
+                       "torches_per_env": c["torches"], "edits_per_step_per_gpu": n_edits,
+                       "l2": "34 GB of world per GPU", "parallelism": f"env shards x{world}"},
+            "reset": {"ms": reset_ms, "voxels_per_s": E * world * Wd * Hd * Dd / (reset_ms / 1e3),
+                      "clocks": reset_clocks},
+            "gpu_launches": None, "clocks": clocks})
+        wb.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def run_workload_reference(args) -> None:
+    """The reference regenerates a region for every edit
+    (src/graphics/Renderer.cpp:1121-1141): one env-step of relight costs one
+    WorldGenerator::generate of the region, timed on the host cores."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    if args.workload != "relight":
+        print(json.dumps({"impl": "reference", "workload": args.workload,
+                          "unavailable": "the reference has no batched CPU path for this workload"}), flush=True)
+        return
+    import numpy as np
+
+    from oracle.oracle import TERRAIN_REFERENCE, Oracle, Reference, WorldSpec, ref_available
+
+    if not ref_available("cpu"):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_cpu.so not built"}), flush=True)
+        return
+    O, R = Oracle(), Reference("cpu")
+    c = RELIGHT
+    spec = WorldSpec(BASE_SEED, c["W"], c["H"], c["D"], terrain=TERRAIN_REFERENCE)
+    torches = O.place_torches(spec, c["torches"], 0x5EED)
+    times = []
+    for i in range(args.warmup + args.steps):
+        timing = []
+        R.generate(BASE_SEED, (0, 0, 0), (c["W"], c["H"], c["D"]), torches, np.full(len(torches), 4, np.uint8),
+                   runs=1, timing=timing)
+        if i >= args.warmup:
+            times.append(timing[-1] / 1e3)
+    value = len(times) / sum(times)
+    print(json.dumps({"impl": "reference", "metric": "env-steps/s (incremental relight)", "value": value,
+                      "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "higher_is_better": True,
+                      "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": os.cpu_count() or 1,
+                                       "kind": "reference",
+                                       "sample": f"one WorldGenerator::generate of a {c['W']}x{c['H']}x{c['D']} region "
+                                                 f"with {len(torches)} torches per env-step (reference terrain)"}}),
+          flush=True)
+
+
 def main() -> None:
     args = parse_args()
-    if args.impl == "reference":
+    if args.workload != "reset":
+        run_workload(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
