@@ -501,6 +501,17 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
             }
     };
 
+    // Plane B0 of the sky flood from an already built plane O: every open cell
+    // above its column's final top is a source (cells outside the region are
+    // not open in O).
+    auto sky_sources = [&](int blo, int nb) {
+        const uint32_t* O = s.O();
+        uint32_t* B0 = s.B(0);
+        for (int w = 0; w < nb; ++w)
+            for (int c = tid; c < kExtCols; c += kThreads)
+                B0[w * kExtCols + c] = O[w * kExtCols + c] & above_mask(blo + 32 * w, s.top_f[c]);
+    };
+
     // ---- output staging helpers ----------------------------------------------
     // Each warp owns one z row of 32 columns, contiguous in memory. A lane
     // builds its column's bytes in the warp's staging area (the flood planes),
@@ -698,9 +709,11 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
             plan_window(p, wi);
             const bool do_block = p.b_lo <= p.b_hi && p.b_lo <= p.r_hi && p.b_hi >= p.r_lo;
             const bool do_sky = p.s_lo <= p.s_hi && p.s_lo <= p.r_hi && p.s_hi >= p.r_lo;
+            bool open_ready = false; // plane O of this window is built (floods only read it)
             if (do_block) {
                 __syncthreads();
                 build(p.w_lo, p.nb, 0);
+                open_ready = true;
                 __syncthreads();
                 bool go = true;
                 if (a.mode == 1) {
@@ -718,7 +731,10 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, i
             if (do_sky) {
                 plan_window(p, wi);
                 __syncthreads();
-                build(p.w_lo, p.nb, 1);
+                if (open_ready)
+                    sky_sources(p.w_lo, p.nb);
+                else
+                    build(p.w_lo, p.nb, 1);
                 __syncthreads();
                 bool go = true;
                 if (a.mode == 1) {
