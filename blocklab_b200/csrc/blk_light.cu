@@ -211,6 +211,9 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
         cnt[w][2] = 0;
         cnt[w][3] = 0;
     }
+    // Fully unrolled: plane pointers, cone reach and counter updates are
+    // compile-time per step.
+#pragma unroll
     for (int step = 1; step <= kMaxDistance; ++step) {
         const uint32_t* cur = s.pool + (1 + ((step - 1) & 1)) * P;
         uint32_t* nxt = s.pool + (1 + (step & 1)) * P;
