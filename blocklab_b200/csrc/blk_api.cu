@@ -5,6 +5,7 @@
 #include "blk_internal.h"
 
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -294,14 +295,28 @@ struct EditArgs {
     int16_t* hmap;
     uint32_t* win_lo;  // per env tile, atomicMin
     uint32_t* win_hi;  // per env tile, atomicMax
+    uint4* boxes;      // one relight box per changed cell
+    uint32_t* box_count;
+    uint32_t box_capacity;
     RegionDims r;
     uint64_t env_stride;
     uint32_t tiles_x, tiles_z;
 };
 
+// Records the cells whose light a change at (x, z), rows ylo..yhi, can alter:
+// rows ylo - 14 .. yhi + 14 of the columns within 14 of (x, z). Two forms are
+// kept and the relight uses the smaller: per-tile row windows (every tile the
+// columns touch), and a 32 x 32-column box around the change (x0 = x - 15
+// clamped to the region holds x - 14 .. x + 14).
 __device__ void mark_dirty(const EditArgs& a, uint32_t env, int32_t x, int32_t z, int32_t ylo, int32_t yhi)
 {
     const int32_t lo = max(ylo - kMaxDistance, 0), hi = min(yhi + kMaxDistance, a.r.H - 1);
+    const uint32_t b = atomicAdd(a.box_count, 1u);
+    if (b < a.box_capacity) {
+        const int32_t bx = max(min(x - 15, a.r.W - 32), 0), bz = max(min(z - 15, a.r.D - 32), 0);
+        a.boxes[b] = make_uint4(env, static_cast<uint32_t>(bx) | (static_cast<uint32_t>(bz) << 16),
+            static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16), 0u);
+    }
     const int32_t tx0 = max(x - kMaxDistance, 0) / 32, tx1 = min(x + kMaxDistance, a.r.W - 1) / 32;
     const int32_t tz0 = max(z - kMaxDistance, 0) / 32, tz1 = min(z + kMaxDistance, a.r.D - 1) / 32;
     for (int32_t tz = tz0; tz <= tz1; ++tz)
@@ -705,6 +720,9 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->dirty_window, 2 * n_tiles, "dirty windows"));
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
+    ctx->box_capacity = 2 * std::max<uint32_t>(c.max_edits, 1);
+    A(dalloc(&ctx->boxes, ctx->box_capacity, "relight boxes"));
+    A(dalloc(&ctx->box_count, 1, "relight box count"));
     A(dalloc(&ctx->flags, 1, "flags"));
     {
         int sms = 148;
@@ -757,7 +775,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
             cudaEventDestroy(ev);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -901,10 +919,14 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     a.hmap = ctx->hmap;
     a.win_lo = win_lo;
     a.win_hi = win_hi;
+    a.boxes = ctx->boxes;
+    a.box_count = ctx->box_count;
+    a.box_capacity = ctx->box_capacity;
     a.r = region(ctx);
     a.env_stride = ctx->env_stride;
     a.tiles_x = ctx->tiles_x;
     a.tiles_z = ctx->tiles_z;
+    BLK_CUDA(cudaMemsetAsync(ctx->box_count, 0, sizeof(uint32_t), st), "memset box count");
     apply_edits_kernel<<<(envs + 127) / 128, 128, 0, st>>>(a);
     BLK_CUDA(cudaGetLastError(), "apply edits launch");
     prof_mark(ctx, mark, 1, st);

@@ -44,6 +44,9 @@ struct blk_ctx {
     uint32_t* dirty_window = nullptr;     // [num_envs * tiles] packed ylo | yhi<<16, 0xFFFFFFFF = clean
     uint32_t* dirty_list = nullptr;       // [num_envs * tiles] dirty tile ids
     uint32_t* dirty_count = nullptr;      // [1]
+    uint4* boxes = nullptr;               // [box_capacity] relight boxes: env, x0 | z0 << 16, ylo | yhi << 16
+    uint32_t* box_count = nullptr;        // [1]
+    uint32_t box_capacity = 0;            // 2 * max_edits (an edit changes at most two cells)
     uint32_t* h_dirty_count = nullptr;    // pinned [1]
 
     uint32_t* park = nullptr;             // tile-kernel scratch: 16 words x 1024 threads per CTA

@@ -63,6 +63,9 @@ struct TileArgs {
     const uint32_t* dirty_list;
     const uint32_t* dirty_window;
     const uint32_t* dirty_count;
+    const uint4* boxes;             // relight boxes (see mark_dirty) and their count
+    const uint32_t* box_count;
+    uint32_t box_capacity;
     uint32_t* flags;
     uint32_t* park;                 // per-CTA scratch for block planes during a sky flood
     uint32_t n_tiles;
@@ -71,7 +74,7 @@ struct TileArgs {
     int32_t tiles_x, tiles_z;
     uint64_t env_stride;
     uint64_t columns;
-    int32_t mode; // 0 = generate, 1 = relight dirty tiles from the resident ids
+    int32_t mode; // 0 = generate, 1 = relight dirty tiles or boxes from the resident ids
 };
 
 template <int NW>
@@ -284,16 +287,12 @@ __device__ void flood_any(int nb, Smem<NW>& s, const int (&slot)[kSlots], uint32
 }
 
 template <int NW>
-__device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t tile_id, int32_t wlo_rows, int32_t whi_rows)
+__device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x0, int z0, int32_t wlo_rows,
+    int32_t whi_rows)
 {
     constexpr int H = 32 * NW;
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
-    const uint32_t tiles_per_env = static_cast<uint32_t>(a.tiles_x * a.tiles_z);
-    const uint32_t env = tile_id / tiles_per_env;
-    const uint32_t t_in_env = tile_id % tiles_per_env;
-    const int x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
-    const int z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
     const uint64_t env_col0 = static_cast<uint64_t>(env) * a.columns;
     uint8_t* env_ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
 
@@ -866,17 +865,41 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem<NW>& s = *reinterpret_cast<Smem<NW>*>(smem_raw);
-    const uint32_t n = a.mode == 0 ? a.n_tiles : *a.dirty_count;
+    // Relight works on boxes when there are no more of them than dirty tiles
+    // (sparse edits), else on the dirty tiles. Every CTA reads the same counts.
+    uint32_t n = a.n_tiles;
+    bool boxes = false;
+    if (a.mode != 0) {
+        const uint32_t nb = *a.box_count, nt = *a.dirty_count;
+        boxes = nb <= a.box_capacity && nb <= nt;
+        n = boxes ? nb : nt;
+    }
+    const uint32_t tiles_per_env = static_cast<uint32_t>(a.tiles_x * a.tiles_z);
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
-        uint32_t tile_id = i;
+        uint32_t env;
+        int x0, z0;
         int32_t wlo_rows = 0, whi_rows = 32 * NW - 1;
+        uint32_t win = 0;
+        if (boxes) {
+            const uint4 b = a.boxes[i];
+            env = b.x;
+            x0 = static_cast<int>(b.y & 0xFFFFu);
+            z0 = static_cast<int>(b.y >> 16);
+            win = b.z;
+        } else {
+            const uint32_t tile_id = a.mode == 0 ? i : a.dirty_list[i];
+            env = tile_id / tiles_per_env;
+            const uint32_t t_in_env = tile_id % tiles_per_env;
+            x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
+            z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
+            if (a.mode != 0)
+                win = a.dirty_window[tile_id];
+        }
         if (a.mode != 0) {
-            tile_id = a.dirty_list[i];
-            const uint32_t win = a.dirty_window[tile_id];
             wlo_rows = static_cast<int32_t>(win & 0xFFFFu) & ~15;
             whi_rows = min(static_cast<int32_t>(win >> 16) | 15, 32 * NW - 1);
         }
-        process_tile<NW>(a, s, tile_id, wlo_rows, whi_rows);
+        process_tile<NW>(a, s, env, x0, z0, wlo_rows, whi_rows);
         __syncthreads();
     }
 }
@@ -998,6 +1021,9 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream)
     a.dirty_list = ctx->dirty_list;
     a.dirty_window = ctx->dirty_window;
     a.dirty_count = ctx->dirty_count;
+    a.boxes = ctx->boxes;
+    a.box_count = ctx->box_count;
+    a.box_capacity = ctx->box_capacity;
     a.flags = ctx->flags;
     a.park = ctx->park;
     a.n_tiles = n_tiles;

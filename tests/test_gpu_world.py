@@ -337,6 +337,56 @@ def test_edit_sequences_relight_exactly(B, oracle, W, H, D):
     wb.close()
 
 
+@pytest.mark.parametrize("W,H,D,per_env", [(128, 64, 96, 2), (45, 96, 70, 1), (200, 128, 33, 3)])
+def test_sparse_edits_relight_exactly(B, oracle, W, H, D, per_env):
+    """A few edits per env (each relit through a box around the change rather
+    than whole dirty tiles), including changes at region borders and torch
+    support removal; several steps, compared with a full relight."""
+    E = 4
+    origin = (7, -3, -11)
+    cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, origin=origin, terrain=TERRAIN_FBM, base=H // 3,
+                        amplitude=H / 5)
+    wb = B.WorldBatch(cfg)
+    rng = np.random.default_rng(W * H + per_env)
+    seeds = rng.integers(1, 1 << 31, E).astype(np.uint32)
+    specs = [WorldSpec(int(s), W, H, D, origin=origin, terrain=TERRAIN_FBM, base=H // 3, amplitude=H / 5)
+             for s in seeds]
+    torches = [oracle.place_torches(sp, 30, B.torch_key(int(s))) for sp, s in zip(specs, seeds)]
+    wb.generate(seeds, np.concatenate([B.make_overrides(t, B.TORCH, env=e) for e, t in enumerate(torches)]))
+    state = []
+    for e in range(E):
+        blocks, hm = oracle.build_blocks(specs[e], torches[e], np.full(len(torches[e]), 4, np.uint8))
+        state.append([blocks, hm])
+    for step in range(5):
+        lists, local = [], []
+        for e in range(E):
+            n = per_env
+            x = rng.integers(0, W, n)
+            z = rng.integers(0, D, n)
+            if step == 1:  # region borders and corners
+                x[0], z[0] = [(0, 0), (W - 1, D - 1), (0, D - 1), (W - 1, 0)][e % 4]
+            hm_l = state[e][1] - origin[1]
+            y = np.clip(hm_l[z, x] + rng.integers(-3, 4, n), 0, H - 1)
+            if step == 3:  # dig a torch's support
+                t = torches[e][e % len(torches[e])] - np.array(origin)
+                x[0], y[0], z[0] = t[0], t[1] - 1, t[2]
+            blk = rng.choice([0, 3, 4], n, p=[0.5, 0.35, 0.15]).astype(np.uint8)
+            if step == 3:
+                blk[0] = 0
+            kind = np.zeros(n, np.uint8)
+            xyz = np.stack([x, y, z], 1)
+            local.append((xyz, kind, blk))
+            lists.append(B.make_overrides(xyz + np.array(origin), blk, env=e, kind=kind))
+        wb.apply_edits(np.concatenate(lists))
+        wb.sync()
+        for e in range(E):
+            xyz, kind, blk = local[e]
+            oracle.apply_edits(state[e][0], state[e][1], xyz, kind, blk, origin_y=origin[1])
+            bl, sl = oracle.light(state[e][0], state[e][1], origin[1], "multi")
+            _assert_world(wb, e, state[e][0], bl, sl, state[e][1], f"step{step} env{e}")
+    wb.close()
+
+
 def test_edits_support_removal_and_heightmap(B, oracle):
     """Digging the block under a torch removes the torch; digging the top block
     lowers the height map (cells below become lit); placing above raises it."""
