@@ -79,7 +79,9 @@ struct TileArgs {
 
 template <int NW>
 struct Smem {
-    static constexpr int kBand = NW < 4 ? NW : 4;                     // max words of one flood band
+    // Max words of one flood band: 3 keeps the flood's registers unspilled;
+    // taller bands are lit in windows.
+    static constexpr int kBand = NW < 3 ? NW : 3;
     static constexpr int kPlane = kBand * kExtCols;                   // words per plane
     static constexpr int kPitch = 32 * NW + 16;                       // staging bytes per column
     // Output staging: every warp at once when its rows fit in 198 KB (with the
@@ -524,6 +526,9 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     constexpr int kPitch = Smem<NW>::kPitch;
     constexpr int kChunks = H / 16;
     constexpr int KB = Smem<NW>::kBand;
+    // Output rows of one window when a tile needs several: with margins of 16
+    // rows below and 14 above they fill KB words.
+    constexpr int kWinRows = ((32 * KB - 30) / 16) * 16;
     auto stage_of = [&]() {
         return reinterpret_cast<uint8_t*>(s.pool) + (warp % Smem<NW>::kStageWarps) * (kTile * kPitch) + lane * kPitch;
     };
@@ -629,7 +634,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     // dirty window). They are lit in windows of at most KB words: a window's
     // flood covers its output rows +-14 so that every path of length <= 14
     // that ends in them stays inside. Mode 0 bands already carry that margin:
-    // one window of the output rows when they fit. Otherwise windows of 96
+    // one window of the output rows when they fit. Otherwise windows of kWinRows
     // output rows with a margin of 16 rows below (every window starts on a
     // 16-row chunk, so its band words split into whole chunks) and 14 above.
     // The plan reads shared memory only, so it is recomputed after each flood
@@ -671,7 +676,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         p.whole = o_lo <= o_hi
             && ((a.mode == 0 && o_hi - o_lo + 1 <= 32 * KB)
                 || (min(o_hi + kMaxDistance, H - 1) - max(o_lo - 16, 0) + 1 <= 32 * KB));
-        p.n_win = o_lo > o_hi ? 0 : (p.whole ? 1 : (o_hi - o_lo + 96) / 96);
+        p.n_win = o_lo > o_hi ? 0 : (p.whole ? 1 : (o_hi - o_lo + kWinRows) / kWinRows);
         p.o_chunks = o_lo > o_hi ? 0u : (((2u << (o_hi >> 4)) - 1u) & ~((1u << (o_lo >> 4)) - 1u));
         p.r_lo = o_lo;
         p.r_hi = o_hi;
@@ -684,8 +689,8 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
             p.w_lo = a.mode == 0 ? o_lo : max(o_lo - 16, 0);
             w_hi = a.mode == 0 ? o_hi : min(o_hi + kMaxDistance, H - 1);
         } else {
-            p.r_lo = o_lo + 96 * wi;
-            p.r_hi = min(p.r_lo + 95, o_hi);
+            p.r_lo = o_lo + kWinRows * wi;
+            p.r_hi = min(p.r_lo + kWinRows - 1, o_hi);
             p.w_lo = max(p.r_lo - 16, 0);
             w_hi = min(p.r_hi + kMaxDistance, H - 1);
         }
