@@ -204,11 +204,16 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
 #pragma unroll
         for (int w = 0; w < NB; ++w)
             own[k][w] = slot[k] >= 0 ? s.B(0)[w * kExtCols + (slot[k] & 0xFFFF)] : 0u;
-    // The interior column is updated at every step: its open mask stays in registers.
-    uint32_t open0[NB];
+    // Open masks of the slot columns stay in registers for the whole flood.
+    uint32_t open0[NB], openh[kSlots][NB];
 #pragma unroll
     for (int w = 0; w < NB; ++w)
         open0[w] = O[w * kExtCols + (slot[0] & 0xFFFF)];
+#pragma unroll
+    for (int k = 1; k < kSlots; ++k)
+#pragma unroll
+        for (int w = 0; w < NB; ++w)
+            openh[k][w] = slot[k] >= 0 ? O[w * kExtCols + (slot[k] & 0xFFFF)] : 0u;
 #pragma unroll
     for (int w = 0; w < KB; ++w) {
         cnt[w][0] = w < NB ? own[0][w < NB ? w : 0] : 0u;
@@ -241,7 +246,7 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
                 const uint32_t up = __funnelshift_l(below, own[k][w], 1); // cell y takes y-1
                 const uint32_t dn = __funnelshift_r(own[k][w], above, 1); // cell y takes y+1
                 const uint32_t n = up | dn | Bw[-1] | Bw[1] | Bw[-kExt] | Bw[kExt];
-                v[w] = own[k][w] | ((k == 0 ? open0[w] : O[w * kExtCols + c]) & n);
+                v[w] = own[k][w] | ((k == 0 ? open0[w] : openh[k][w]) & n);
             }
 #pragma unroll
             for (int w = 0; w < NB; ++w) {
