@@ -81,6 +81,31 @@ __device__ inline float fbm_lattice(uint32_t seed, int32_t x, int32_t z)
     return __fsub_rn(__fmul_rn(q, 2.0f), 1.0f);
 }
 
+// Cell of octave o (lattice spacing 64 >> o) holding world coordinate v: the
+// lattice index and the smoothstep weight of v inside the cell.
+__device__ inline void fbm_cell(int o, int32_t v, int32_t& i, float& w)
+{
+    const float scale = 1.0f / static_cast<float>(64 >> o); // exact power of two
+    const float f = __fmul_rn(static_cast<float>(v), scale);
+    const float fl = floorf(f);
+    i = static_cast<int32_t>(fl);
+    const float t = __fsub_rn(f, fl);
+    w = __fmul_rn(__fmul_rn(t, t), __fsub_rn(3.0f, __fmul_rn(2.0f, t)));
+}
+
+// Bilinear mix of one octave's four corner values.
+__device__ inline float fbm_mix(float v00, float v10, float v01, float v11, float wx, float wz)
+{
+    const float a = __fadd_rn(v00, __fmul_rn(__fsub_rn(v10, v00), wx));
+    const float b = __fadd_rn(v01, __fmul_rn(__fsub_rn(v11, v01), wx));
+    return __fadd_rn(a, __fmul_rn(__fsub_rn(b, a), wz));
+}
+
+__device__ inline uint32_t fbm_octave_seed(uint32_t seed, int o)
+{
+    return hash32(hash_combine2(seed, static_cast<uint32_t>(o)));
+}
+
 // 4-octave value-noise fBm in [-1, 1]: lattice spacing 64 >> o, lacunarity 2,
 // gain 0.5, smoothstep-weighted bilinear interpolation, normalised by 1.875;
 // octave o uses the seed hash(hash_combine(seed, o)).
@@ -90,25 +115,13 @@ __device__ inline float fbm(uint32_t seed, int32_t x, int32_t z)
     float amp = 1.0f;
 #pragma unroll
     for (int o = 0; o < 4; ++o) {
-        const uint32_t s = hash32(hash_combine2(seed, static_cast<uint32_t>(o)));
-        const float scale = 1.0f / static_cast<float>(64 >> o);
-        const float fx = __fmul_rn(static_cast<float>(x), scale);
-        const float fz = __fmul_rn(static_cast<float>(z), scale);
-        const float flx = floorf(fx);
-        const float flz = floorf(fz);
-        const int32_t ix = static_cast<int32_t>(flx);
-        const int32_t iz = static_cast<int32_t>(flz);
-        const float tx = __fsub_rn(fx, flx);
-        const float tz = __fsub_rn(fz, flz);
-        const float wx = __fmul_rn(__fmul_rn(tx, tx), __fsub_rn(3.0f, __fmul_rn(2.0f, tx)));
-        const float wz = __fmul_rn(__fmul_rn(tz, tz), __fsub_rn(3.0f, __fmul_rn(2.0f, tz)));
-        const float v00 = fbm_lattice(s, ix, iz);
-        const float v10 = fbm_lattice(s, ix + 1, iz);
-        const float v01 = fbm_lattice(s, ix, iz + 1);
-        const float v11 = fbm_lattice(s, ix + 1, iz + 1);
-        const float a = __fadd_rn(v00, __fmul_rn(__fsub_rn(v10, v00), wx));
-        const float b = __fadd_rn(v01, __fmul_rn(__fsub_rn(v11, v01), wx));
-        const float n = __fadd_rn(a, __fmul_rn(__fsub_rn(b, a), wz));
+        const uint32_t s = fbm_octave_seed(seed, o);
+        int32_t ix, iz;
+        float wx, wz;
+        fbm_cell(o, x, ix, wx);
+        fbm_cell(o, z, iz, wz);
+        const float n = fbm_mix(fbm_lattice(s, ix, iz), fbm_lattice(s, ix + 1, iz), fbm_lattice(s, ix, iz + 1),
+            fbm_lattice(s, ix + 1, iz + 1), wx, wz);
         acc = __fadd_rn(acc, __fmul_rn(amp, n));
         amp = __fmul_rn(amp, 0.5f);
     }

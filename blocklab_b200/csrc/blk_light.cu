@@ -931,6 +931,69 @@ __global__ void terrain_kernel(const uint32_t* seeds, TerrainParams t, int32_t W
     }
 }
 
+// fBm surfaces, one CTA per 64 x 64 columns of one env at a time: each
+// octave's lattice values over the block (at most 10 x 10: a 64-column span
+// meets at most 64 / 8 + 1 cells) are hashed once into shared memory instead
+// of four times per column; the per-column arithmetic is fbm()'s.
+constexpr int kFbmBlock = 64;
+__global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds, TerrainParams t, int32_t W,
+    int32_t D, uint32_t num_envs, int16_t* out)
+{
+    __shared__ float lat[4][100];
+    __shared__ int32_t lat_ix[4], lat_iz[4], lat_nx[4], lat_nz[4];
+    const int bx = blockIdx.x * kFbmBlock, bz = blockIdx.y * kFbmBlock;
+    const int ex = min(bx + kFbmBlock - 1, W - 1), ez = min(bz + kFbmBlock - 1, D - 1);
+    if (threadIdx.x < 4) {
+        const int o = threadIdx.x;
+        int32_t i0, i1, k0, k1;
+        float w;
+        fbm_cell(o, t.origin_x + bx, i0, w);
+        fbm_cell(o, t.origin_x + ex, i1, w);
+        fbm_cell(o, t.origin_z + bz, k0, w);
+        fbm_cell(o, t.origin_z + ez, k1, w);
+        lat_ix[o] = i0;
+        lat_iz[o] = k0;
+        lat_nx[o] = i1 - i0 + 2; // corners ix .. ix + 1 of every cell met
+        lat_nz[o] = k1 - k0 + 2;
+    }
+    for (uint32_t env = blockIdx.z; env < num_envs; env += gridDim.z) {
+        const uint32_t seed = seeds[env];
+        __syncthreads();
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+            const uint32_t so = fbm_octave_seed(seed, o);
+            const int nx = lat_nx[o], nz = lat_nz[o];
+            for (int k = threadIdx.x; k < nx * nz; k += blockDim.x)
+                lat[o][k] = fbm_lattice(so, lat_ix[o] + k % nx, lat_iz[o] + k / nx);
+        }
+        __syncthreads();
+        const uint64_t env_col0 = static_cast<uint64_t>(env) * W * D;
+        for (int k = threadIdx.x; k < kFbmBlock * kFbmBlock; k += blockDim.x) {
+            const int x = bx + (k % kFbmBlock), z = bz + (k / kFbmBlock);
+            if (x >= W || z >= D)
+                continue;
+            float acc = 0.0f;
+            float amp = 1.0f;
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                int32_t ix, iz;
+                float wx, wz;
+                fbm_cell(o, t.origin_x + x, ix, wx);
+                fbm_cell(o, t.origin_z + z, iz, wz);
+                const int nx = lat_nx[o];
+                const float* L = lat[o] + (iz - lat_iz[o]) * nx + (ix - lat_ix[o]);
+                const float n = fbm_mix(L[0], L[1], L[nx], L[nx + 1], wx, wz);
+                acc = __fadd_rn(acc, __fmul_rn(amp, n));
+                amp = __fmul_rn(amp, 0.5f);
+            }
+            const float f = __fdiv_rn(acc, 1.875f);
+            int32_t top = t.base + static_cast<int32_t>(roundf(__fmul_rn(t.amplitude, f))) - t.origin_y;
+            top = top < -1 ? -1 : (top > t.height + 4 ? t.height + 4 : top);
+            out[env_col0 + static_cast<uint64_t>(z) * W + x] = static_cast<int16_t>(top);
+        }
+    }
+}
+
 template <int NW>
 int launch_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
 {
@@ -1009,6 +1072,14 @@ int halo_order_size() { return kHaloCols; }
 
 int launch_terrain(blk_ctx* ctx, cudaStream_t stream)
 {
+    if (ctx->cfg.terrain_mode == BLK_TERRAIN_FBM) {
+        const dim3 grid((ctx->cfg.width + kFbmBlock - 1) / kFbmBlock, (ctx->cfg.depth + kFbmBlock - 1) / kFbmBlock,
+            std::min<uint32_t>(ctx->cfg.num_envs, 65535));
+        terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
+            static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), ctx->cfg.num_envs,
+            ctx->terrain_top);
+        return cuda_fail(cudaGetLastError(), "terrain_fbm_kernel launch");
+    }
     const uint64_t total = static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->columns_per_env;
     uint64_t blocks = (total + 255) / 256;
     if (blocks > 148ull * 32)
