@@ -110,6 +110,9 @@ SIGNATURES = {
     "blk_profile_enable": (ctypes.c_int, [_VP, ctypes.c_int]),
     "blk_profile_read": (ctypes.c_int, [_VP, ctypes.POINTER(ProfileC), ctypes.c_int]),
     "blk_convert_rgba8_to_float_nchw": (ctypes.c_int, [_VP, _VP, _U32, _U32, _U32, _UP]),
+    "blk_query_cells": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _VP, _UP]),
+    "blk_query_solid": (ctypes.c_int, [_VP, _VP, _U32, _VP, _UP]),
+    "blk_snapshot_overrides": (ctypes.c_int, [_VP, _U32, _VP, _U32, _VP, _UP]),
 }
 
 

@@ -548,6 +548,114 @@ __global__ void __launch_bounds__(1024) row_scan_one_block(const uint32_t* in, u
         }
 }
 
+// ---------------------------------------------------------- sparse queries --
+__global__ void query_cells_kernel(const blk_cell_query* q, uint32_t n, const uint8_t* ids, const uint8_t* light,
+    const int16_t* hmap, RegionDims r, uint64_t env_stride, uint8_t* out_block, uint8_t* out_light,
+    int32_t* out_height)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const blk_cell_query c = q[i];
+        const int32_t x = c.x - r.ox, y = c.y - r.oy, z = c.z - r.oz;
+        const bool column = c.env < r.num_envs && x >= 0 && x < r.W && z >= 0 && z < r.D;
+        const bool inside = column && y >= 0 && y < r.H;
+        const uint64_t col = static_cast<uint64_t>(z) * r.W + x;
+        uint8_t b = 255, l = 0;
+        if (inside) {
+            const uint64_t idx = static_cast<uint64_t>(c.env) * env_stride + col * r.H + y;
+            b = ids[idx];
+            l = light[idx];
+        }
+        if (out_block)
+            out_block[i] = b;
+        if (out_light)
+            out_light[i] = l;
+        if (out_height)
+            out_height[i] = column ? static_cast<int32_t>(hmap[static_cast<uint64_t>(c.env) * r.W * r.D + col])
+                                   : INT32_MIN;
+    }
+}
+
+// One warp per box; the warp stops at the first solid cell it meets.
+__global__ void query_solid_kernel(const blk_box_query* q, uint32_t n, const uint8_t* ids, RegionDims r,
+    uint64_t env_stride, uint8_t* out)
+{
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t warps = gridDim.x * (blockDim.x / 32);
+    for (uint32_t i = (blockIdx.x * blockDim.x + threadIdx.x) / 32; i < n; i += warps) {
+        const blk_box_query b = q[i];
+        const int32_t x0 = max(b.min_x - r.ox, 0), x1 = min(b.max_x - r.ox, r.W - 1);
+        const int32_t y0 = max(b.min_y - r.oy, 0), y1 = min(b.max_y - r.oy, r.H - 1);
+        const int32_t z0 = max(b.min_z - r.oz, 0), z1 = min(b.max_z - r.oz, r.D - 1);
+        bool found = false;
+        if (b.env < r.num_envs && x0 <= x1 && y0 <= y1 && z0 <= z1) {
+            const uint64_t ny = y1 - y0 + 1, nx = x1 - x0 + 1;
+            const uint64_t total = ny * nx * static_cast<uint64_t>(z1 - z0 + 1);
+            const uint8_t* env_ids = ids + static_cast<uint64_t>(b.env) * env_stride;
+            for (uint64_t base = 0; base < total; base += 32) {
+                const uint64_t k = base + lane;
+                bool solid = false;
+                if (k < total) {
+                    const int32_t y = y0 + static_cast<int32_t>(k % ny);
+                    const int32_t x = x0 + static_cast<int32_t>((k / ny) % nx);
+                    const int32_t z = z0 + static_cast<int32_t>(k / (ny * nx));
+                    solid = is_opaque(env_ids[(static_cast<uint64_t>(z) * r.W + x) * r.H + y]);
+                }
+                if (__any_sync(0xFFFFFFFFu, solid)) {
+                    found = true;
+                    break;
+                }
+            }
+        }
+        if (lane == 0)
+            out[i] = found ? 1 : 0;
+    }
+}
+
+// ------------------------------------------------------------- snapshots --
+// Cells of one env whose block differs from its terrain (layer rule of the
+// column's surface): count per column, then write in (z, x, y) order.
+__global__ void snapshot_count_kernel(const uint8_t* ids, const int16_t* terrain_top, RegionDims r, uint32_t* count)
+{
+    const uint64_t columns = static_cast<uint64_t>(r.W) * r.D;
+    for (uint64_t col = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; col < columns;
+         col += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const int32_t top = terrain_top[col];
+        uint32_t n = 0;
+        for (int32_t y = 0; y < r.H; ++y)
+            n += ids[col * r.H + y] != layer_block(y, top) ? 1u : 0u;
+        count[col] = n;
+    }
+}
+
+__global__ void snapshot_write_kernel(const uint8_t* ids, const int16_t* terrain_top, RegionDims r, uint32_t env,
+    const uint32_t* count, const uint32_t* offset, blk_override* out, uint32_t capacity, uint32_t* total)
+{
+    const uint64_t columns = static_cast<uint64_t>(r.W) * r.D;
+    for (uint64_t col = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; col < columns;
+         col += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        if (col == columns - 1)
+            *total = offset[col] + count[col];
+        uint32_t pos = offset[col];
+        if (count[col] == 0 || pos >= capacity)
+            continue;
+        const int32_t top = terrain_top[col];
+        const int32_t x = static_cast<int32_t>(col % r.W), z = static_cast<int32_t>(col / r.W);
+        for (int32_t y = 0; y < r.H && pos < capacity; ++y) {
+            const uint8_t b = ids[col * r.H + y];
+            if (b == layer_block(y, top))
+                continue;
+            blk_override o;
+            o.x = x + r.ox;
+            o.y = y + r.oy;
+            o.z = z + r.oz;
+            o.env = static_cast<uint16_t>(env);
+            o.block = b;
+            o.kind = 0;
+            out[pos++] = o;
+        }
+    }
+}
+
 // ------------------------------------------------------- effective light --
 __global__ void effective_light_kernel(const uint4* light, uint4* out, const uint8_t* dimming, uint64_t quads_per_env,
     uint64_t total)
@@ -610,6 +718,16 @@ int cuda_fail(cudaError_t e, const char* what)
         return BLK_OK;
     set_error(std::string(what) + ": " + cudaGetErrorString(e));
     return BLK_ERR_CUDA;
+}
+
+bool device_memory(const void* p)
+{
+    cudaPointerAttributes attr {};
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
 }
 
 int stage_input(const void* src, size_t bytes, void* staging, cudaStream_t stream, const void** out)
@@ -1026,6 +1144,82 @@ int blk_readback(blk_ctx* ctx, uint32_t env_begin, uint32_t n_envs, uint8_t* ids
                      ctx->columns_per_env * n_envs * sizeof(int16_t), cudaMemcpyDefault, st),
             "readback height map");
     return BLK_OK;
+}
+
+int blk_query_cells(blk_ctx* ctx, const blk_cell_query* queries, uint32_t n, uint8_t* out_block, uint8_t* out_light,
+    int32_t* out_height, uintptr_t stream_handle)
+{
+    if (!ctx || (n && !queries)) {
+        set_error("blk_query_cells: invalid argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!ctx->generated) {
+        set_error("blk_query_cells: call blk_generate first");
+        return BLK_ERR_NOT_READY;
+    }
+    if (n == 0)
+        return BLK_OK;
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!device_memory(queries) || (out_block && !device_memory(out_block)) || (out_light && !device_memory(out_light))
+        || (out_height && !device_memory(out_height))) {
+        set_error("blk_query_cells: queries and outputs must be device memory");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    query_cells_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream_handle)>>>(queries, n, ctx->ids, ctx->light,
+        ctx->hmap, region(ctx), ctx->env_stride, out_block, out_light, out_height);
+    return cuda_fail(cudaGetLastError(), "query_cells_kernel launch");
+}
+
+int blk_query_solid(blk_ctx* ctx, const blk_box_query* queries, uint32_t n, uint8_t* out_solid,
+    uintptr_t stream_handle)
+{
+    if (!ctx || (n && (!queries || !out_solid))) {
+        set_error("blk_query_solid: invalid argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!ctx->generated) {
+        set_error("blk_query_solid: call blk_generate first");
+        return BLK_ERR_NOT_READY;
+    }
+    if (n == 0)
+        return BLK_OK;
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!device_memory(queries) || !device_memory(out_solid)) {
+        set_error("blk_query_solid: queries and outputs must be device memory");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    query_solid_kernel<<<grid_for(static_cast<uint64_t>(n) * 32, 256), 256, 0, as_stream(stream_handle)>>>(queries,
+        n, ctx->ids, region(ctx), ctx->env_stride, out_solid);
+    return cuda_fail(cudaGetLastError(), "query_solid_kernel launch");
+}
+
+int blk_snapshot_overrides(blk_ctx* ctx, uint32_t env, blk_override* out, uint32_t capacity, uint32_t* count,
+    uintptr_t stream_handle)
+{
+    if (!ctx || !count || (capacity && !out) || env >= ctx->cfg.num_envs) {
+        set_error("blk_snapshot_overrides: invalid argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!ctx->generated) {
+        set_error("blk_snapshot_overrides: call blk_generate first");
+        return BLK_ERR_NOT_READY;
+    }
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!device_memory(count) || (capacity && !device_memory(out))) {
+        set_error("blk_snapshot_overrides: outputs must be device memory");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    const uint64_t columns = ctx->columns_per_env;
+    const uint8_t* ids = ctx->ids + static_cast<uint64_t>(env) * ctx->env_stride;
+    const int16_t* top = ctx->terrain_top + static_cast<uint64_t>(env) * columns;
+    // Scratch: the override CSR counts / offsets are not live between calls.
+    snapshot_count_kernel<<<grid_for(columns, 256), 256, 0, st>>>(ids, top, region(ctx), ctx->col_count);
+    BLK_CUDA(cudaGetLastError(), "snapshot count launch");
+    BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, columns, st));
+    snapshot_write_kernel<<<grid_for(columns, 256), 256, 0, st>>>(ids, top, region(ctx), env, ctx->col_count,
+        ctx->col_offset, out, capacity, count);
+    return cuda_fail(cudaGetLastError(), "snapshot write launch");
 }
 
 int blk_sync(blk_ctx* ctx, uintptr_t stream_handle)

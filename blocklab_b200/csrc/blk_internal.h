@@ -71,6 +71,7 @@ int cuda_fail(cudaError_t e, const char* what);
 
 // Copies `bytes` from host or device memory `src` into the device buffer
 // `staging` (when src is host memory) and returns the device pointer to use.
+bool device_memory(const void* p);
 int stage_input(const void* src, size_t bytes, void* staging, cudaStream_t stream, const void** out);
 
 TerrainParams terrain_params(const blk_ctx* ctx);

@@ -174,6 +174,51 @@ class WorldBatch:
         n = int(cnt.item())
         return vox[: min(n, cap)], n, tuple(int(v) for v in hdr.tolist())
 
+    def query_cells(self, xyz, env=0, stream: Optional[torch.cuda.Stream] = None):
+        """Block id (255 outside the region), light byte and column height (world
+        y, INT32_MIN outside) of world cells xyz (N, 3); env scalar or (N,)."""
+        q = _queries(CELL_QUERY_DTYPE, xyz, env, ("x", "y", "z"))
+        dev = torch.device("cuda", self.device)
+        qd = torch.from_numpy(q.view(np.uint8)).to(dev)
+        n = len(q)
+        block = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+        light = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+        height = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        check(N.lib.blk_query_cells(self._ctx, qd.data_ptr(), n, block.data_ptr(), light.data_ptr(), height.data_ptr(),
+                                    _stream_handle(stream, self.device)))
+        return block[:n], light[:n], height[:n]
+
+    def query_solid(self, box_min, box_max, env=0, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """1 where the inclusive world box [box_min, box_max] (N, 3), clipped to
+        the region, holds a solid block (World::hasSolidBlockInArea)."""
+        box_min, box_max = np.asarray(box_min, np.int64).reshape(-1, 3), np.asarray(box_max, np.int64).reshape(-1, 3)
+        q = np.zeros(len(box_min), BOX_QUERY_DTYPE)
+        for k, name in enumerate(("x", "y", "z")):
+            q["min_" + name] = box_min[:, k]
+            q["max_" + name] = box_max[:, k]
+        q["env"] = env
+        dev = torch.device("cuda", self.device)
+        qd = torch.from_numpy(q.view(np.uint8)).to(dev)
+        out = torch.empty(max(len(q), 1), dtype=torch.uint8, device=dev)
+        check(N.lib.blk_query_solid(self._ctx, qd.data_ptr(), len(q), out.data_ptr(),
+                                    _stream_handle(stream, self.device)))
+        return out[: len(q)]
+
+    def snapshot(self, env: int, stream: Optional[torch.cuda.Stream] = None) -> np.ndarray:
+        """Overlay of one env: the cells that differ from its terrain, as
+        override records in (z, x, y) order; generate(seed, snapshot) rebuilds it."""
+        dev = torch.device("cuda", self.device)
+        cnt = torch.zeros(1, dtype=torch.int32, device=dev)
+        cap = 1 << 16
+        while True:
+            out = torch.empty(cap * 16, dtype=torch.uint8, device=dev)
+            check(N.lib.blk_snapshot_overrides(self._ctx, env, out.data_ptr(), cap, cnt.data_ptr(),
+                                               _stream_handle(stream, self.device)))
+            n = int(cnt.item())
+            if n <= cap:
+                return out[: n * 16].cpu().numpy().view(OVERRIDE_DTYPE).copy()
+            cap = n
+
     def effective_light(self, dimming, out: Optional[torch.Tensor] = None,
                         stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """(sky - min(sky, dimming[env])) << 4 | block for every cell."""
@@ -210,6 +255,35 @@ class WorldBatch:
                                  out_light.data_ptr() if light else None, out_hm.data_ptr() if height_map else None,
                                  _stream_handle(stream, self.device)))
         return out_ids, out_light, out_hm
+
+
+CELL_QUERY_DTYPE = np.dtype([("x", "<i4"), ("y", "<i4"), ("z", "<i4"), ("env", "<u4")])
+BOX_QUERY_DTYPE = np.dtype([("min_x", "<i4"), ("min_y", "<i4"), ("min_z", "<i4"), ("max_x", "<i4"), ("max_y", "<i4"),
+                            ("max_z", "<i4"), ("env", "<u4"), ("reserved", "<u4")])
+
+
+def _queries(dtype, xyz, env, names):
+    xyz = np.asarray(xyz, np.int64).reshape(-1, 3)
+    q = np.zeros(len(xyz), dtype)
+    for k, name in enumerate(names):
+        q[name] = xyz[:, k]
+    q["env"] = env
+    return q
+
+
+def save_snapshot(path: str, seeds, overrides, tick: int = 0, config: Optional[WorldConfig] = None) -> None:
+    """Writes a batch snapshot: per-env seeds, the overlay records of every env
+    (WorldBatch.snapshot), the day tick and the region."""
+    meta = {} if config is None else {k: getattr(config, k) for k in ("width", "height", "depth", "terrain", "base",
+                                                                      "amplitude")}
+    np.savez(path, seeds=np.asarray(seeds, np.uint32), overrides=np.asarray(overrides, OVERRIDE_DTYPE),
+             tick=np.int64(tick), meta=np.array(repr(meta)))
+
+
+def load_snapshot(path: str):
+    """(seeds, overrides, tick) of a snapshot written by save_snapshot."""
+    with np.load(path) as z:
+        return z["seeds"], z["overrides"].view(OVERRIDE_DTYPE), int(z["tick"])
 
 
 def sky_light_at_time(tick: int) -> int:

@@ -174,6 +174,46 @@ int blk_effective_light(blk_ctx* ctx, const uint8_t* dimming, uint8_t* out, uint
 /* Integer sky level at a day tick (src/world/Lighting.cpp:21-49). Host only. */
 uint8_t blk_sky_light_at_time(uint32_t tick);
 
+/* Sparse queries of the resident worlds. They replace the reference's copy of
+ * the whole block cache to the host after every generation
+ * (src/world/WorldGenerator.cu:798-815, src/world/World.cpp:149-183), which its
+ * physics then reads through World::block (src/world/World.cpp:221-231),
+ * World::terrainHeight (src/world/World.h:56, src/world/World.cpp:67-78) and
+ * World::hasSolidBlockInArea (src/world/World.cpp:289-307). Queries use world
+ * coordinates; queries and outputs are device memory. */
+typedef struct blk_cell_query {
+    int32_t x, y, z;
+    uint32_t env;
+} blk_cell_query;
+
+typedef struct blk_box_query {
+    int32_t min_x, min_y, min_z;
+    int32_t max_x, max_y, max_z; /* inclusive */
+    uint32_t env;
+    uint32_t reserved;
+} blk_box_query;
+
+/* Per query i: out_block[i] = block id, or 255 outside the region (where
+ * World::block returns null); out_light[i] = sky << 4 | block light, 0 outside;
+ * out_height[i] = world y of the highest solid block of column (x, z), or
+ * INT32_MIN when the column is outside the region. Any output may be NULL. */
+int blk_query_cells(blk_ctx* ctx, const blk_cell_query* queries, uint32_t n, uint8_t* out_block, uint8_t* out_light,
+    int32_t* out_height, uintptr_t stream);
+
+/* out_solid[i] = 1 if the box of query i, clipped to the region, holds a solid
+ * (opaque) block, else 0 (World::hasSolidBlockInArea). */
+int blk_query_solid(blk_ctx* ctx, const blk_box_query* queries, uint32_t n, uint8_t* out_solid, uintptr_t stream);
+
+/* Snapshot of one env's overlay: every cell whose block differs from the
+ * generated terrain, as blk_override records (world coordinates, env = `env`),
+ * in ascending (z, x, y) order. blk_generate with the env's seed and these
+ * overrides rebuilds the same world (ids, light, height map). The reference
+ * keeps the overlay as World's override columns (src/world/World.h:143,
+ * src/world/World.cpp:239-287). `out` (capacity entries) and `count` are device
+ * memory; *count receives the full size even when it exceeds the capacity. */
+int blk_snapshot_overrides(blk_ctx* ctx, uint32_t env, blk_override* out, uint32_t capacity, uint32_t* count,
+    uintptr_t stream);
+
 /* Copies env range [env_begin, env_begin + n_envs) of the world arrays to
  * caller memory in the device layout (any of the outputs may be NULL).
  * Replaces the per-generation cache readback (src/world/WorldGenerator.cu:798-815). */
