@@ -8,12 +8,13 @@ conversion, as hand-written sm_100a CUDA behind a C ABI (include/blk_world.h).
 from ._native import (AIR, DIRT, EDIT_REMOVE_TORCH, EDIT_SET, GRASS, STONE, TERRAIN_FBM, TERRAIN_FLAT,
                       TERRAIN_REFERENCE, TORCH, BlkError)
 from .observation import convert_rgba8_to_float_nchw
-from .world import (BOX_QUERY_DTYPE, CELL_QUERY_DTYPE, OVERRIDE_DTYPE, WorldBatch, WorldConfig, load_snapshot,
-                    make_overrides, save_snapshot, sky_light_at_time, sky_light_dimming, torch_key)
+from .world import (BOX_QUERY_DTYPE, CELL_QUERY_DTYPE, OVERRIDE_DTYPE, RENDER_PARAMS_DTYPE, WorldBatch, WorldConfig,
+                    load_snapshot, make_overrides, render_params_at, save_snapshot, sky_light_at_time,
+                    sky_light_dimming, torch_key)
 
 __all__ = [
     "AIR", "GRASS", "DIRT", "STONE", "TORCH", "EDIT_SET", "EDIT_REMOVE_TORCH", "TERRAIN_REFERENCE", "TERRAIN_FBM",
     "TERRAIN_FLAT", "BlkError", "convert_rgba8_to_float_nchw", "OVERRIDE_DTYPE", "WorldBatch", "WorldConfig",
     "make_overrides", "sky_light_at_time", "sky_light_dimming", "torch_key", "CELL_QUERY_DTYPE", "BOX_QUERY_DTYPE",
-    "save_snapshot", "load_snapshot",
+    "save_snapshot", "load_snapshot", "RENDER_PARAMS_DTYPE", "render_params_at",
 ]

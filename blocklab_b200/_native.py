@@ -113,6 +113,9 @@ SIGNATURES = {
     "blk_query_cells": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _VP, _UP]),
     "blk_query_solid": (ctypes.c_int, [_VP, _VP, _U32, _VP, _UP]),
     "blk_snapshot_overrides": (ctypes.c_int, [_VP, _U32, _VP, _U32, _VP, _UP]),
+    "blk_render_params_at": (None, [ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                    _U32, _VP]),
+    "blk_render_frames": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _UP]),
 }
 
 

@@ -6,6 +6,7 @@
 
 #include <cstdio>
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -841,6 +842,7 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     ctx->box_capacity = 2 * std::max<uint32_t>(c.max_edits, 1);
     A(dalloc(&ctx->boxes, ctx->box_capacity, "relight boxes"));
     A(dalloc(&ctx->box_count, 1, "relight box count"));
+    A(dalloc(&ctx->render_params, envs, "render parameters"));
     A(dalloc(&ctx->flags, 1, "flags"));
     {
         int sms = 148;
@@ -893,7 +895,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
             cudaEventDestroy(ev);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -1123,6 +1125,110 @@ uint8_t blk_sky_light_at_time(uint32_t t)
     if (tt <= sunriseEnd)
         return static_cast<uint8_t>(4 + 11 * (tt - sunriseStart) / (sunriseEnd - sunriseStart));
     return 15;
+}
+
+void blk_render_params_at(float x, float y, float z, float yaw, float pitch, uint32_t tick, blk_render_params* out)
+{
+    if (!out)
+        return;
+    const float pi = 3.14159265358979323846f;
+    const int t = static_cast<int>(tick % 24000u);
+    auto normalize3 = [](float v[3]) {
+        const float inv = 1.0f / std::sqrt(v[0] * v[0] + v[1] * v[1] + v[2] * v[2]);
+        v[0] *= inv;
+        v[1] *= inv;
+        v[2] *= inv;
+    };
+    // Camera (src/graphics/Renderer.cpp:76-80, 773-778): eye 1.62 above the feet.
+    blk_render_params p {};
+    p.origin[0] = x;
+    p.origin[1] = y + 1.62f;
+    p.origin[2] = z;
+    const float pc = std::cos(pitch);
+    p.forward[0] = std::sin(yaw) * pc;
+    p.forward[1] = std::sin(pitch);
+    p.forward[2] = std::cos(yaw) * pc;
+    normalize3(p.forward);
+    p.right[0] = std::cos(yaw);
+    p.right[1] = 0.0f;
+    p.right[2] = -std::sin(yaw);
+    normalize3(p.right);
+    p.up[0] = p.forward[1] * p.right[2] - p.forward[2] * p.right[1];
+    p.up[1] = p.forward[2] * p.right[0] - p.forward[0] * p.right[2];
+    p.up[2] = p.forward[0] * p.right[1] - p.forward[1] * p.right[0];
+    normalize3(p.up);
+    // Projection and fog (src/graphics/Renderer.cpp:795-800).
+    p.far_plane = 48.0f;
+    p.fov_radians = pi / 2.25f;
+    p.fog_start = 10.0f;
+    p.fog_end = 28.0f;
+    // Sky light factor (src/world/Lighting.cpp:21-51, float trait 4/15 .. 1).
+    const float fmin = 4.0f / 15.0f, fmax = 1.0f;
+    float factor = fmax;
+    if (t >= 12000 && t <= 13702)
+        factor = fmax - (fmax - fmin) * static_cast<float>(t - 12000) / static_cast<float>(13702 - 12000);
+    else if (t > 13702 && t <= 22300)
+        factor = fmin;
+    else if (t > 22300 && t <= 23961)
+        factor = fmin + (fmax - fmin) * static_cast<float>(t - 22300) / static_cast<float>(23961 - 22300);
+    // Sky colour (src/world/Lighting.cpp:53-80): night-day mix by brightness,
+    // then sunset / sunrise tints over their ramps.
+    const float day[3] = { 0.42f, 0.64f, 0.86f }, night[3] = { 0.015f, 0.025f, 0.070f };
+    const float sunrise[3] = { 0.72f, 0.42f, 0.24f }, sunset[3] = { 0.75f, 0.34f, 0.20f };
+    const float brightness = (factor - fmin) / (fmax - fmin);
+    for (int k = 0; k < 3; ++k)
+        p.sky_color[k] = night[k] * (1.0f - brightness) + day[k] * brightness;
+    auto tint = [&](int start, int end, const float* target) {
+        if (t >= start && t <= end) {
+            const float progress = static_cast<float>(t - start) / static_cast<float>(end - start);
+            const float tri = 1.0f - std::fabs(2.0f * progress - 1.0f);
+            const float c = std::fmin(std::fmax(tri, 0.0f), 1.0f);
+            const float w = c * c * (3.0f - 2.0f * c);
+            for (int k = 0; k < 3; ++k)
+                p.sky_color[k] = p.sky_color[k] * (1.0f - w) + target[k] * w;
+        }
+    };
+    tint(12000, 13702, sunset);
+    tint(22300, 23961, sunrise);
+    p.sky_light_dimming = 15u - blk_sky_light_at_time(static_cast<uint32_t>(t));
+    // Light direction (src/world/Lighting.cpp:88-112): the sun (or moon) on a
+    // circle around noon, tilted 0.3 along z, always above the horizon.
+    int offset = t - 6000;
+    if (offset < -12000)
+        offset += 24000;
+    else if (offset >= 12000)
+        offset -= 24000;
+    const float angle = 2.0f * pi * static_cast<float>(offset) / 24000.0f;
+    float sun[3] = { -std::sin(angle), std::cos(angle), 0.3f };
+    if (sun[1] < 0.0f)
+        for (float& v : sun)
+            v = -v;
+    normalize3(sun);
+    for (int k = 0; k < 3; ++k)
+        p.sky_light_direction[k] = sun[k];
+    *out = p;
+}
+
+int blk_render_frames(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
+    uint8_t* out_rgba, uintptr_t stream_handle)
+{
+    if (!ctx || !params || !out_rgba || width == 0 || height == 0 || width > 8192 || height > 8192) {
+        set_error("blk_render_frames: invalid argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!ctx->generated) {
+        set_error("blk_render_frames: call blk_generate first");
+        return BLK_ERR_NOT_READY;
+    }
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!device_memory(out_rgba)) {
+        set_error("blk_render_frames: out_rgba must be device memory");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t st = as_stream(stream_handle);
+    const void* p = nullptr;
+    BLK_CHECK(stage_input(params, sizeof(blk_render_params) * ctx->cfg.num_envs, ctx->render_params, st, &p));
+    return launch_render(ctx, static_cast<const blk_render_params*>(p), width, height, out_rgba, st);
 }
 
 int blk_readback(blk_ctx* ctx, uint32_t env_begin, uint32_t n_envs, uint8_t* ids, uint8_t* light, int16_t* height_map,

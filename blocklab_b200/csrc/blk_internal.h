@@ -51,6 +51,7 @@ struct blk_ctx {
 
     uint32_t* park = nullptr;             // tile-kernel scratch: 16 words x 1024 threads per CTA
     uint32_t park_ctas = 0;
+    blk_render_params* render_params = nullptr; // [num_envs] staging of host-resident render parameters
     uint32_t* flags = nullptr;            // device error flag word
     uint32_t* h_flags = nullptr;          // pinned mirror
 
@@ -78,6 +79,8 @@ TerrainParams terrain_params(const blk_ctx* ctx);
 
 int launch_relight(blk_ctx* ctx, cudaStream_t stream);
 int launch_terrain(blk_ctx* ctx, cudaStream_t stream);
+int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,
+    cudaStream_t stream);
 void halo_order_table(uint16_t* out);
 int halo_order_size();
 

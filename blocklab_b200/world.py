@@ -204,6 +204,20 @@ class WorldBatch:
                                     _stream_handle(stream, self.device)))
         return out[: len(q)]
 
+    def render(self, params, width: int, height: int, out: Optional[torch.Tensor] = None,
+               stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """RGBA8 sRGB frames (num_envs, height, width, 4) of every env from
+        per-env render parameters (RENDER_PARAMS_DTYPE records)."""
+        params = np.ascontiguousarray(params, RENDER_PARAMS_DTYPE).reshape(-1)
+        if len(params) != self.config.num_envs:
+            raise ValueError("one render parameter record per env")
+        if out is None:
+            out = torch.empty((self.config.num_envs, height, width, 4), dtype=torch.uint8,
+                              device=torch.device("cuda", self.device))
+        check(N.lib.blk_render_frames(self._ctx, params.ctypes.data, width, height, out.data_ptr(),
+                                      _stream_handle(stream, self.device)))
+        return out
+
     def snapshot(self, env: int, stream: Optional[torch.cuda.Stream] = None) -> np.ndarray:
         """Overlay of one env: the cells that differ from its terrain, as
         override records in (z, x, y) order; generate(seed, snapshot) rebuilds it."""
@@ -260,6 +274,21 @@ class WorldBatch:
 CELL_QUERY_DTYPE = np.dtype([("x", "<i4"), ("y", "<i4"), ("z", "<i4"), ("env", "<u4")])
 BOX_QUERY_DTYPE = np.dtype([("min_x", "<i4"), ("min_y", "<i4"), ("min_z", "<i4"), ("max_x", "<i4"), ("max_y", "<i4"),
                             ("max_z", "<i4"), ("env", "<u4"), ("reserved", "<u4")])
+
+
+RENDER_PARAMS_DTYPE = np.dtype([("origin", "<f4", 3), ("forward", "<f4", 3), ("right", "<f4", 3), ("up", "<f4", 3),
+                                ("far_plane", "<f4"), ("fov_radians", "<f4"), ("fog_start", "<f4"), ("fog_end", "<f4"),
+                                ("sky_color", "<f4", 3), ("sky_light_dimming", "<u4"),
+                                ("sky_light_direction", "<f4", 3), ("reserved", "<u4")])
+
+
+def render_params_at(position, yaw: float, pitch: float, tick: int) -> np.ndarray:
+    """blk_render_params of an agent with feet at `position` looking along
+    yaw / pitch at day tick `tick` (Renderer::buildRenderParams)."""
+    out = np.zeros(1, RENDER_PARAMS_DTYPE)
+    x, y, z = (float(v) for v in position)
+    N.lib.blk_render_params_at(x, y, z, float(yaw), float(pitch), int(tick) % 24000, out.ctypes.data)
+    return out[0]
 
 
 def _queries(dtype, xyz, env, names):

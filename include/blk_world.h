@@ -214,6 +214,40 @@ int blk_query_solid(blk_ctx* ctx, const blk_box_query* queries, uint32_t n, uint
 int blk_snapshot_overrides(blk_ctx* ctx, uint32_t env, blk_override* out, uint32_t capacity, uint32_t* count,
     uintptr_t stream);
 
+/* Camera and sky of one env's frame: the reference's RenderParams
+ * (shaders/render_params.hlsl, filled by Renderer::buildRenderParams,
+ * src/graphics/Renderer.cpp:773-808) without the viewport and frame fields. */
+typedef struct blk_render_params {
+    float origin[3];   /* eye position, world coordinates */
+    float forward[3];  /* unit view direction */
+    float right[3];
+    float up[3];
+    float far_plane;   /* 48 in the reference */
+    float fov_radians; /* vertical field of view, pi / 2.25 in the reference */
+    float fog_start, fog_end;
+    float sky_color[3];
+    uint32_t sky_light_dimming; /* 15 - skyLightAtTime(t) */
+    float sky_light_direction[3];
+    uint32_t reserved;
+} blk_render_params;
+
+/* Render parameters of an agent standing at (x, y, z) (feet) looking along
+ * yaw / pitch (radians) at day tick `tick` (0..23999): eye 1.62 above the
+ * feet, the reference's projection and fog constants, sky colour, light
+ * direction and dimming at that tick (src/graphics/Renderer.cpp:76-80,773-808;
+ * src/world/Lighting.cpp:53-118). Host only. */
+void blk_render_params_at(float x, float y, float z, float yaw, float pitch, uint32_t tick, blk_render_params* out);
+
+/* Frames of every env, RGBA8 sRGB, shape (num_envs, height, width, 4): the
+ * first face along each pixel's view ray, shaded as the reference's voxel
+ * pipeline shades it (shaders/voxel.vert.hlsl:110-158, shaders/lighting.hlsl,
+ * shaders/mesh.frag.hlsl:12-82, shaders/fog.hlsl), sky colour where no face
+ * lies within the far plane. Only the world region is drawn (no mobs, drops
+ * or held items). `params` holds num_envs entries (host or device memory);
+ * `out_rgba` is device memory. */
+int blk_render_frames(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
+    uint8_t* out_rgba, uintptr_t stream);
+
 /* Copies env range [env_begin, env_begin + n_envs) of the world arrays to
  * caller memory in the device layout (any of the outputs may be NULL).
  * Replaces the per-generation cache readback (src/world/WorldGenerator.cu:798-815). */

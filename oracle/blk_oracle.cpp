@@ -514,3 +514,334 @@ uint32_t orc_apply_edits(uint32_t W, uint32_t H, uint32_t D, int32_t origin_y, u
 }
 
 } // extern "C"
+
+// ---------------------------------------------------------------- frames --
+// CPU restatement of the voxel pipeline's shading for one region, ray-cast
+// per pixel centre: shaders/voxel.vert.hlsl:110-158 (faces, torch box, face
+// light), shaders/lighting.hlsl:3-30, shaders/mesh.frag.hlsl:12-82 (texels,
+// sRGB palette, fog mix), shaders/projection.hlsl (camera), an sRGB target.
+// Volumes in the reference layout x + W * (y + H * z).
+namespace {
+
+struct RenderParamsC {
+    float origin[3], forward[3], right[3], up[3];
+    float far_plane, fov_radians, fog_start, fog_end;
+    float sky_color[3];
+    uint32_t sky_light_dimming;
+    float sky_light_direction[3];
+    uint32_t reserved;
+};
+
+enum { kLeft = 0, kRight, kTop, kBottom, kFront, kBack };
+
+float frac_(float x) { return x - std::floor(x); }
+float sat_(float x) { return std::fmin(std::fmax(x, 0.0f), 1.0f); }
+float lerp_(float a, float b, float t) { return a + t * (b - a); }
+
+float hash21_(float px, float py)
+{
+    float x = frac_(px * 0.1031f), y = frac_(py * 0.1031f), z = frac_(px * 0.1031f);
+    const float d = x * (y + 33.33f) + y * (z + 33.33f) + z * (x + 33.33f);
+    x += d;
+    y += d;
+    z += d;
+    return frac_((x + y) * z);
+}
+
+void texel_(int mat, float u, float v, float wx, float wz, float rgb[3])
+{
+    float tx, ty;
+    if (mat == 0) {
+        tx = std::floor(wx * 16.0f);
+        ty = std::floor(wz * 16.0f);
+    } else {
+        tx = std::floor(sat_(u) * 15.999f);
+        ty = std::floor(sat_(v) * 15.999f);
+    }
+    const float n = hash21_(tx + mat * 17.0f, ty + mat * 17.0f);
+    float c[3];
+    auto mix3 = [&](float a0, float a1, float a2, float b0, float b1, float b2) {
+        c[0] = lerp_(a0, b0, n);
+        c[1] = lerp_(a1, b1, n);
+        c[2] = lerp_(a2, b2, n);
+    };
+    if (mat == 0) { // grass top
+        const float blade = hash21_(tx * 1.7f + 4.0f, ty * 1.7f + 4.0f) >= 0.68f ? 1.0f : 0.0f;
+        mix3(0.22f, 0.50f, 0.18f, 0.36f, 0.64f, 0.27f);
+        c[0] += blade * 0.02f;
+        c[1] += blade * 0.04f;
+        c[2] += blade * 0.01f;
+    } else if (mat == 1) {
+        mix3(0.35f, 0.20f, 0.10f, 0.56f, 0.36f, 0.18f);
+    } else if (mat == 2) {
+        mix3(0.43f, 0.44f, 0.44f, 0.57f, 0.58f, 0.58f);
+    } else if (mat == 3) { // grass side
+        const float dirt[3] = { lerp_(0.32f, 0.48f, n), lerp_(0.20f, 0.31f, n), lerp_(0.11f, 0.17f, n) };
+        const float grass[3] = { lerp_(0.18f, 0.30f, n), lerp_(0.46f, 0.58f, n), lerp_(0.15f, 0.21f, n) };
+        float chance = 1.0f;
+        if (ty >= 15.0f)
+            chance = 0.0f;
+        else if (ty >= 14.0f)
+            chance = 0.12f;
+        else if (ty >= 13.0f)
+            chance = 0.32f;
+        else if (ty >= 12.0f)
+            chance = 0.58f;
+        const float m = hash21_(tx + 11.0f, ty + 11.0f) >= 1.0f - chance ? 1.0f : 0.0f;
+        for (int k = 0; k < 3; ++k)
+            c[k] = lerp_(grass[k], dirt[k], m);
+    } else if (mat == 6) { // torch side
+        const float wood[3] = { lerp_(0.46f, 0.58f, n), lerp_(0.25f, 0.34f, n), lerp_(0.10f, 0.16f, n) };
+        const float ember[3] = { lerp_(1.00f, 1.00f, n), lerp_(0.52f, 0.88f, n), lerp_(0.08f, 0.24f, n) };
+        const float e = v >= 0.72f ? 1.0f : 0.0f;
+        for (int k = 0; k < 3; ++k)
+            c[k] = lerp_(wood[k], ember[k], e);
+    } else { // torch top
+        mix3(1.00f, 0.52f, 0.08f, 1.00f, 0.88f, 0.24f);
+    }
+    for (int k = 0; k < 3; ++k)
+        rgb[k] = std::pow(sat_(c[k]), 2.2f);
+}
+
+float face_dot_(int f, const float v[3])
+{
+    switch (f) {
+    case kLeft: return -v[0];
+    case kRight: return v[0];
+    case kTop: return v[1];
+    case kBottom: return -v[1];
+    case kFront: return v[2];
+    default: return -v[2];
+    }
+}
+
+float face_sky_(int f, const RenderParamsC& p)
+{
+    const float direct = lerp_(0.4f, 1.0f, sat_(face_dot_(f, p.sky_light_direction)));
+    const float t = sat_(p.sky_light_direction[1] / 0.6f);
+    const float fallback = 1.0f - t * t * (3.0f - 2.0f * t);
+    if (fallback < 1e-3f)
+        return direct;
+    const float k = 1.0f / std::sqrt(1.09f);
+    const float fd[3] = { 0.0f, k, 0.3f * k };
+    return lerp_(direct, lerp_(0.4f, 1.0f, sat_(face_dot_(f, fd))), fallback);
+}
+
+float face_block_(int f)
+{
+    const float ka = 1.0f / std::sqrt(0.35f * 0.35f + 0.85f * 0.85f + 0.45f * 0.45f);
+    const float fa = 1.0f / std::sqrt(0.55f * 0.55f + 0.65f * 0.65f + 0.25f * 0.25f);
+    const float key[3] = { 0.35f * ka, 0.85f * ka, 0.45f * ka }, fill[3] = { -0.55f * fa, 0.65f * fa, -0.25f * fa };
+    return 0.45f + sat_(face_dot_(f, key)) * 0.40f + sat_(face_dot_(f, fill)) * 0.15f;
+}
+
+uint32_t srgb8_(float c)
+{
+    c = sat_(c);
+    const float s = c <= 0.0031308f ? 12.92f * c : 1.055f * std::pow(c, 1.0f / 2.4f) - 0.055f;
+    return static_cast<uint32_t>(std::lrint(s * 255.0f));
+}
+
+} // namespace
+
+extern "C" void orc_render_frame(uint32_t W, uint32_t H, uint32_t D, int32_t ox, int32_t oy, int32_t oz,
+    const uint8_t* blocks, const uint8_t* block_light, const uint8_t* sky_light, const void* params, uint32_t width,
+    uint32_t height, uint8_t* out_rgba)
+{
+    RenderParamsC p;
+    std::memcpy(&p, params, sizeof(p));
+    const int dims[3] = { static_cast<int>(W), static_cast<int>(H), static_cast<int>(D) };
+    auto inside = [&](const int c[3]) {
+        return c[0] >= 0 && c[1] >= 0 && c[2] >= 0 && c[0] < dims[0] && c[1] < dims[1] && c[2] < dims[2];
+    };
+    auto idx = [&](const int c[3]) { return static_cast<size_t>(c[0]) + W * (static_cast<size_t>(c[1]) + H * c[2]); };
+    auto block = [&](const int c[3]) -> uint8_t { return inside(c) ? blocks[idx(c)] : 0; };
+    auto opaque = [](uint8_t b) { return b != 0 && b != 4; };
+    const float t = std::tan(p.fov_radians * 0.5f);
+    const float aspect = static_cast<float>(width) / static_cast<float>(height);
+    const float o[3] = { p.origin[0] - ox, p.origin[1] - oy, p.origin[2] - oz };
+    const int off[6][3] = { { -1, 0, 0 }, { 1, 0, 0 }, { 0, 1, 0 }, { 0, -1, 0 }, { 0, 0, 1 }, { 0, 0, -1 } };
+    const float kNear = 0.05f;
+    for (uint32_t py = 0; py < height; ++py)
+        for (uint32_t px = 0; px < width; ++px) {
+            const float xn = (px + 0.5f) / width * 2.0f - 1.0f, yn = (py + 0.5f) / height * 2.0f - 1.0f;
+            const float vx = xn * aspect * t, vy = -yn * t;
+            float d[3];
+            for (int k = 0; k < 3; ++k)
+                d[k] = p.right[k] * vx + p.up[k] * vy + p.forward[k];
+            float s0 = 0.0f, s1 = p.far_plane;
+            int entry_axis = -1;
+            for (int k = 0; k < 3; ++k) {
+                if (std::fabs(d[k]) < 1e-20f) {
+                    if (o[k] < 0.0f || o[k] >= dims[k])
+                        s1 = -1.0f;
+                } else {
+                    float ta = (0.0f - o[k]) / d[k], tb = (dims[k] - o[k]) / d[k];
+                    if (ta > tb)
+                        std::swap(ta, tb);
+                    if (ta > s0) {
+                        s0 = ta;
+                        entry_axis = k;
+                    }
+                    s1 = std::fmin(s1, tb);
+                }
+            }
+            // hit: depth, face, block, owner cell, neighbour cell, box coordinates
+            float hs = -1.0f, hl[3] = { 0, 0, 0 };
+            int hf = -1, hn[3] = { 0, 0, 0 };
+            uint8_t hb = 0;
+            auto face_hit = [&](const int* owner, const int* other, int ax, float sh) {
+                const int dir = other[ax] - owner[ax];
+                hs = sh;
+                hf = ax == 0 ? (dir > 0 ? kRight : kLeft) : (ax == 1 ? (dir > 0 ? kTop : kBottom) : (dir > 0 ? kFront : kBack));
+                hb = block(owner);
+                for (int k = 0; k < 3; ++k) {
+                    hn[k] = other[k];
+                    hl[k] = sat_(o[k] + d[k] * sh - owner[k]);
+                }
+                hl[ax] = dir > 0 ? 1.0f : 0.0f;
+            };
+            if (s0 <= s1) {
+                int c[3], st[3];
+                float tmax[3], tdel[3];
+                for (int k = 0; k < 3; ++k) {
+                    int ck = static_cast<int>(std::floor(o[k] + d[k] * s0));
+                    ck = std::min(std::max(ck, 0), dims[k] - 1);
+                    c[k] = ck;
+                    if (d[k] > 0.0f) {
+                        st[k] = 1;
+                        tdel[k] = 1.0f / d[k];
+                        tmax[k] = (ck + 1 - o[k]) / d[k];
+                    } else if (d[k] < 0.0f) {
+                        st[k] = -1;
+                        tdel[k] = -1.0f / d[k];
+                        tmax[k] = (ck - o[k]) / d[k];
+                    } else {
+                        st[k] = 0;
+                        tdel[k] = 3.0e38f;
+                        tmax[k] = 3.0e38f;
+                    }
+                }
+                float s_cell = s0;
+                if (entry_axis >= 0 && s0 >= kNear && s0 <= p.far_plane && opaque(block(c))) {
+                    int out_c[3] = { c[0], c[1], c[2] };
+                    out_c[entry_axis] -= st[entry_axis];
+                    face_hit(c, out_c, entry_axis, s0);
+                }
+                const int max_steps = dims[0] + dims[1] + dims[2] + 3;
+                for (int it = 0; it < max_steps && hs < 0.0f; ++it) {
+                    const uint8_t cur = block(c);
+                    const int ax = tmax[0] <= tmax[1] ? (tmax[0] <= tmax[2] ? 0 : 2) : (tmax[1] <= tmax[2] ? 1 : 2);
+                    const float s_cross = tmax[ax];
+                    if (cur == 4) {
+                        const float lo[3] = { c[0] + 0.4375f, static_cast<float>(c[1]), c[2] + 0.4375f };
+                        const float hi[3] = { c[0] + 0.5625f, c[1] + 0.65f, c[2] + 0.5625f };
+                        float tin = -3.0e38f, tout = 3.0e38f;
+                        int fin = -1, fout = -1;
+                        for (int k = 0; k < 3; ++k) {
+                            if (d[k] == 0.0f) {
+                                if (o[k] < lo[k] || o[k] > hi[k])
+                                    tin = 3.0e38f;
+                                continue;
+                            }
+                            float ta = (lo[k] - o[k]) / d[k], tb = (hi[k] - o[k]) / d[k];
+                            int fa = k == 0 ? kLeft : (k == 1 ? kBottom : kBack);
+                            int fb = k == 0 ? kRight : (k == 1 ? kTop : kFront);
+                            if (ta > tb) {
+                                std::swap(ta, tb);
+                                std::swap(fa, fb);
+                            }
+                            if (ta > tin) {
+                                tin = ta;
+                                fin = fa;
+                            }
+                            if (tb < tout) {
+                                tout = tb;
+                                fout = fb;
+                            }
+                        }
+                        const float lo_s = std::fmax(s_cell, kNear);
+                        if (tin <= tout) {
+                            float sh = -1.0f;
+                            int fh = -1;
+                            if (fin >= 0 && fin != kBottom && tin >= lo_s && tin <= s_cross)
+                                sh = tin, fh = fin;
+                            else if (fout >= 0 && fout != kBottom && tout >= lo_s && tout <= s_cross)
+                                sh = tout, fh = fout;
+                            if (fh >= 0 && sh <= p.far_plane) {
+                                hs = sh;
+                                hf = fh;
+                                hb = 4;
+                                for (int k = 0; k < 3; ++k)
+                                    hn[k] = c[k] + off[fh][k];
+                                hl[0] = sat_((o[0] + d[0] * sh - lo[0]) / 0.125f);
+                                hl[1] = sat_((o[1] + d[1] * sh - lo[1]) / 0.65f);
+                                hl[2] = sat_((o[2] + d[2] * sh - lo[2]) / 0.125f);
+                                break;
+                            }
+                        }
+                    }
+                    if (s_cross > s1 + 1e-4f || s_cross > p.far_plane)
+                        break;
+                    int nxt[3] = { c[0], c[1], c[2] };
+                    nxt[ax] += st[ax];
+                    const uint8_t nb = block(nxt);
+                    if (s_cross >= kNear && opaque(cur) != opaque(nb)) {
+                        if (opaque(cur))
+                            face_hit(c, nxt, ax, s_cross);
+                        else
+                            face_hit(nxt, c, ax, s_cross);
+                        break;
+                    }
+                    for (int k = 0; k < 3; ++k)
+                        c[k] = nxt[k];
+                    s_cell = s_cross;
+                    tmax[ax] += tdel[ax];
+                    if (!inside(c))
+                        break;
+                }
+            }
+            float rgb[3];
+            if (hs < 0.0f) {
+                for (int k = 0; k < 3; ++k)
+                    rgb[k] = p.sky_color[k];
+            } else {
+                uint32_t sky = 0, blk = 0;
+                if (inside(hn)) {
+                    sky = sky_light[idx(hn)];
+                    blk = block_light[idx(hn)];
+                }
+                if (hb == 4)
+                    blk = 15;
+                const uint32_t cur_sky = sky - std::min(sky, p.sky_light_dimming);
+                const float light = std::fmax(cur_sky * face_sky_(hf, p), blk * face_block_(hf)) / 15.0f;
+                float u, v;
+                switch (hf) {
+                case kLeft:
+                case kRight: u = hl[2]; v = hl[1]; break;
+                case kTop: u = hl[0]; v = hl[2]; break;
+                case kBottom: u = hl[2]; v = hl[0]; break;
+                default: u = hl[0]; v = hl[1]; break;
+                }
+                int mat;
+                if (hb == 1)
+                    mat = hf == kTop ? 0 : (hf == kBottom ? 1 : 3);
+                else if (hb == 2)
+                    mat = 1;
+                else if (hb == 3)
+                    mat = 2;
+                else
+                    mat = hf == kTop ? 7 : 6;
+                float alb[3];
+                texel_(mat, u, v, o[0] + d[0] * hs + ox, o[2] + d[2] * hs + oz, alb);
+                const float fog = sat_((hs - p.fog_start) / std::fmax(p.fog_end - p.fog_start, 0.001f));
+                for (int k = 0; k < 3; ++k)
+                    rgb[k] = lerp_(sat_(alb[k] * light), p.sky_color[k], fog);
+            }
+            uint8_t* q = out_rgba + (static_cast<size_t>(py) * width + px) * 4;
+            q[0] = static_cast<uint8_t>(srgb8_(rgb[0]));
+            q[1] = static_cast<uint8_t>(srgb8_(rgb[1]));
+            q[2] = static_cast<uint8_t>(srgb8_(rgb[2]));
+            q[3] = 255;
+        }
+}

@@ -89,6 +89,14 @@ uint32_t orc_permute(uint32_t i, uint32_t n, uint32_t key);
 uint32_t orc_apply_edits(uint32_t W, uint32_t H, uint32_t D, int32_t origin_y, uint8_t* blocks, int16_t* height_map,
     const int32_t* edit_xyz, const uint8_t* edit_kind, const uint8_t* edit_block, uint32_t n_edits);
 
+// Ray-cast RGBA8 sRGB frame (height x width x 4) of one region with the
+// voxel pipeline's shading (shaders/voxel.vert.hlsl:110-158,
+// shaders/lighting.hlsl:3-30, shaders/mesh.frag.hlsl:12-82, shaders/fog.hlsl);
+// `params` is a blk_render_params record (include/blk_world.h).
+void orc_render_frame(uint32_t W, uint32_t H, uint32_t D, int32_t ox, int32_t oy, int32_t oz, const uint8_t* blocks,
+    const uint8_t* block_light, const uint8_t* sky_light, const void* params, uint32_t width, uint32_t height,
+    uint8_t* out_rgba);
+
 #ifdef __cplusplus
 }
 #endif

@@ -187,6 +187,20 @@ class Oracle:
                                         _ptr(blk), ctypes.c_uint32(len(kind)))
 
     # -- whole pipeline -------------------------------------------------------
+    def render_frame(self, spec: WorldSpec, blocks, block_light, sky_light, params, width: int, height: int):
+        """RGBA8 frame (height, width, 4) of one region (reference-layout
+        volumes) for a blk_render_params record given as 96 raw bytes."""
+        raw = np.frombuffer(bytes(params), np.uint8)
+        assert raw.size == 96
+        out = np.zeros((height, width, 4), np.uint8)
+        self.lib.orc_render_frame(ctypes.c_uint32(spec.width), ctypes.c_uint32(spec.height), ctypes.c_uint32(spec.depth),
+                                  ctypes.c_int32(spec.origin[0]), ctypes.c_int32(spec.origin[1]),
+                                  ctypes.c_int32(spec.origin[2]), _ptr(np.ascontiguousarray(blocks, np.uint8)),
+                                  _ptr(np.ascontiguousarray(block_light, np.uint8)),
+                                  _ptr(np.ascontiguousarray(sky_light, np.uint8)), _ptr(raw.copy()),
+                                  ctypes.c_uint32(width), ctypes.c_uint32(height), _ptr(out))
+        return out
+
     def generate(self, spec: WorldSpec, ovr_xyz=None, ovr_block=None, method: str = "per_source"):
         blocks, hm = self.build_blocks(spec, ovr_xyz, ovr_block)
         bl, sl = self.light(blocks, hm, spec.origin[1], method)
@@ -254,4 +268,30 @@ class Reference:
                                         ctypes.c_uint32(w), ctypes.c_uint32(h))
         if rc != 0:
             raise RuntimeError(f"reference conversion failed: {rc}")
+        return out
+
+
+class ReferenceLighting:
+    """The reference's sky functions (src/world/Lighting.cpp) built from its
+    sources into oracle/_ref/libref_lighting.so."""
+
+    def __init__(self):
+        self.lib = ctypes.CDLL(os.path.join(HERE, "_ref", "libref_lighting.so"))
+        self.lib.ref_sky_light_at.restype = ctypes.c_uint8
+        self.lib.ref_sky_light_at.argtypes = [ctypes.c_uint32]
+        for name in ("ref_sky_color_at", "ref_sky_direction_at"):
+            getattr(self.lib, name).restype = None
+            getattr(self.lib, name).argtypes = [ctypes.c_uint32, ctypes.c_void_p]
+
+    def sky_light(self, t: int) -> int:
+        return int(self.lib.ref_sky_light_at(t))
+
+    def sky_color(self, t: int) -> np.ndarray:
+        out = np.zeros(3, np.float32)
+        self.lib.ref_sky_color_at(t, out.ctypes.data)
+        return out
+
+    def sky_direction(self, t: int) -> np.ndarray:
+        out = np.zeros(3, np.float32)
+        self.lib.ref_sky_direction_at(t, out.ctypes.data)
         return out

@@ -1,12 +1,14 @@
 // Minimal vector types standing in for glm when the reference world generator
-// is compiled as a test oracle. Only construction, member access, +, - and ==
-// are provided: the generation/lighting path does no glm arithmetic beyond
-// moving coordinates around (reference: src/world/WorldGenerator.cu,
-// src/world/WorldGenerator.h, include/blocklab/utility/Math.h).
+// and sky functions are compiled as a test oracle: construction, member
+// access, +, -, scalar *, == and the three functions below. The generation /
+// lighting path does no glm arithmetic beyond moving coordinates around
+// (reference: src/world/WorldGenerator.cu, src/world/WorldGenerator.h,
+// include/blocklab/utility/Math.h, src/world/Lighting.cpp).
 //
 // Test infrastructure only; never linked into the product library.
 #pragma once
 
+#include <cmath>
 #include <cstdint>
 
 namespace glm {
@@ -30,6 +32,8 @@ struct tvec3 {
     constexpr explicit tvec3(const tvec3<U>& o) : x(static_cast<T>(o.x)), y(static_cast<T>(o.y)), z(static_cast<T>(o.z)) {}
     friend constexpr tvec3 operator+(tvec3 a, const tvec3& b) { return { a.x + b.x, a.y + b.y, a.z + b.z }; }
     friend constexpr tvec3 operator-(tvec3 a, const tvec3& b) { return { a.x - b.x, a.y - b.y, a.z - b.z }; }
+    friend constexpr tvec3 operator-(const tvec3& a) { return { -a.x, -a.y, -a.z }; }
+    friend constexpr tvec3 operator*(const tvec3& a, T s) { return { a.x * s, a.y * s, a.z * s }; }
     friend constexpr bool operator==(const tvec3& a, const tvec3& b) { return a.x == b.x && a.y == b.y && a.z == b.z; }
 };
 
@@ -39,6 +43,28 @@ struct tvec4 {
     constexpr tvec4() = default;
     constexpr tvec4(T a, T b, T c, T d) : x(a), y(b), z(c), w(d) {}
 };
+
+// The few functions the reference's sky colour and light direction use
+// (src/world/Lighting.cpp:53-112), written to glm's published formulas:
+// mix(x, y, a) = x * (1 - a) + y * a; smoothstep clamps (x - e0) / (e1 - e0)
+// to [0, 1] and returns t * t * (3 - 2 * t); normalize(v) = v * (1 / sqrt(dot(v, v))).
+template <typename T>
+constexpr tvec3<T> mix(const tvec3<T>& x, const tvec3<T>& y, T a)
+{
+    return x * (T(1) - a) + y * a;
+}
+template <typename T>
+T smoothstep(T e0, T e1, T x)
+{
+    T t = (x - e0) / (e1 - e0);
+    t = t < T(0) ? T(0) : (t > T(1) ? T(1) : t);
+    return t * t * (T(3) - T(2) * t);
+}
+template <typename T>
+tvec3<T> normalize(const tvec3<T>& v)
+{
+    return v * (T(1) / std::sqrt(v.x * v.x + v.y * v.y + v.z * v.z));
+}
 
 using vec2 = tvec2<float>;
 using vec3 = tvec3<float>;
