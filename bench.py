@@ -51,11 +51,12 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--envs", type=int, default=None,
                     help="envs per GPU (default: the workload's; smaller batches are for profiler captures)")
-    ap.add_argument("--workload", choices=["reset", "relight", "daynight", "scaleout"], default="reset",
+    ap.add_argument("--workload", choices=["reset", "relight", "daynight", "scaleout", "render"], default="reset",
                     help="reset (default): 128 worlds 256x256x128 regenerated + lit + frames converted per step; "
                          "relight: 1024 worlds 128^3, 10k edits per step + exact relight; daynight: 4096 worlds "
                          "128x128x96, sky sweep + 84x84 frame conversion per step; scaleout: 1024 worlds 256^3 per "
-                         "GPU, 5000x1024/8192 edits per GPU per step + 90x160 frames, optional NCCL gather")
+                         "GPU, 5000x1024/8192 edits per GPU per step + 90x160 frames, optional NCCL gather; "
+                         "render: the reset worlds rendered to 160x90 RGBA8 frames and converted each step")
     ap.add_argument("--gather", action="store_true", help="scaleout: gather observations to rank 0 every step")
     ap.add_argument("--materialize", action="store_true",
                     help="daynight: also materialise the effective light of every cell each step")
@@ -557,6 +558,35 @@ def run_workload(args) -> None:
                 "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_step": conv_bytes, "traffic": None},
             "gpu_launches": (2 if eff is not None else 1) * args.steps, "clocks": clocks})
+        wb.close()
+    elif args.workload == "render":
+        E = args.envs or ENVS_PER_GPU
+        cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, max_overrides=E * TORCHES)
+        wb = B.WorldBatch(cfg, device=local)
+        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+        wb.generate(seeds, wb.place_torches(seeds, TORCHES))
+        hm = wb.height_map.cpu().numpy()
+        # Agents at the world centre on the surface, looking around, at several day times.
+        params = np.array([B.render_params_at((W / 2, hm[e, D // 2, W // 2] + 1, D / 2), 0.7 * e, -0.25,
+                                              (6000 + 997 * e) % 24000) for e in range(E)], B.RENDER_PARAMS_DTYPE)
+        params_dev = torch.from_numpy(params.view(np.uint8).copy()).to(dev)
+        frames = torch.empty((E, FRAME_H, FRAME_W, 4), dtype=torch.uint8, device=dev)
+        obs = torch.empty((E, 3, FRAME_H, FRAME_W), dtype=torch.float32, device=dev)
+        from blocklab_b200 import _native as N
+
+        def step(k):
+            N.check(N.lib.blk_render_frames(wb._ctx, params_dev.data_ptr(), FRAME_W, FRAME_H, frames.data_ptr(),
+                                            torch.cuda.current_stream(dev).cuda_stream))
+            B.convert_rgba8_to_float_nchw(frames, out=obs)
+
+        ms, clocks = time_steps(step, args.steps, args.warmup, dev, pg, local)
+        line.update({
+            "metric": "frames/s (render + convert)", "value": E * world * args.steps / (ms / 1e3), "unit": "frames/s",
+            "ms_per_step": ms / args.steps, "dtype": "u8 -> f32",
+            "config": {"workload": "render: ray-cast 160x90 RGBA8 frames of the reset worlds, convert to NCHW",
+                       "envs_per_gpu": E, "world": [W, H, D], "frames": [E, 3, FRAME_H, FRAME_W],
+                       "parallelism": f"env shards x{world}"},
+            "gpu_launches": 2 * args.steps, "clocks": clocks})
         wb.close()
     else:  # scaleout
         c = dict(SCALEOUT)
