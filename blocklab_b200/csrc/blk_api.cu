@@ -843,6 +843,7 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->boxes, ctx->box_capacity, "relight boxes"));
     A(dalloc(&ctx->box_count, 1, "relight box count"));
     A(dalloc(&ctx->render_params, envs, "render parameters"));
+    A(dalloc(&ctx->col_summary, envs * ctx->columns_per_env, "column summaries"));
     A(dalloc(&ctx->flags, 1, "flags"));
     {
         int sms = 148;
@@ -895,7 +896,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
             cudaEventDestroy(ev);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->col_summary, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -965,6 +966,7 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
         BLK_CUDA(cudaGetLastError(), "override kernels");
     }
     const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;
+    BLK_CHECK(launch_column_summary(ctx, st));
     prof_mark(ctx, mark, 1, st);
     BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_tiles), st));
     prof_mark(ctx, mark, 2, st);

@@ -33,6 +33,7 @@ struct blk_ctx {
     uint32_t* col_offset = nullptr;   // [env * columns + 1]
     uint64_t* entries = nullptr;      // [max_overrides], key y<<40 | order<<8 | block
     uint8_t* ovr_owner = nullptr;     // [max_overrides], 1 for the override owning its column segment
+    uint4* col_summary = nullptr;     // [env * columns] generation column summaries (see column_summary_kernel)
     uint32_t* scan_partials = nullptr;
     uint64_t scan_blocks = 0;
 
@@ -79,6 +80,7 @@ TerrainParams terrain_params(const blk_ctx* ctx);
 
 int launch_relight(blk_ctx* ctx, cudaStream_t stream);
 int launch_terrain(blk_ctx* ctx, cudaStream_t stream);
+int launch_column_summary(blk_ctx* ctx, cudaStream_t stream);
 int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,
     cudaStream_t stream);
 void halo_order_table(uint16_t* out);

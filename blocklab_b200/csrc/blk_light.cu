@@ -60,6 +60,7 @@ struct TileArgs {
     const uint16_t* halo_order;     // halo ext columns sorted by cone distance
     const uint32_t* col_offset;
     const uint64_t* entries;
+    const uint4* col_summary;       // generation: per column summary (column_summary_kernel)
     const uint32_t* dirty_list;
     const uint32_t* dirty_window;
     const uint32_t* dirty_count;
@@ -311,26 +312,21 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     }
 
     // ---- phase A: per-column summary -----------------------------------
-    // All global loads of the thread's columns are issued before any is used.
-    int32_t pa_top[kColIters];
-    uint32_t pa_beg[kColIters], pa_end[kColIters];
+    // Generation reads each ext column's precomputed summary (one 16-byte
+    // load); relight reads the height map. All loads are issued before use.
+    uint4 pa[kColIters];
 #pragma unroll
     for (int it = 0; it < kColIters; ++it) {
         const int c = tid + it * kThreads;
-        pa_top[it] = -1;
-        pa_beg[it] = 0;
-        pa_end[it] = 0;
+        pa[it] = make_uint4(0u, 0u, 0u, 0u);
         if (c < kExtCols) {
             const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
             if (in_world(a, gx, gz)) {
                 const uint64_t col = env_col0 + static_cast<uint64_t>(gz) * a.W + gx;
-                if (a.mode == 0) {
-                    pa_top[it] = __ldg(a.terrain_top + col);
-                    pa_beg[it] = __ldg(a.col_offset + col);
-                    pa_end[it] = __ldg(a.col_offset + col + 1);
-                } else {
-                    pa_top[it] = __ldg(a.hmap + col);
-                }
+                if (a.mode == 0)
+                    pa[it] = __ldg(a.col_summary + col);
+                else
+                    pa[it].x = static_cast<uint16_t>(__ldg(a.hmap + col));
             }
         }
     }
@@ -350,73 +346,23 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
             continue;
         }
         if (a.mode == 0) {
-            const int32_t top = pa_top[it];
-            const int32_t tc = min(top, H - 1);
-            const uint32_t beg = pa_beg[it];
-            const uint32_t n = pa_end[it] - beg;
-            int32_t topf = tc;
-            if (n > 0) {
-                const uint64_t* e = a.entries + beg;
-                int32_t hi_opaque = -1;
-                int32_t dlo = 1 << 20, dhi = -(1 << 20);
-                // Winners: the last entry of each y run (entries sorted by y, then input order).
-                for (uint32_t i = 0; i < n; ++i) {
-                    const uint64_t v = __ldg(e + i);
-                    const int32_t y = static_cast<int32_t>(entry_y(v));
-                    if (i + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + i + 1))) == y)
-                        continue;
-                    const uint8_t b = entry_block(v);
-                    if (is_opaque(b))
-                        hi_opaque = max(hi_opaque, y);
-                    if (b == Torch) {
-                        atomicMin(&s.tmin, y);
-                        atomicMax(&s.tmax, y);
-                    }
-                }
-                // Terrain part of the height map: walk down through cells whose
-                // winning override is non-opaque.
-                int32_t yt = tc;
-                int32_t i = static_cast<int32_t>(n) - 1;
-                while (yt >= 0) {
-                    while (i >= 0 && static_cast<int32_t>(entry_y(__ldg(e + i))) > yt)
-                        --i;
-                    if (i >= 0 && static_cast<int32_t>(entry_y(__ldg(e + i))) == yt
-                        && !is_opaque(entry_block(__ldg(e + i)))) {
-                        --yt;
-                        continue;
-                    }
-                    break;
-                }
-                topf = max(hi_opaque, yt);
-                if (interior) {
-                    // Open cells below the final top: non-opaque overrides there, and
-                    // terrain air between the terrain surface and a higher opaque override.
-                    for (uint32_t k = 0; k < n; ++k) {
-                        const uint64_t v = __ldg(e + k);
-                        const int32_t y = static_cast<int32_t>(entry_y(v));
-                        if (k + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + k + 1))) == y)
-                            continue;
-                        if (!is_opaque(entry_block(v)) && y < topf) {
-                            dlo = min(dlo, y);
-                            dhi = max(dhi, y);
-                        }
-                    }
-                    if (tc + 1 < topf) {
-                        dlo = min(dlo, tc + 1);
-                        dhi = max(dhi, topf - 1);
-                    }
-                    if (dlo <= dhi) {
-                        atomicMin(&s.dmin, dlo);
-                        atomicMax(&s.dmax, dhi);
-                    }
-                }
+            const uint4 v = pa[it];
+            s.top_t[c] = static_cast<int16_t>(v.x & 0xFFFFu);
+            s.top_f[c] = static_cast<int16_t>(v.x >> 16);
+            s.ovr[c] = v.y;
+            const int32_t tlo = static_cast<int16_t>(v.z & 0xFFFFu), thi = static_cast<int16_t>(v.z >> 16);
+            if (tlo <= thi) {
+                atomicMin(&s.tmin, tlo);
+                atomicMax(&s.tmax, thi);
             }
-            s.top_t[c] = static_cast<int16_t>(top);
-            s.top_f[c] = static_cast<int16_t>(topf);
-            s.ovr[c] = (beg << 5) | (n < kCntSat ? n : kCntSat);
+            const int32_t dlo = static_cast<int16_t>(v.w & 0xFFFFu), dhi = static_cast<int16_t>(v.w >> 16);
+            if (interior && dlo <= dhi) {
+                atomicMin(&s.dmin, dlo);
+                atomicMax(&s.dmax, dhi);
+            }
         } else {
             s.top_t[c] = -1;
-            s.top_f[c] = static_cast<int16_t>(clamp_top(pa_top[it] - a.origin_y, H));
+            s.top_f[c] = static_cast<int16_t>(clamp_top(static_cast<int16_t>(pa[it].x) - a.origin_y, H));
             s.ovr[c] = 0;
         }
     }
@@ -1070,6 +1016,91 @@ void halo_order_table(uint16_t* out)
 
 int halo_order_size() { return kHaloCols; }
 
+// Generation summary of every column, computed once per column instead of
+// once per tile whose ext region holds it: x = terrain surface | final top
+// << 16 (local y, int16), y = override list begin << 5 | min(count, 31),
+// z = torch rows min | max << 16, w = rows of open cells under the final top
+// min | max << 16 (empty ranges as 32767 | -32768 << 16).
+__global__ void column_summary_kernel(const int16_t* terrain_top, const uint32_t* col_offset, const uint64_t* entries,
+    int32_t H, uint64_t total, uint4* out)
+{
+    constexpr uint32_t kEmpty = 0x7FFFu | (0x8000u << 16);
+    for (uint64_t col = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; col < total;
+         col += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const int32_t top = terrain_top[col];
+        const int32_t tc = min(top, H - 1);
+        const uint32_t beg = col_offset[col];
+        const uint32_t n = col_offset[col + 1] - beg;
+        int32_t topf = tc;
+        int32_t tlo = 1 << 20, thi = -(1 << 20), dlo = 1 << 20, dhi = -(1 << 20);
+        if (n > 0) {
+            const uint64_t* e = entries + beg;
+            int32_t hi_opaque = -1;
+            // Winners: the last entry of each y run (entries sorted by y, then input order).
+            for (uint32_t i = 0; i < n; ++i) {
+                const uint64_t v = e[i];
+                const int32_t y = static_cast<int32_t>(entry_y(v));
+                if (i + 1 < n && static_cast<int32_t>(entry_y(e[i + 1])) == y)
+                    continue;
+                const uint8_t b = entry_block(v);
+                if (is_opaque(b))
+                    hi_opaque = max(hi_opaque, y);
+                if (b == Torch) {
+                    tlo = min(tlo, y);
+                    thi = max(thi, y);
+                }
+            }
+            // Terrain part of the height map: walk down through cells whose
+            // winning override is non-opaque.
+            int32_t yt = tc;
+            int32_t i = static_cast<int32_t>(n) - 1;
+            while (yt >= 0) {
+                while (i >= 0 && static_cast<int32_t>(entry_y(e[i])) > yt)
+                    --i;
+                if (i >= 0 && static_cast<int32_t>(entry_y(e[i])) == yt && !is_opaque(entry_block(e[i]))) {
+                    --yt;
+                    continue;
+                }
+                break;
+            }
+            topf = max(hi_opaque, yt);
+            // Open cells below the final top: non-opaque overrides there, and
+            // terrain air between the terrain surface and a higher opaque override.
+            for (uint32_t k = 0; k < n; ++k) {
+                const uint64_t v = e[k];
+                const int32_t y = static_cast<int32_t>(entry_y(v));
+                if (k + 1 < n && static_cast<int32_t>(entry_y(e[k + 1])) == y)
+                    continue;
+                if (!is_opaque(entry_block(v)) && y < topf) {
+                    dlo = min(dlo, y);
+                    dhi = max(dhi, y);
+                }
+            }
+            if (tc + 1 < topf) {
+                dlo = min(dlo, tc + 1);
+                dhi = max(dhi, topf - 1);
+            }
+        }
+        uint4 r;
+        r.x = static_cast<uint32_t>(static_cast<uint16_t>(top)) | (static_cast<uint32_t>(static_cast<uint16_t>(topf)) << 16);
+        r.y = (beg << 5) | (n < kCntSat ? n : kCntSat);
+        r.z = tlo <= thi ? static_cast<uint32_t>(static_cast<uint16_t>(tlo)) | (static_cast<uint32_t>(thi) << 16) : kEmpty;
+        r.w = dlo <= dhi ? static_cast<uint32_t>(static_cast<uint16_t>(dlo)) | (static_cast<uint32_t>(dhi) << 16) : kEmpty;
+        out[col] = r;
+    }
+}
+
+int launch_column_summary(blk_ctx* ctx, cudaStream_t stream)
+{
+    const uint64_t total = static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->columns_per_env;
+    uint64_t blocks = (total + 255) / 256;
+    if (blocks > 148ull * 32)
+        blocks = 148ull * 32;
+    column_summary_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ctx->terrain_top, ctx->col_offset,
+        ctx->entries, static_cast<int32_t>(ctx->cfg.height), total, ctx->col_summary);
+    return cuda_fail(cudaGetLastError(), "column_summary_kernel launch");
+}
+
 int launch_terrain(blk_ctx* ctx, cudaStream_t stream)
 {
     if (ctx->cfg.terrain_mode == BLK_TERRAIN_FBM) {
@@ -1099,6 +1130,7 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream)
     a.halo_order = ctx->halo_order;
     a.col_offset = ctx->col_offset;
     a.entries = ctx->entries;
+    a.col_summary = ctx->col_summary;
     a.dirty_list = ctx->dirty_list;
     a.dirty_window = ctx->dirty_window;
     a.dirty_count = ctx->dirty_count;
