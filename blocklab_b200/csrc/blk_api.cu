@@ -792,7 +792,7 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     }
     *out = nullptr;
     const blk_world_config& c = *config;
-    if (c.num_envs == 0 || c.num_envs > 65536 || c.width == 0 || c.depth == 0 || c.width > 4096 || c.depth > 4096
+    if (c.num_envs == 0 || c.num_envs > 65536 || c.max_overrides > (1u << 26) || c.width == 0 || c.depth == 0 || c.width > 4096 || c.depth > 4096
         || c.height == 0 || c.height % 32 != 0 || c.height > 256 || c.terrain_mode < 0 || c.terrain_mode > 2) {
         set_error("blk_ctx_create: unsupported configuration (num_envs 1..65536, W/D 1..4096, H a multiple of 32 up "
                   "to 128, terrain_mode 0..2)");

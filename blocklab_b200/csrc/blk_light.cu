@@ -51,6 +51,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kSlots = 3;                           // interior + up to 2 halo columns per thread
 constexpr int kColIters = (kExtCols + kThreads - 1) / kThreads;
 constexpr uint32_t kCntSat = 31;                    // packed override count saturates here
+constexpr uint32_t kOvrInline = 0x80000000u;        // packed list holds its single entry: y << 8 | block
 
 struct TileArgs {
     uint8_t* ids;
@@ -402,6 +403,31 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         e = a.entries + beg;
     };
 
+    // Calls fn(y, block) for the winning override of every y of ext column c
+    // whose y lies in [ylo, yhi] (entries sorted by y, then input order; the
+    // last of a y run wins).
+    auto for_each_winner = [&](int c, int32_t ylo, int32_t yhi, auto&& fn) {
+        const uint32_t packed = s.ovr[c];
+        if (packed & kOvrInline) {
+            const int32_t y = static_cast<int32_t>((packed >> 8) & 0x1FFu);
+            if (y >= ylo && y <= yhi)
+                fn(y, static_cast<uint8_t>(packed & 0xFFu));
+            return;
+        }
+        const uint64_t* e;
+        uint32_t n;
+        overrides_of(c, e, n);
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint64_t v = __ldg(e + i);
+            const int32_t y = static_cast<int32_t>(entry_y(v));
+            if (y < ylo || y > yhi)
+                continue;
+            if (i + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + i + 1))) == y)
+                continue;
+            fn(y, entry_block(v));
+        }
+    };
+
     // Open-cell and source bits of ext column c for the 32 rows from ybase.
     // source: 0 = torches, 1 = lit cells (above the final top).
     auto column_bits = [&](int c, int ybase, int source, uint32_t& open, uint32_t& src) {
@@ -413,22 +439,13 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         const uint32_t inside = inside_mask(ybase, H); // bands start at row >= 0
         if (a.mode == 0) {
             open = above_mask(ybase, min(static_cast<int32_t>(s.top_t[c]), H - 1));
-            const uint64_t* e;
-            uint32_t n;
-            overrides_of(c, e, n);
-            for (uint32_t i = 0; i < n; ++i) {
-                const uint64_t v = __ldg(e + i);
-                const int32_t y = static_cast<int32_t>(entry_y(v));
-                if (y < ybase || y >= ybase + 32)
-                    continue;
-                if (i + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + i + 1))) == y)
-                    continue;
-                const uint8_t b = entry_block(v);
-                const uint32_t bit = 1u << (y - ybase);
-                open = is_opaque(b) ? (open & ~bit) : (open | bit);
-                if (source == 0 && b == Torch)
-                    src |= bit;
-            }
+            if ((s.ovr[c] & (kOvrInline | kCntSat)) != 0u)
+                for_each_winner(c, ybase, ybase + 31, [&](int32_t y, uint8_t b) {
+                    const uint32_t bit = 1u << (y - ybase);
+                    open = is_opaque(b) ? (open & ~bit) : (open | bit);
+                    if (source == 0 && b == Torch)
+                        src |= bit;
+                });
         } else {
             const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
             uint32_t t;
@@ -562,16 +579,8 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                     *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
                 // Winning overrides (latest of each y) replace the terrain bytes.
-                const uint64_t* obeg;
-                uint32_t ocnt;
-                overrides_of(c0, obeg, ocnt);
-                for (uint32_t i = 0; i < ocnt; ++i) {
-                    const uint64_t v = __ldg(obeg + i);
-                    const int32_t y = static_cast<int32_t>(entry_y(v));
-                    if (i + 1 < ocnt && static_cast<int32_t>(entry_y(__ldg(obeg + i + 1))) == y)
-                        continue;
-                    my[y] = entry_block(v);
-                }
+                if ((s.ovr[c0] & (kOvrInline | kCntSat)) != 0u)
+                    for_each_winner(c0, 0, H - 1, [&](int32_t y, uint8_t b) { my[y] = b; });
             }
             __syncwarp();
             if (z0 + warp < a.D)
@@ -1083,7 +1092,10 @@ __global__ void column_summary_kernel(const int16_t* terrain_top, const uint32_t
         }
         uint4 r;
         r.x = static_cast<uint32_t>(static_cast<uint16_t>(top)) | (static_cast<uint32_t>(static_cast<uint16_t>(topf)) << 16);
-        r.y = (beg << 5) | (n < kCntSat ? n : kCntSat);
+        // A single override (a torch, mostly) is stored inline: its cell needs no
+        // entry load later.
+        r.y = n == 1 ? kOvrInline | (entry_y(entries[beg]) << 8) | entry_block(entries[beg])
+                     : (beg << 5) | (n < kCntSat ? n : kCntSat);
         r.z = tlo <= thi ? static_cast<uint32_t>(static_cast<uint16_t>(tlo)) | (static_cast<uint32_t>(thi) << 16) : kEmpty;
         r.w = dlo <= dhi ? static_cast<uint32_t>(static_cast<uint16_t>(dlo)) | (static_cast<uint32_t>(dhi) << 16) : kEmpty;
         out[col] = r;

@@ -81,7 +81,7 @@ typedef struct blk_world_config {
     int32_t terrain_mode;   /* blk_terrain_mode */
     int32_t fbm_base;
     float fbm_amplitude;
-    uint32_t max_overrides; /* capacity of one blk_generate override list */
+    uint32_t max_overrides; /* capacity of one blk_generate override list, at most 2^26 */
     uint32_t max_edits;     /* capacity of one blk_apply_edits list */
 } blk_world_config;
 
