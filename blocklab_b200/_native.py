@@ -116,6 +116,7 @@ SIGNATURES = {
     "blk_render_params_at": (None, [ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                     _U32, _VP]),
     "blk_render_frames": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _UP]),
+    "blk_generate_envs": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _U32, _UP]),
 }
 
 

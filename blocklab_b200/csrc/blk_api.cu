@@ -13,7 +13,6 @@
 
 namespace blk {
 
-int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream);
 
 namespace {
 thread_local std::string g_last_error;
@@ -124,6 +123,7 @@ struct RegionDims {
     int32_t ox, oy, oz;
     int32_t W, H, D;
     uint32_t num_envs;
+    const uint8_t* env_mask; // override kernels: only envs set here (nullptr = all)
 };
 
 __device__ inline bool local_cell(const RegionDims& r, const blk_override& o, int32_t& x, int32_t& y, int32_t& z)
@@ -131,7 +131,8 @@ __device__ inline bool local_cell(const RegionDims& r, const blk_override& o, in
     x = o.x - r.ox;
     y = o.y - r.oy;
     z = o.z - r.oz;
-    return o.env < r.num_envs && x >= 0 && y >= 0 && z >= 0 && x < r.W && y < r.H && z < r.D && o.block <= Torch;
+    return o.env < r.num_envs && (!r.env_mask || r.env_mask[o.env]) && x >= 0 && y >= 0 && z >= 0 && x < r.W
+        && y < r.H && z < r.D && o.block <= Torch;
 }
 
 __global__ void ovr_count_kernel(const blk_override* ovr, uint32_t n, RegionDims r, uint32_t* col_count)
@@ -549,6 +550,31 @@ __global__ void __launch_bounds__(1024) row_scan_one_block(const uint32_t* in, u
         }
 }
 
+// ---------------------------------------------------------- partial reset --
+// Marks the listed envs, installs their seeds and lists their tiles
+// (0xFFFFFFFF for an out-of-range env id, which also raises a flag).
+__global__ void env_select_kernel(const uint32_t* env_ids, const uint32_t* seeds, uint32_t n, uint32_t num_envs,
+    uint32_t tiles_per_env, uint8_t* mask, uint32_t* env_seeds, uint32_t* tile_list, uint32_t* flags)
+{
+    const uint64_t total = static_cast<uint64_t>(n) * tiles_per_env;
+    for (uint64_t k = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; k < total;
+         k += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t i = static_cast<uint32_t>(k / tiles_per_env), t = static_cast<uint32_t>(k % tiles_per_env);
+        const uint32_t e = env_ids[i];
+        if (e >= num_envs) {
+            tile_list[k] = 0xFFFFFFFFu;
+            if (t == 0)
+                atomicOr(flags, kFlagEnvIndex);
+            continue;
+        }
+        tile_list[k] = e * tiles_per_env + t;
+        if (t == 0) {
+            mask[e] = 1;
+            env_seeds[e] = seeds[i];
+        }
+    }
+}
+
 // ---------------------------------------------------------- sparse queries --
 __global__ void query_cells_kernel(const blk_cell_query* q, uint32_t n, const uint8_t* ids, const uint8_t* light,
     const int16_t* hmap, RegionDims r, uint64_t env_stride, uint8_t* out_block, uint8_t* out_light,
@@ -693,6 +719,7 @@ RegionDims region(const blk_ctx* ctx)
     r.H = static_cast<int32_t>(ctx->cfg.height);
     r.D = static_cast<int32_t>(ctx->cfg.depth);
     r.num_envs = ctx->cfg.num_envs;
+    r.env_mask = nullptr;
     return r;
 }
 
@@ -844,6 +871,9 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->box_count, 1, "relight box count"));
     A(dalloc(&ctx->render_params, envs, "render parameters"));
     A(dalloc(&ctx->col_summary, envs * ctx->columns_per_env, "column summaries"));
+    A(dalloc(&ctx->env_mask, envs, "partial reset env mask"));
+    A(dalloc(&ctx->env_list, envs, "partial reset env ids"));
+    A(dalloc(&ctx->seed_list, envs, "partial reset seeds"));
     A(dalloc(&ctx->flags, 1, "flags"));
     {
         int sms = 148;
@@ -896,7 +926,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
             cudaEventDestroy(ev);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->col_summary, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -971,6 +1001,62 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
     BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_tiles), st));
     prof_mark(ctx, mark, 2, st);
     ctx->generated = true;
+    return BLK_OK;
+}
+
+int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, const uint32_t* env_seeds,
+    const blk_override* overrides, uint32_t n_overrides, uintptr_t stream_handle)
+{
+    if (!ctx || (n_envs && (!env_ids || !env_seeds)) || (n_overrides && !overrides)) {
+        set_error("blk_generate_envs: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!ctx->generated) {
+        set_error("blk_generate_envs: call blk_generate first");
+        return BLK_ERR_NOT_READY;
+    }
+    if (n_envs > ctx->cfg.num_envs || n_overrides > ctx->cfg.max_overrides) {
+        set_error("blk_generate_envs: more envs or overrides than the context holds");
+        return BLK_ERR_CAPACITY;
+    }
+    if (n_envs == 0)
+        return BLK_OK;
+    cudaStream_t st = as_stream(stream_handle);
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t envs = ctx->cfg.num_envs;
+    const void *ids_dev = nullptr, *seeds_dev = nullptr, *ovr_dev = nullptr;
+    BLK_CHECK(stage_input(env_ids, n_envs * sizeof(uint32_t), ctx->env_list, st, &ids_dev));
+    BLK_CHECK(stage_input(env_seeds, n_envs * sizeof(uint32_t), ctx->seed_list, st, &seeds_dev));
+    BLK_CHECK(stage_input(overrides, static_cast<size_t>(n_overrides) * sizeof(blk_override), ctx->ovr, st, &ovr_dev));
+    const auto* ovr = static_cast<const blk_override*>(ovr_dev);
+    const uint32_t tiles_per_env = ctx->tiles_x * ctx->tiles_z;
+    const uint64_t n_items = static_cast<uint64_t>(n_envs) * tiles_per_env;
+    BLK_CUDA(cudaMemsetAsync(ctx->env_mask, 0, envs, st), "memset env mask");
+    env_select_kernel<<<grid_for(n_items, 256), 256, 0, st>>>(static_cast<const uint32_t*>(ids_dev),
+        static_cast<const uint32_t*>(seeds_dev), n_envs, ctx->cfg.num_envs, tiles_per_env, ctx->env_mask, ctx->seeds,
+        ctx->dirty_list, ctx->flags);
+    BLK_CUDA(cudaGetLastError(), "env select launch");
+    RegionDims r = region(ctx);
+    r.env_mask = ctx->env_mask;
+    const uint64_t n_cols = envs * ctx->columns_per_env;
+    const int mark = prof_begin(ctx, 0, st);
+    BLK_CHECK(launch_terrain(ctx, st, ctx->env_mask));
+    BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
+    if (n_overrides)
+        ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
+    BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, n_cols + 1, st));
+    if (n_overrides) {
+        BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset cursors");
+        ovr_scatter_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset,
+            ctx->col_count, ctx->entries, ctx->ovr_owner);
+        ovr_sort_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset, ctx->entries,
+            ctx->ovr_owner);
+        BLK_CUDA(cudaGetLastError(), "override kernels");
+    }
+    BLK_CHECK(launch_column_summary(ctx, st, ctx->env_mask));
+    prof_mark(ctx, mark, 1, st);
+    BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_items), st, true));
+    prof_mark(ctx, mark, 2, st);
     return BLK_OK;
 }
 
@@ -1353,6 +1439,8 @@ int blk_sync(blk_ctx* ctx, uintptr_t stream_handle)
             msg += " edit bookkeeping overflow";
         if (f & kFlagPermuteGuard)
             msg += " permutation guard hit";
+        if (f & kFlagEnvIndex)
+            msg += " partial reset env index out of range";
         set_error(msg);
         return BLK_ERR_DEVICE_FLAG;
     }

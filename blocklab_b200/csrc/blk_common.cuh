@@ -21,6 +21,7 @@ enum : uint32_t {
     kFlagBandTooWide = 1u << 1,    // light band wider than the compiled maximum
     kFlagEditOverflow = 1u << 2,   // changed-cell list of an edit batch overflowed
     kFlagPermuteGuard = 1u << 3,   // permutation walk hit its iteration bound
+    kFlagEnvIndex = 1u << 4,       // an env index of a partial reset is out of range
 };
 
 // src/utility/Hash.h:10-24

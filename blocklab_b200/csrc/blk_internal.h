@@ -34,6 +34,9 @@ struct blk_ctx {
     uint64_t* entries = nullptr;      // [max_overrides], key y<<40 | order<<8 | block
     uint8_t* ovr_owner = nullptr;     // [max_overrides], 1 for the override owning its column segment
     uint4* col_summary = nullptr;     // [env * columns] generation column summaries (see column_summary_kernel)
+    uint8_t* env_mask = nullptr;      // [num_envs] envs of a partial reset
+    uint32_t* env_list = nullptr;     // [num_envs] staging of a partial reset's env ids
+    uint32_t* seed_list = nullptr;    // [num_envs] staging of a partial reset's seeds
     uint32_t* scan_partials = nullptr;
     uint64_t scan_blocks = 0;
 
@@ -79,8 +82,11 @@ int stage_input(const void* src, size_t bytes, void* staging, cudaStream_t strea
 TerrainParams terrain_params(const blk_ctx* ctx);
 
 int launch_relight(blk_ctx* ctx, cudaStream_t stream);
-int launch_terrain(blk_ctx* ctx, cudaStream_t stream);
-int launch_column_summary(blk_ctx* ctx, cudaStream_t stream);
+// env_mask (device, one byte per env) restricts the work to the envs set in it; nullptr = all.
+int launch_terrain(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask = nullptr);
+int launch_column_summary(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask = nullptr);
+// Mode 0 over a tile list (ctx->dirty_list, n_tiles entries, 0xFFFFFFFF = skip) when `listed`.
+int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed = false);
 int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,
     cudaStream_t stream);
 void halo_order_table(uint16_t* out);

@@ -77,6 +77,7 @@ struct TileArgs {
     uint64_t env_stride;
     uint64_t columns;
     int32_t mode; // 0 = generate, 1 = relight dirty tiles or boxes from the resident ids
+    int32_t listed; // mode 0: tiles from dirty_list (0xFFFFFFFF = skip) instead of all
 };
 
 template <int NW>
@@ -852,7 +853,9 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
             z0 = static_cast<int>(b.y >> 16);
             win = b.z;
         } else {
-            const uint32_t tile_id = a.mode == 0 ? i : a.dirty_list[i];
+            const uint32_t tile_id = a.mode == 0 && !a.listed ? i : a.dirty_list[i];
+            if (tile_id == 0xFFFFFFFFu)
+                continue; // uniform over the CTA
             env = tile_id / tiles_per_env;
             const uint32_t t_in_env = tile_id % tiles_per_env;
             x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
@@ -872,12 +875,14 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
 // Terrain surface of every column of every env (local y, clamped to
 // [-1, H+4], which preserves the layer rule inside the region).
 __global__ void terrain_kernel(const uint32_t* seeds, TerrainParams t, int32_t W, int32_t D, uint64_t total,
-    int16_t* out)
+    const uint8_t* env_mask, int16_t* out)
 {
     const uint64_t columns = static_cast<uint64_t>(W) * D;
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const uint32_t env = static_cast<uint32_t>(i / columns);
+        if (env_mask && !env_mask[env])
+            continue;
         const uint64_t col = i - env * columns;
         const int32_t x = static_cast<int32_t>(col % W), z = static_cast<int32_t>(col / W);
         int32_t top = terrain_top_local(t, seeds[env], t.origin_x + x, t.origin_z + z);
@@ -892,7 +897,7 @@ __global__ void terrain_kernel(const uint32_t* seeds, TerrainParams t, int32_t W
 // of four times per column; the per-column arithmetic is fbm()'s.
 constexpr int kFbmBlock = 64;
 __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds, TerrainParams t, int32_t W,
-    int32_t D, uint32_t num_envs, int16_t* out)
+    int32_t D, uint32_t num_envs, const uint8_t* env_mask, int16_t* out)
 {
     __shared__ float lat[4][100];
     __shared__ int32_t lat_ix[4], lat_iz[4], lat_nx[4], lat_nz[4];
@@ -912,6 +917,8 @@ __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds,
         lat_nz[o] = k1 - k0 + 2;
     }
     for (uint32_t env = blockIdx.z; env < num_envs; env += gridDim.z) {
+        if (env_mask && !env_mask[env])
+            continue; // uniform over the block
         const uint32_t seed = seeds[env];
         __syncthreads();
 #pragma unroll
@@ -1031,11 +1038,13 @@ int halo_order_size() { return kHaloCols; }
 // z = torch rows min | max << 16, w = rows of open cells under the final top
 // min | max << 16 (empty ranges as 32767 | -32768 << 16).
 __global__ void column_summary_kernel(const int16_t* terrain_top, const uint32_t* col_offset, const uint64_t* entries,
-    int32_t H, uint64_t total, uint4* out)
+    int32_t H, uint64_t total, uint64_t columns, const uint8_t* env_mask, uint4* out)
 {
     constexpr uint32_t kEmpty = 0x7FFFu | (0x8000u << 16);
     for (uint64_t col = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; col < total;
          col += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        if (env_mask && !env_mask[col / columns])
+            continue;
         const int32_t top = terrain_top[col];
         const int32_t tc = min(top, H - 1);
         const uint32_t beg = col_offset[col];
@@ -1102,24 +1111,24 @@ __global__ void column_summary_kernel(const int16_t* terrain_top, const uint32_t
     }
 }
 
-int launch_column_summary(blk_ctx* ctx, cudaStream_t stream)
+int launch_column_summary(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
 {
     const uint64_t total = static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->columns_per_env;
     uint64_t blocks = (total + 255) / 256;
     if (blocks > 148ull * 32)
         blocks = 148ull * 32;
     column_summary_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ctx->terrain_top, ctx->col_offset,
-        ctx->entries, static_cast<int32_t>(ctx->cfg.height), total, ctx->col_summary);
+        ctx->entries, static_cast<int32_t>(ctx->cfg.height), total, ctx->columns_per_env, env_mask, ctx->col_summary);
     return cuda_fail(cudaGetLastError(), "column_summary_kernel launch");
 }
 
-int launch_terrain(blk_ctx* ctx, cudaStream_t stream)
+int launch_terrain(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
 {
     if (ctx->cfg.terrain_mode == BLK_TERRAIN_FBM) {
         const dim3 grid((ctx->cfg.width + kFbmBlock - 1) / kFbmBlock, (ctx->cfg.depth + kFbmBlock - 1) / kFbmBlock,
             std::min<uint32_t>(ctx->cfg.num_envs, 65535));
         terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
-            static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), ctx->cfg.num_envs,
+            static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), ctx->cfg.num_envs, env_mask,
             ctx->terrain_top);
         return cuda_fail(cudaGetLastError(), "terrain_fbm_kernel launch");
     }
@@ -1128,11 +1137,11 @@ int launch_terrain(blk_ctx* ctx, cudaStream_t stream)
     if (blocks > 148ull * 32)
         blocks = 148ull * 32;
     terrain_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
-        static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), total, ctx->terrain_top);
+        static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), total, env_mask, ctx->terrain_top);
     return cuda_fail(cudaGetLastError(), "terrain_kernel launch");
 }
 
-int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream)
+int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed)
 {
     TileArgs a {};
     a.ids = ctx->ids;
@@ -1160,6 +1169,7 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream)
     a.env_stride = ctx->env_stride;
     a.columns = ctx->columns_per_env;
     a.mode = mode;
+    a.listed = listed ? 1 : 0;
     switch (ctx->cfg.height / 32) {
     case 1:
         return launch_nw<1>(ctx, a, n_tiles, stream);

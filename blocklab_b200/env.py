@@ -1,8 +1,9 @@
 """World-state environment batch: the reset / step surface of the reference's
 BlockLabEnv (python/blocklab/env.py:155-194) restricted to the world-state
-path. The renderer, agent and rewards are not part of this library: `step`
-takes the caller's edits (dig / place / torch) and, optionally, the rendered
-RGBA8 frames, and returns the float32 NCHW observation.
+path. The agent and rewards are not part of this library: `step` takes the
+caller's edits (dig / place / torch) and, optionally, rendered RGBA8 frames,
+and returns the float32 NCHW observation; `render` produces the observation
+from the library's own ray-cast frames of the worlds.
 
 Observations are double-buffered device tensors, valid until the next call
 after the following one (the reference's renderer double-buffers them the
@@ -65,6 +66,20 @@ class WorldEnv:
         self._reset_done = True
         obs = self._next_obs(frames)
         return obs, {"observation_version": self._version, "env_begin": self.env_begin}
+
+    def reset_envs(self, env_ids, *, seed: int = 1, overrides=None):
+        """Regenerates only the listed worlds (indices local to this process);
+        world i gets the seed of its global index, as in reset()."""
+        ids = np.asarray(env_ids, np.int64)
+        seeds = np.array([env_seeds(seed, self.env_begin + int(i), 1, self.seed_policy)[0] for i in ids], np.uint32)
+        self.world.generate_envs(ids.astype(np.uint32), seeds, overrides)
+
+    def render(self, params) -> torch.Tensor:
+        """Observation rendered by the library itself: ray-cast RGBA8 frames of
+        every owned world from per-env render parameters (render_params_at),
+        converted to float32 NCHW."""
+        frames = self.world.render(params, self.width, self.height)
+        return self._next_obs(frames)
 
     def step(self, edits=None, frames: Optional[torch.Tensor] = None):
         """Applies edits (World::setBlock semantics, exact relight) and converts

@@ -137,6 +137,27 @@ class WorldBatch:
         check(N.lib.blk_generate(self._ctx, seeds_p, ovr_p, n, _stream_handle(stream, self.device)))
         del keep1, keep2
 
+    def generate_envs(self, env_ids, env_seeds, overrides=None, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Regenerates only the listed envs (distinct indices) with their seeds and
+        overrides; the other envs keep their state."""
+        ids_p, keep1 = _ptr(np.asarray(env_ids, np.uint32) if not isinstance(env_ids, torch.Tensor) else env_ids)
+        seeds_p, keep2 = _ptr(np.asarray(env_seeds, np.uint32) if not isinstance(env_seeds, torch.Tensor)
+                              else env_seeds)
+        n_envs = len(env_ids)
+        if len(env_seeds) != n_envs:
+            raise ValueError("one seed per listed env")
+        if overrides is None:
+            ovr_p, n, keep3 = 0, 0, None
+        elif isinstance(overrides, torch.Tensor):
+            ovr_p, keep3 = _ptr(overrides)
+            n = overrides.numel() * overrides.element_size() // 16
+        else:
+            arr = np.ascontiguousarray(overrides, OVERRIDE_DTYPE)
+            ovr_p, keep3 = _ptr(arr)
+            n = len(arr)
+        check(N.lib.blk_generate_envs(self._ctx, ids_p, n_envs, seeds_p, ovr_p, n, _stream_handle(stream, self.device)))
+        del keep1, keep2, keep3
+
     def place_torches(self, env_seeds, per_env: int, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """Device override list of `per_env` torches per env on the terrain surface."""
         n = self.config.num_envs * per_env

@@ -126,6 +126,15 @@ int blk_views(blk_ctx* ctx, blk_world_views* out);
 int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* overrides, uint32_t n_overrides,
     uintptr_t stream);
 
+/* Regenerates and relights only the envs listed in env_ids[n_envs] (distinct
+ * indices; out-of-range ones are skipped and reported by blk_sync), with
+ * seeds env_seeds[n_envs] and the overrides of those envs (records of other
+ * envs are ignored); every other env keeps its state. The batched per-env
+ * reset the reference leaves for later (include/blocklab/environment/Environment.h:33);
+ * requires a prior blk_generate. Arrays may be host or device memory. */
+int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, const uint32_t* env_seeds,
+    const blk_override* overrides, uint32_t n_overrides, uintptr_t stream);
+
 /* Writes up to `per_env` torch overrides per env at distinct pseudo-random
  * columns, one cell above the terrain surface (benchmark world construction).
  * `out` is device memory of num_envs*per_env entries; *out_count (device)

@@ -113,3 +113,68 @@ def test_observation_buffers_and_dlpack(B):
     with pytest.raises(ValueError):
         env.step(frames=torch.zeros((3, 24, 31, 4), dtype=torch.uint8, device="cuda"))
     env.close()
+
+
+def test_partial_reset_matches_full_generation(B):
+    W2, H2, D2, E2 = 70, 64, 50, 4
+    cfg = B.WorldConfig(num_envs=E2, width=W2, height=H2, depth=D2, origin=(3, 0, -9), terrain=TERRAIN_FBM, base=25,
+                        amplitude=15.0)
+    rng = np.random.default_rng(9)
+    seeds = np.array([11, 12, 13, 14], np.uint32)
+    new = np.array([101, 103], np.uint32)
+
+    def overrides(envs):
+        out = []
+        for e in envs:
+            cells = rng.choice(W2 * H2 * D2, 300, replace=False)
+            xyz = np.stack([cells % W2, (cells // W2) % H2, cells // (W2 * H2)], 1) + np.array([3, 0, -9])
+            out.append(B.make_overrides(xyz, rng.choice([0, 3, 4], 300).astype(np.uint8), env=e))
+        return np.concatenate(out)
+
+    first = overrides(range(E2))
+    partial = overrides([0, 1, 3])  # env 0's records must be ignored
+    wb = B.WorldBatch(cfg)
+    wb.generate(seeds, first)
+    before = (wb.ids.clone(), wb.light.clone(), wb.height_map.clone())
+    wb.generate_envs([1, 3], new, partial)
+    wb.sync()
+    # reference: a full generation with the new seeds and the partial overrides for envs 1, 3
+    full_seeds = seeds.copy()
+    full_seeds[[1, 3]] = new
+    keep = partial[partial["env"] != 0]
+    ref = B.WorldBatch(cfg)
+    ref.generate(full_seeds, np.concatenate([first[np.isin(first["env"], [0, 2])], keep]))
+    ref.sync()
+    for e in (1, 3):
+        assert torch.equal(wb.ids[e], ref.ids[e]) and torch.equal(wb.light[e], ref.light[e])
+        assert torch.equal(wb.height_map[e], ref.height_map[e])
+    for e in (0, 2):
+        assert torch.equal(wb.ids[e], before[0][e]) and torch.equal(wb.light[e], before[1][e])
+        assert torch.equal(wb.height_map[e], before[2][e])
+    # edits and relight still work after a partial reset
+    hm = wb.height_map.cpu().numpy()
+    ed = B.make_overrides([[3 + 5, int(hm[1, 4, 5]), -9 + 4]], B.AIR, env=1)
+    wb.apply_edits(ed)
+    ref.apply_edits(ed)
+    wb.sync()
+    ref.sync()
+    assert torch.equal(wb.light, torch.cat([before[1][0:1], ref.light[1:2], before[1][2:3], ref.light[3:4]]))
+    # an env index out of range is reported by sync
+    wb.generate_envs([1, 9], [5, 6])
+    with pytest.raises(B.BlkError):
+        wb.sync()
+    wb.close()
+    ref.close()
+
+
+def test_env_renders_its_observations(B):
+    env = _env(B)
+    env.reset(seed=4)
+    params = np.array([B.render_params_at((-10 + 3 * e, 45, -5), 0.5 * e, -0.4, 3000) for e in range(3)],
+                      B.RENDER_PARAMS_DTYPE)
+    obs = env.render(params)
+    frames = env.world.render(params, 32, 24)
+    torch.cuda.synchronize()
+    assert obs.shape == (3, 3, 24, 32)
+    assert torch.equal(obs[:, 1], frames[..., 1].float() * np.float32(1.0 / 255.0))
+    env.close()
