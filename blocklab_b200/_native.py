@@ -117,6 +117,7 @@ SIGNATURES = {
                                     _U32, _VP]),
     "blk_render_frames": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _UP]),
     "blk_generate_envs": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _U32, _UP]),
+    "blk_render_observations": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _VP, _UP]),
 }
 
 

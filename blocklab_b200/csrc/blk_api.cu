@@ -1297,26 +1297,42 @@ void blk_render_params_at(float x, float y, float z, float yaw, float pitch, uin
     *out = p;
 }
 
-int blk_render_frames(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
-    uint8_t* out_rgba, uintptr_t stream_handle)
+static int render_common(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
+    uint8_t* out_rgba, float* out_nchw, uintptr_t stream_handle, const char* name)
 {
-    if (!ctx || !params || !out_rgba || width == 0 || height == 0 || width > 8192 || height > 8192) {
-        set_error("blk_render_frames: invalid argument");
+    if (!ctx || !params || (!out_rgba && !out_nchw) || width == 0 || height == 0 || width > 8192 || height > 8192) {
+        set_error(std::string(name) + ": invalid argument");
         return BLK_ERR_INVALID_ARGUMENT;
     }
     if (!ctx->generated) {
-        set_error("blk_render_frames: call blk_generate first");
+        set_error(std::string(name) + ": call blk_generate first");
         return BLK_ERR_NOT_READY;
     }
     BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    if (!device_memory(out_rgba)) {
-        set_error("blk_render_frames: out_rgba must be device memory");
+    if ((out_rgba && !device_memory(out_rgba)) || (out_nchw && !device_memory(out_nchw))) {
+        set_error(std::string(name) + ": outputs must be device memory");
         return BLK_ERR_INVALID_ARGUMENT;
     }
     cudaStream_t st = as_stream(stream_handle);
     const void* p = nullptr;
     BLK_CHECK(stage_input(params, sizeof(blk_render_params) * ctx->cfg.num_envs, ctx->render_params, st, &p));
-    return launch_render(ctx, static_cast<const blk_render_params*>(p), width, height, out_rgba, st);
+    return launch_render(ctx, static_cast<const blk_render_params*>(p), width, height, out_rgba, out_nchw, st);
+}
+
+int blk_render_frames(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
+    uint8_t* out_rgba, uintptr_t stream_handle)
+{
+    return render_common(ctx, params, width, height, out_rgba, nullptr, stream_handle, "blk_render_frames");
+}
+
+int blk_render_observations(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
+    float* out_nchw, uint8_t* out_rgba, uintptr_t stream_handle)
+{
+    if (!out_nchw) {
+        set_error("blk_render_observations: null observation tensor");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    return render_common(ctx, params, width, height, out_rgba, out_nchw, stream_handle, "blk_render_observations");
 }
 
 int blk_readback(blk_ctx* ctx, uint32_t env_begin, uint32_t n_envs, uint8_t* ids, uint8_t* light, int16_t* height_map,

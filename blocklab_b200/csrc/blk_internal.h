@@ -88,7 +88,7 @@ int launch_column_summary(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_
 // Mode 0 over a tile list (ctx->dirty_list, n_tiles entries, 0xFFFFFFFF = skip) when `listed`.
 int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed = false);
 int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,
-    cudaStream_t stream);
+    float* out_nchw, cudaStream_t stream);
 void halo_order_table(uint16_t* out);
 int halo_order_size();
 

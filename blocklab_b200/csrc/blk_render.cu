@@ -28,7 +28,8 @@ struct RenderArgs {
     int32_t ox, oy, oz;
     uint64_t env_stride;
     uint32_t width, height, num_envs;
-    uint8_t* out;
+    uint8_t* out;     // RGBA8 (env, y, x, 4), or nullptr
+    float* out_nchw;  // float32 (env, 3, y, x) = RGBA8 channel * (1 / 255), or nullptr
 };
 
 // Faces in the reference's order: left, right, top, bottom, front, back
@@ -424,14 +425,25 @@ __global__ void __launch_bounds__(128) render_kernel(RenderArgs a)
         g = lerp_(saturate_(ag * light), p.sky_color[1], fog);
         b = lerp_(saturate_(ab * light), p.sky_color[2], fog);
     }
-    const uint32_t rgba = to_srgb8(r) | (to_srgb8(g) << 8) | (to_srgb8(b) << 16) | (255u << 24);
-    reinterpret_cast<uint32_t*>(a.out)[(static_cast<uint64_t>(env) * a.height + py) * a.width + px] = rgba;
+    const uint32_t cr = to_srgb8(r), cg = to_srgb8(g), cb = to_srgb8(b);
+    if (a.out)
+        reinterpret_cast<uint32_t*>(a.out)[(static_cast<uint64_t>(env) * a.height + py) * a.width + px]
+            = cr | (cg << 8) | (cb << 16) | (255u << 24);
+    if (a.out_nchw) {
+        // The observation conversion of the same bytes (src/environment/CudaObservation.cu:13-31).
+        const uint64_t plane = static_cast<uint64_t>(a.width) * a.height;
+        float* o = a.out_nchw + static_cast<uint64_t>(env) * 3 * plane + static_cast<uint64_t>(py) * a.width + px;
+        const float k = 1.0f / 255.0f;
+        o[0] = __fmul_rn(static_cast<float>(cr), k);
+        o[plane] = __fmul_rn(static_cast<float>(cg), k);
+        o[2 * plane] = __fmul_rn(static_cast<float>(cb), k);
+    }
 }
 
 } // namespace
 
 int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,
-    cudaStream_t stream)
+    float* out_nchw, cudaStream_t stream)
 {
     RenderArgs a;
     a.ids = ctx->ids;
@@ -448,6 +460,7 @@ int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width,
     a.height = height;
     a.num_envs = ctx->cfg.num_envs;
     a.out = out;
+    a.out_nchw = out_nchw;
     const dim3 grid((width * height + 127) / 128, ctx->cfg.num_envs);
     render_kernel<<<grid, 128, 0, stream>>>(a);
     return cuda_fail(cudaGetLastError(), "render_kernel launch");

@@ -78,8 +78,11 @@ class WorldEnv:
         """Observation rendered by the library itself: ray-cast RGBA8 frames of
         every owned world from per-env render parameters (render_params_at),
         converted to float32 NCHW."""
-        frames = self.world.render(params, self.width, self.height)
-        return self._next_obs(frames)
+        out = self._obs[self._flip]
+        self._flip ^= 1
+        self.world.render_observations(params, self.width, self.height, out=out)
+        self._version += 1
+        return out
 
     def step(self, edits=None, frames: Optional[torch.Tensor] = None):
         """Applies edits (World::setBlock semantics, exact relight) and converts

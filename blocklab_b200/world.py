@@ -239,6 +239,20 @@ class WorldBatch:
                                       _stream_handle(stream, self.device)))
         return out
 
+    def render_observations(self, params, width: int, height: int, out: Optional[torch.Tensor] = None,
+                            stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """Rendered frames written straight into a float32 (num_envs, 3, height,
+        width) observation tensor (equal to converting the RGBA8 frames)."""
+        params = np.ascontiguousarray(params, RENDER_PARAMS_DTYPE).reshape(-1)
+        if len(params) != self.config.num_envs:
+            raise ValueError("one render parameter record per env")
+        if out is None:
+            out = torch.empty((self.config.num_envs, 3, height, width), dtype=torch.float32,
+                              device=torch.device("cuda", self.device))
+        check(N.lib.blk_render_observations(self._ctx, params.ctypes.data, width, height, out.data_ptr(), None,
+                                            _stream_handle(stream, self.device)))
+        return out
+
     def snapshot(self, env: int, stream: Optional[torch.cuda.Stream] = None) -> np.ndarray:
         """Overlay of one env: the cells that differ from its terrain, as
         override records in (z, x, y) order; generate(seed, snapshot) rebuilds it."""

@@ -257,6 +257,14 @@ void blk_render_params_at(float x, float y, float z, float yaw, float pitch, uin
 int blk_render_frames(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
     uint8_t* out_rgba, uintptr_t stream);
 
+/* The same frames written straight into the float32 NCHW observation tensor
+ * (num_envs, 3, height, width), equal to blk_convert_rgba8_to_float_nchw of
+ * the RGBA8 frames (src/environment/CudaObservation.cu:13-44) without the
+ * round trip through them; `out_rgba` may also be given (else NULL). Both are
+ * device memory. */
+int blk_render_observations(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height,
+    float* out_nchw, uint8_t* out_rgba, uintptr_t stream);
+
 /* Copies env range [env_begin, env_begin + n_envs) of the world arrays to
  * caller memory in the device layout (any of the outputs may be NULL).
  * Replaces the per-generation cache readback (src/world/WorldGenerator.cu:798-815). */

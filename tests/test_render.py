@@ -135,3 +135,22 @@ def test_render_then_convert_pipeline():
     with pytest.raises(ValueError):
         wb.render(params[:1], 84, 84)
     wb.close()
+
+
+@pytest.mark.gpu
+def test_render_observations_equal_converted_frames():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import blocklab_b200 as B
+
+    cfg = B.WorldConfig(num_envs=3, width=64, height=64, depth=64, origin=(-32, 0, -32))
+    wb = B.WorldBatch(cfg)
+    wb.generate([7, 8, 9], wb.place_torches([7, 8, 9], 60))
+    params = np.array([B.render_params_at((e - 3.0, 44, 2.0), 1.1 * e, -0.35, 9000 * e) for e in range(3)],
+                      B.RENDER_PARAMS_DTYPE)
+    frames = wb.render(params, 96, 72)
+    want = B.convert_rgba8_to_float_nchw(frames)
+    got = wb.render_observations(params, 96, 72)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+    wb.close()
