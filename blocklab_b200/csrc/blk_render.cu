@@ -223,7 +223,9 @@ __global__ void __launch_bounds__(128) render_kernel(RenderArgs a)
     const float o[3] = { p.origin[0] - a.ox, p.origin[1] - a.oy, p.origin[2] - a.oz };
     const int dims[3] = { a.W, a.H, a.D };
     constexpr float kNear = 0.05f;
-    const float far = p.far_plane;
+    // Past the fog end a face takes the sky colour (fog factor 1), which is
+    // also the colour of an empty pixel: the walk stops there.
+    const float far = p.fog_end > p.fog_start ? fminf(p.far_plane, p.fog_end) : p.far_plane;
 
     // Parameter range of the ray inside the region box, and the axis whose
     // boundary it enters through when the camera is outside.

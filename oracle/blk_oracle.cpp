@@ -662,6 +662,8 @@ extern "C" void orc_render_frame(uint32_t W, uint32_t H, uint32_t D, int32_t ox,
     const float o[3] = { p.origin[0] - ox, p.origin[1] - oy, p.origin[2] - oz };
     const int off[6][3] = { { -1, 0, 0 }, { 1, 0, 0 }, { 0, 1, 0 }, { 0, -1, 0 }, { 0, 0, 1 }, { 0, 0, -1 } };
     const float kNear = 0.05f;
+    // The walk stops at the fog end, where faces take the sky colour.
+    const float far = p.fog_end > p.fog_start ? std::fmin(p.far_plane, p.fog_end) : p.far_plane;
     for (uint32_t py = 0; py < height; ++py)
         for (uint32_t px = 0; px < width; ++px) {
             const float xn = (px + 0.5f) / width * 2.0f - 1.0f, yn = (py + 0.5f) / height * 2.0f - 1.0f;
@@ -669,7 +671,7 @@ extern "C" void orc_render_frame(uint32_t W, uint32_t H, uint32_t D, int32_t ox,
             float d[3];
             for (int k = 0; k < 3; ++k)
                 d[k] = p.right[k] * vx + p.up[k] * vy + p.forward[k];
-            float s0 = 0.0f, s1 = p.far_plane;
+            float s0 = 0.0f, s1 = far;
             int entry_axis = -1;
             for (int k = 0; k < 3; ++k) {
                 if (std::fabs(d[k]) < 1e-20f) {
@@ -723,7 +725,7 @@ extern "C" void orc_render_frame(uint32_t W, uint32_t H, uint32_t D, int32_t ox,
                     }
                 }
                 float s_cell = s0;
-                if (entry_axis >= 0 && s0 >= kNear && s0 <= p.far_plane && opaque(block(c))) {
+                if (entry_axis >= 0 && s0 >= kNear && s0 <= far && opaque(block(c))) {
                     int out_c[3] = { c[0], c[1], c[2] };
                     out_c[entry_axis] -= st[entry_axis];
                     face_hit(c, out_c, entry_axis, s0);
@@ -768,7 +770,7 @@ extern "C" void orc_render_frame(uint32_t W, uint32_t H, uint32_t D, int32_t ox,
                                 sh = tin, fh = fin;
                             else if (fout >= 0 && fout != kBottom && tout >= lo_s && tout <= s_cross)
                                 sh = tout, fh = fout;
-                            if (fh >= 0 && sh <= p.far_plane) {
+                            if (fh >= 0 && sh <= far) {
                                 hs = sh;
                                 hf = fh;
                                 hb = 4;
@@ -781,7 +783,7 @@ extern "C" void orc_render_frame(uint32_t W, uint32_t H, uint32_t D, int32_t ox,
                             }
                         }
                     }
-                    if (s_cross > s1 + 1e-4f || s_cross > p.far_plane)
+                    if (s_cross > s1 + 1e-4f || s_cross > far)
                         break;
                     int nxt[3] = { c[0], c[1], c[2] };
                     nxt[ax] += st[ax];
