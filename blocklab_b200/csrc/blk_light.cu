@@ -161,33 +161,24 @@ __device__ inline bool in_world(const TileArgs& a, int gx, int gz) { return gx >
 template <int H>
 __device__ inline void id_bits(const uint8_t* column, int ybase, uint32_t& open, uint32_t& torch)
 {
+    // ybase is a multiple of 16 (relight windows start on 16-row chunks), so
+    // the word is exactly the two 16-byte chunks from row ybase.
     open = 0u;
     torch = 0u;
-    const int a0 = ybase & ~15;
-    uint32_t ob[3] = { 0u, 0u, 0u }, tb[3] = { 0u, 0u, 0u };
 #pragma unroll
-    for (int q = 0; q < 3; ++q) {
-        const int r = a0 + 16 * q;
-        if (r < 0 || r >= H)
+    for (int q = 0; q < 2; ++q) {
+        const int r = ybase + 16 * q;
+        if (r >= H)
             continue;
         const uint4 v4 = *reinterpret_cast<const uint4*>(column + r);
         const uint32_t v[4] = { v4.x, v4.y, v4.z, v4.w };
-        uint32_t o16 = 0u, t16 = 0u;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint32_t t = bytes_eq(v[j], Torch);
-            o16 |= pack4(bytes_eq(v[j], Air) | t) << (4 * j);
-            t16 |= pack4(t) << (4 * j);
+            open |= pack4(bytes_eq(v[j], Air) | t) << (16 * q + 4 * j);
+            torch |= pack4(t) << (16 * q + 4 * j);
         }
-        ob[q] = o16;
-        tb[q] = t16;
     }
-    // 48 bits starting at row a0; take 32 starting at row ybase.
-    const int sh = ybase - a0; // 0..15
-    const uint64_t o48 = static_cast<uint64_t>(ob[0]) | (static_cast<uint64_t>(ob[1]) << 16) | (static_cast<uint64_t>(ob[2]) << 32);
-    const uint64_t t48 = static_cast<uint64_t>(tb[0]) | (static_cast<uint64_t>(tb[1]) << 16) | (static_cast<uint64_t>(tb[2]) << 32);
-    open = static_cast<uint32_t>(o48 >> sh);
-    torch = static_cast<uint32_t>(t48 >> sh);
 }
 
 // 14 dilation steps of S over NB band words. Plane O holds the open cells and
