@@ -456,13 +456,16 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     auto build = [&](int blo, int nb, int source) {
         uint32_t* O = s.O();
         uint32_t* B0 = s.B(0);
-        for (int w = 0; w < nb; ++w)
-            for (int c = tid; c < kExtCols; c += kThreads) {
-                uint32_t o, src;
-                column_bits(c, blo + 32 * w, source, o, src);
-                O[w * kExtCols + c] = o;
-                B0[w * kExtCols + c] = src;
-            }
+        for (int c = tid; c < kExtCols; c += kThreads) {
+#pragma unroll
+            for (int w = 0; w < Smem<NW>::kBand; ++w)
+                if (w < nb) {
+                    uint32_t o, src;
+                    column_bits(c, blo + 32 * w, source, o, src);
+                    O[w * kExtCols + c] = o;
+                    B0[w * kExtCols + c] = src;
+                }
+        }
     };
 
     // Plane B0 of the sky flood from an already built plane O: every open cell
