@@ -1,5 +1,6 @@
 // Fused world generation + exact sky/block light for one 32x32-column tile
-// per CTA step, and the same kernel in relight mode over dirty tiles.
+// per CTA step, and the same kernel in relight mode over dirty tiles or over
+// 32x32-column boxes around changed cells.
 //
 // Light model (reference: src/world/WorldGenerator.cu:364-588). The reference
 // runs one breadth-first search per light source over a 29^3 cube and
@@ -30,13 +31,17 @@
 // so that whole warps drop out of later steps. In y only the band of rows that
 // can hold non-trivial light is processed (torch rows +-14 for block light,
 // dark open rows +-14 for sky light), in words that start at the band's first
-// row; every other row has block light 0 and trivial sky light (15 above the
+// row, at most 3 words at a time (taller bands in windows of 64 output rows);
+// every other row has block light 0 and trivial sky light (15 above the
 // height map, 0 at or below it).
 //
-// The kernel is persistent (one CTA per SM walking the tiles) so one tile's
-// output stores drain while the next tile computes, and every warp writes its
-// 32 finished columns (contiguous in memory) with coalesced 16-byte stores
-// from a shared staging area.
+// Per-column inputs of generation (terrain surface, final top, the column's
+// override list or its lone override inline, torch and dark rows) are
+// summarised once per column by column_summary_kernel; a tile reads one
+// 16-byte summary per ext column. The kernel is persistent (one CTA per SM
+// walking the tiles), and every warp writes its 32 finished columns
+// (contiguous in memory) with coalesced 16-byte stores from a shared staging
+// area.
 #include "blk_internal.h"
 
 namespace blk {
