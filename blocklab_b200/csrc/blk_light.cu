@@ -104,12 +104,73 @@ struct Smem {
     int16_t top_f[kExtCols];   // final highest opaque local y, -1 none, -2 outside the world
     uint32_t ovr[kExtCols];    // override list: begin << 5 | min(count, 31)
     int32_t tmin, tmax, dmin, dmax;
+    int32_t omin;              // generation: lowest open row of the ext region (rows below are opaque everywhere)
 
     __device__ uint32_t* O() { return pool; }
     __device__ uint32_t* B(int i) { return pool + (1 + i) * kPlane; }
 };
 
-__device__ inline uint32_t spread4(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
+// Rows r of 32 as 4-bit levels given as bit planes (bit r of p_k = bit k of the
+// level of row r): nibble j of n_k = level of row 4j + k. Pairs bits of even and
+// odd rows, then pairs of pairs (a bit-matrix transpose by masked shifts).
+__device__ inline void level_nibbles(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3, uint32_t& n0, uint32_t& n1,
+    uint32_t& n2, uint32_t& n3)
+{
+    const uint32_t e01 = (p0 & 0x55555555u) | ((p1 << 1) & 0xAAAAAAAAu); // pair i: row 2i, bits 0, 1
+    const uint32_t o01 = ((p0 >> 1) & 0x55555555u) | (p1 & 0xAAAAAAAAu); // pair i: row 2i + 1
+    const uint32_t e23 = (p2 & 0x55555555u) | ((p3 << 1) & 0xAAAAAAAAu);
+    const uint32_t o23 = ((p2 >> 1) & 0x55555555u) | (p3 & 0xAAAAAAAAu);
+    n0 = (e01 & 0x33333333u) | ((e23 << 2) & 0xCCCCCCCCu);
+    n2 = ((e01 >> 2) & 0x33333333u) | (e23 & 0xCCCCCCCCu);
+    n1 = (o01 & 0x33333333u) | ((o23 << 2) & 0xCCCCCCCCu);
+    n3 = ((o01 >> 2) & 0x33333333u) | (o23 & 0xCCCCCCCCu);
+}
+
+// Light bytes of 32 rows (out[q] holds rows 4q .. 4q + 3, one byte each) from
+// the block level bit planes b and either the sky level bit planes s
+// (sky = true) or, for trivial sky light, level 15 above row `topf` (r0 = row
+// of bit 0).
+__device__ inline void light_bytes(const uint32_t (&b)[4], const uint32_t (&s)[4], bool sky, int32_t topf, int32_t r0,
+    uint32_t (&out)[8])
+{
+    uint32_t n[4], l[4], h[4];
+    level_nibbles(b[0], b[1], b[2], b[3], n[0], n[1], n[2], n[3]);
+    if (sky) {
+        uint32_t m[4];
+        level_nibbles(s[0], s[1], s[2], s[3], m[0], m[1], m[2], m[3]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            l[k] = (n[k] & 0x0F0F0F0Fu) | ((m[k] << 4) & 0xF0F0F0F0u);
+            h[k] = ((n[k] >> 4) & 0x0F0F0F0Fu) | (m[k] & 0xF0F0F0F0u);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            l[k] = n[k] & 0x0F0F0F0Fu;        // byte m: row 8m + k
+            h[k] = (n[k] >> 4) & 0x0F0F0F0Fu; // byte m: row 8m + 4 + k
+        }
+    }
+    const uint32_t la = __byte_perm(l[0], l[1], 0x5140), lb = __byte_perm(l[0], l[1], 0x7362);
+    const uint32_t lc = __byte_perm(l[2], l[3], 0x5140), ld = __byte_perm(l[2], l[3], 0x7362);
+    const uint32_t ha = __byte_perm(h[0], h[1], 0x5140), hb = __byte_perm(h[0], h[1], 0x7362);
+    const uint32_t hc = __byte_perm(h[2], h[3], 0x5140), hd = __byte_perm(h[2], h[3], 0x7362);
+    out[0] = __byte_perm(la, lc, 0x5410);
+    out[2] = __byte_perm(la, lc, 0x7632);
+    out[4] = __byte_perm(lb, ld, 0x5410);
+    out[6] = __byte_perm(lb, ld, 0x7632);
+    out[1] = __byte_perm(ha, hc, 0x5410);
+    out[3] = __byte_perm(ha, hc, 0x7632);
+    out[5] = __byte_perm(hb, hd, 0x5410);
+    out[7] = __byte_perm(hb, hd, 0x7632);
+    if (!sky) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            // Rows of this word at or below topf keep sky 0; the shift clamps at 32.
+            const int32_t d = max(topf - (r0 + 4 * q) + 1, 0);
+            out[q] |= __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(min(d, 4)) * 8u);
+        }
+    }
+}
 
 __device__ inline uint32_t entry_y(uint64_t e) { return static_cast<uint32_t>(e >> 40); }
 __device__ inline uint8_t entry_block(uint64_t e) { return static_cast<uint8_t>(e & 0xFF); }
@@ -250,7 +311,8 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
 #pragma unroll
             for (int w = 0; w < NB; ++w) {
                 own[k][w] = v[w];
-                nxt[w * kExtCols + c] = v[w];
+                if (step < kMaxDistance) // nothing reads the planes after the last step
+                    nxt[w * kExtCols + c] = v[w];
             }
             if (k == 0) {
 #pragma unroll
@@ -265,7 +327,10 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
                 }
             }
         }
-        __syncthreads();
+        // After the last step both callers pass a barrier before the pool is
+        // written again.
+        if (step < kMaxDistance)
+            __syncthreads();
     }
 }
 
@@ -307,6 +372,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         s.tmax = -(1 << 20);
         s.dmin = 1 << 20;
         s.dmax = -(1 << 20);
+        s.omin = 1 << 20;
     }
 
     // ---- phase A: per-column summary -----------------------------------
@@ -329,6 +395,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         }
     }
     __syncthreads();
+    int32_t open_lo = 1 << 20; // lowest open row among this thread's ext columns
 #pragma unroll
     for (int it = 0; it < kColIters; ++it) {
         const int c = tid + it * kThreads;
@@ -358,11 +425,21 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                 atomicMin(&s.dmin, dlo);
                 atomicMax(&s.dmax, dhi);
             }
+            // Open cells of the column: every row above the final top, and the
+            // dark rows below it.
+            open_lo = min(open_lo, static_cast<int32_t>(static_cast<int16_t>(v.x >> 16)) + 1);
+            if (dlo <= dhi)
+                open_lo = min(open_lo, dlo);
         } else {
             s.top_t[c] = -1;
             s.top_f[c] = static_cast<int16_t>(clamp_top(static_cast<int16_t>(pa[it].x) - a.origin_y, H));
             s.ovr[c] = 0;
         }
+    }
+    if (a.mode == 0) {
+        open_lo = __reduce_min_sync(0xFFFFFFFFu, open_lo);
+        if (lane == 0)
+            atomicMin(&s.omin, open_lo);
     }
     __syncthreads();
 
@@ -518,28 +595,25 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
 
     // One 16-row chunk of light bytes: block bits, sky bits for the chunk rows
     // in sky_rows, trivial sky light (15 above the final top) elsewhere.
-    auto emit = [&](uint8_t* my, int32_t topf, int r0, uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3, uint32_t s0,
-                    uint32_t s1, uint32_t s2, uint32_t s3, uint32_t sky_rows) {
-        const bool block_any = (b0 | b1 | b2 | b3) != 0u;
+    auto emit_trivial = [&](uint8_t* my, int32_t topf, int r0) {
         uint32_t wv[4];
-        if (!block_any && sky_rows == 0u && (r0 > topf || r0 + 15 <= topf)) {
-            const uint32_t v = r0 > topf ? 0xF0F0F0F0u : 0u;
-            wv[0] = wv[1] = wv[2] = wv[3] = v;
-        } else {
-            const uint32_t lit = above_mask(r0, topf) & ~sky_rows;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int j = 4 * q;
-                uint32_t v = spread4((b0 >> j) & 0xFu) | (spread4((b1 >> j) & 0xFu) << 1)
-                    | (spread4((b2 >> j) & 0xFu) << 2) | (spread4((b3 >> j) & 0xFu) << 3);
-                if (sky_rows != 0u)
-                    v |= (spread4((s0 >> j) & 0xFu) << 4) | (spread4((s1 >> j) & 0xFu) << 5)
-                        | (spread4((s2 >> j) & 0xFu) << 6) | (spread4((s3 >> j) & 0xFu) << 7);
-                v |= spread4((lit >> j) & 0xFu) * 0xF0u;
-                wv[q] = v;
-            }
+        for (int q = 0; q < 4; ++q) {
+            const int32_t d = max(topf - (r0 + 4 * q) + 1, 0);
+            wv[q] = __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(min(d, 4)) * 8u);
         }
         *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    };
+    // One band word (32 rows from r0): block levels from b, sky levels from s
+    // (sky) or trivial; writes the 16-row halves selected by lo_on / hi_on.
+    auto emit_word = [&](uint8_t* my, int32_t topf, int r0, const uint32_t (&b)[4], const uint32_t (&sv)[4], bool sky,
+                         bool lo_on, bool hi_on) {
+        uint32_t o[8];
+        light_bytes(b, sv, sky, topf, r0, o);
+        if (lo_on)
+            *reinterpret_cast<uint4*>(my + r0) = make_uint4(o[0], o[1], o[2], o[3]);
+        if (hi_on)
+            *reinterpret_cast<uint4*>(my + r0 + 16) = make_uint4(o[4], o[5], o[6], o[7]);
     };
 
     // ---- block ids and height map (generation) -------------------------------
@@ -622,7 +696,11 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                 p.s_lo = max(dmin - kMaxDistance, 0);
                 p.s_hi = min(dmax + kMaxDistance, H - 1);
             }
-            const int32_t u_lo = min(p.b_lo, p.s_lo), u_hi = max(p.b_hi, p.s_hi);
+            // Rows below the lowest open row of the ext region are opaque in
+            // every column: their light is 0 and they carry none, so the band
+            // starts no lower than that row. Sources are open cells, so the
+            // band stays non-empty.
+            const int32_t u_lo = max(min(p.b_lo, p.s_lo), s.omin), u_hi = max(p.b_hi, p.s_hi);
             if (u_lo <= u_hi) {
                 o_lo = u_lo & ~15;
                 o_hi = min(u_hi | 15, H - 1);
@@ -761,35 +839,22 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
 #pragma unroll
                 for (int ch = 0; ch < kChunks; ++ch)
                     if ((trivial >> ch) & 1u)
-                        emit(my, topf, ch * 16, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u);
+                        emit_trivial(my, topf, ch * 16);
                 if (band_chunks != 0u) {
-                    if (!have_sky) {
 #pragma unroll
-                        for (int j = 0; j < KB; ++j)
-#pragma unroll
-                            for (int half = 0; half < 2; ++half) {
-                                const int r0 = p.w_lo + 32 * j + 16 * half;
-                                if (r0 >= H || !((band_chunks >> (r0 >> 4)) & 1u))
-                                    continue;
-                                const int sh = 16 * half;
-                                emit(my, topf, r0, (cb[j][0] >> sh) & 0xFFFFu, (cb[j][1] >> sh) & 0xFFFFu,
-                                    (cb[j][2] >> sh) & 0xFFFFu, (cb[j][3] >> sh) & 0xFFFFu, 0u, 0u, 0u, 0u, 0u);
-                            }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < KB; ++j)
-#pragma unroll
-                            for (int half = 0; half < 2; ++half) {
-                                const int r0 = p.w_lo + 32 * j + 16 * half;
-                                if (r0 >= H || !((band_chunks >> (r0 >> 4)) & 1u))
-                                    continue;
-                                const int sh = 16 * half;
-                                const uint32_t* pk = park + j * 4 * kThreads + tid;
-                                emit(my, topf, r0, (pk[0] >> sh) & 0xFFFFu, (pk[kThreads] >> sh) & 0xFFFFu,
-                                    (pk[2 * kThreads] >> sh) & 0xFFFFu, (pk[3 * kThreads] >> sh) & 0xFFFFu,
-                                    (cs[j][0] >> sh) & 0xFFFFu, (cs[j][1] >> sh) & 0xFFFFu, (cs[j][2] >> sh) & 0xFFFFu,
-                                    (cs[j][3] >> sh) & 0xFFFFu, 0xFFFFu);
-                            }
+                    for (int j = 0; j < KB; ++j) {
+                        const int r0 = p.w_lo + 32 * j;
+                        const bool lo_on = r0 < H && ((band_chunks >> (r0 >> 4)) & 1u);
+                        const bool hi_on = r0 + 16 < H && ((band_chunks >> ((r0 >> 4) + 1)) & 1u);
+                        if (!lo_on && !hi_on)
+                            continue;
+                        if (!have_sky) {
+                            emit_word(my, topf, r0, cb[j], cb[j], false, lo_on, hi_on);
+                        } else {
+                            const uint32_t* pk = park + j * 4 * kThreads + tid;
+                            const uint32_t bp[4] = { pk[0], pk[kThreads], pk[2 * kThreads], pk[3 * kThreads] };
+                            emit_word(my, topf, r0, bp, cs[j], true, lo_on, hi_on);
+                        }
                     }
                 }
             }
@@ -815,7 +880,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
 #pragma unroll
                 for (int ch = 0; ch < kChunks; ++ch)
                     if ((mask >> ch) & 1u)
-                        emit(my, topf, ch * 16, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u);
+                        emit_trivial(my, topf, ch * 16);
             }
             __syncwarp();
             if (gz < a.D)
