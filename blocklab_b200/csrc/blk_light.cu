@@ -311,8 +311,7 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
 #pragma unroll
             for (int w = 0; w < NB; ++w) {
                 own[k][w] = v[w];
-                if (step < kMaxDistance) // nothing reads the planes after the last step
-                    nxt[w * kExtCols + c] = v[w];
+                nxt[w * kExtCols + c] = v[w];
             }
             if (k == 0) {
 #pragma unroll
@@ -327,10 +326,7 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
                 }
             }
         }
-        // After the last step both callers pass a barrier before the pool is
-        // written again.
-        if (step < kMaxDistance)
-            __syncthreads();
+        __syncthreads();
     }
 }
 
