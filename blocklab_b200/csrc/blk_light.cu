@@ -222,27 +222,25 @@ __device__ inline int cone_distance(int c)
 
 __device__ inline bool in_world(const TileArgs& a, int gx, int gz) { return gx >= 0 && gz >= 0 && gx < a.W && gz < a.D; }
 
-// Open-cell and torch bits of the 32 rows starting at `ybase` (any row, not
-// necessarily aligned) of a resident id column; rows outside [0, H) are 0.
-template <int H>
-__device__ inline void id_bits(const uint8_t* column, int ybase, uint32_t& open, uint32_t& torch)
+// 0x80 in every byte of x that is zero (bytes below 0x80: adding 0x7F carries
+// into bit 7 exactly when the byte is non-zero, and never into the next byte).
+__device__ inline uint32_t zero_bytes(uint32_t x) { return ((x + 0x7F7F7F7Fu) & 0x80808080u) ^ 0x80808080u; }
+// Bit 7 of each byte -> 4 packed bits.
+__device__ inline uint32_t pack4_hi(uint32_t m) { return ((m >> 7) * 0x10204080u) >> 28; }
+
+// Open-cell and torch bits of the 32 rows held in v (two 16-byte chunks of a
+// resident id column, ids 0..4): open = Air or Torch (id & ~4 == 0).
+__device__ inline void id_bits(const uint4 (&v)[2], uint32_t& open, uint32_t& torch)
 {
-    // ybase is a multiple of 16 (relight windows start on 16-row chunks), so
-    // the word is exactly the two 16-byte chunks from row ybase.
     open = 0u;
     torch = 0u;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-        const int r = ybase + 16 * q;
-        if (r >= H)
-            continue;
-        const uint4 v4 = *reinterpret_cast<const uint4*>(column + r);
-        const uint32_t v[4] = { v4.x, v4.y, v4.z, v4.w };
+        const uint32_t w[4] = { v[q].x, v[q].y, v[q].z, v[q].w };
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const uint32_t t = bytes_eq(v[j], Torch);
-            open |= pack4(bytes_eq(v[j], Air) | t) << (16 * q + 4 * j);
-            torch |= pack4(t) << (16 * q + 4 * j);
+            open |= pack4_hi(zero_bytes(w[j] & 0xFBFBFBFBu)) << (16 * q + 4 * j);
+            torch |= pack4_hi(zero_bytes(w[j] ^ 0x04040404u)) << (16 * q + 4 * j);
         }
     }
 }
@@ -353,7 +351,7 @@ __device__ void flood_any(int nb, Smem<NW>& s, const int (&slot)[kSlots], uint32
     }
 }
 
-template <int NW>
+template <int NW, int MODE>
 __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x0, int z0, int32_t wlo_rows,
     int32_t whi_rows)
 {
@@ -383,7 +381,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
             const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
             if (in_world(a, gx, gz)) {
                 const uint64_t col = env_col0 + static_cast<uint64_t>(gz) * a.W + gx;
-                if (a.mode == 0)
+                if (MODE == 0)
                     pa[it] = __ldg(a.col_summary + col);
                 else
                     pa[it].x = static_cast<uint16_t>(__ldg(a.hmap + col));
@@ -406,7 +404,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
             s.ovr[c] = 0;
             continue;
         }
-        if (a.mode == 0) {
+        if (MODE == 0) {
             const uint4 v = pa[it];
             s.top_t[c] = static_cast<int16_t>(v.x & 0xFFFFu);
             s.top_f[c] = static_cast<int16_t>(v.x >> 16);
@@ -432,7 +430,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
             s.ovr[c] = 0;
         }
     }
-    if (a.mode == 0) {
+    if (MODE == 0) {
         open_lo = __reduce_min_sync(0xFFFFFFFFu, open_lo);
         if (lane == 0)
             atomicMin(&s.omin, open_lo);
@@ -498,8 +496,8 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         }
     };
 
-    // Open-cell and source bits of ext column c for the 32 rows from ybase.
-    // source: 0 = torches, 1 = lit cells (above the final top).
+    // Generation: open-cell and source bits of ext column c for the 32 rows
+    // from ybase. source: 0 = torches, 1 = lit cells (above the final top).
     auto column_bits = [&](int c, int ybase, int source, uint32_t& open, uint32_t& src) {
         const int32_t topf = s.top_f[c];
         open = 0u;
@@ -507,22 +505,14 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         if (topf < -1)
             return; // outside the world
         const uint32_t inside = inside_mask(ybase, H); // bands start at row >= 0
-        if (a.mode == 0) {
-            open = above_mask(ybase, min(static_cast<int32_t>(s.top_t[c]), H - 1));
-            if ((s.ovr[c] & (kOvrInline | kCntSat)) != 0u)
-                for_each_winner(c, ybase, ybase + 31, [&](int32_t y, uint8_t b) {
-                    const uint32_t bit = 1u << (y - ybase);
-                    open = is_opaque(b) ? (open & ~bit) : (open | bit);
-                    if (source == 0 && b == Torch)
-                        src |= bit;
-                });
-        } else {
-            const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
-            uint32_t t;
-            id_bits<H>(env_ids + (static_cast<uint64_t>(gz) * a.W + gx) * H, ybase, open, t);
-            if (source == 0)
-                src = t;
-        }
+        open = above_mask(ybase, min(static_cast<int32_t>(s.top_t[c]), H - 1));
+        if ((s.ovr[c] & (kOvrInline | kCntSat)) != 0u)
+            for_each_winner(c, ybase, ybase + 31, [&](int32_t y, uint8_t b) {
+                const uint32_t bit = 1u << (y - ybase);
+                open = is_opaque(b) ? (open & ~bit) : (open | bit);
+                if (source == 0 && b == Torch)
+                    src |= bit;
+            });
         if (source == 1)
             src = above_mask(ybase, topf);
         open &= inside;
@@ -534,6 +524,49 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     auto build = [&](int blo, int nb, int source) {
         uint32_t* O = s.O();
         uint32_t* B0 = s.B(0);
+        if (MODE != 0) {
+            // Relight: from the resident ids. Each word's loads for all of this
+            // thread's ext columns are in flight before any is decoded. Window
+            // words start on 16-row chunks, so a word is two aligned chunks.
+            constexpr int kInFlight = 2; // columns whose loads are in flight together
+            for (int w = 0; w < nb; ++w) {
+                const int ybase = blo + 32 * w;
+                const uint32_t inside = inside_mask(ybase, H);
+#pragma unroll
+                for (int it0 = 0; it0 < kColIters; it0 += kInFlight) {
+                    uint4 v[kInFlight][2];
+#pragma unroll
+                    for (int k = 0; k < kInFlight; ++k) {
+                        const int c = tid + (it0 + k) * kThreads;
+                        v[k][0] = v[k][1] = make_uint4(0u, 0u, 0u, 0u);
+                        if (c < kExtCols && s.top_f[c] >= -1) {
+                            const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
+                            const uint8_t* col = env_ids + (static_cast<uint64_t>(gz) * a.W + gx) * H + ybase;
+                            v[k][0] = __ldg(reinterpret_cast<const uint4*>(col));
+                            if (ybase + 16 < H)
+                                v[k][1] = __ldg(reinterpret_cast<const uint4*>(col + 16));
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < kInFlight; ++k) {
+                        const int c = tid + (it0 + k) * kThreads;
+                        if (c >= kExtCols)
+                            break;
+                        uint32_t open = 0u, src = 0u;
+                        const int32_t topf = s.top_f[c];
+                        if (topf >= -1) {
+                            uint32_t t;
+                            id_bits(v[k], open, t);
+                            open &= inside;
+                            src = (source == 0 ? t : above_mask(ybase, topf)) & open;
+                        }
+                        O[w * kExtCols + c] = open;
+                        B0[w * kExtCols + c] = src;
+                    }
+                }
+            }
+            return;
+        }
         for (int c = tid; c < kExtCols; c += kThreads) {
 #pragma unroll
             for (int w = 0; w < Smem<NW>::kBand; ++w)
@@ -613,7 +646,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     };
 
     // ---- block ids and height map (generation) -------------------------------
-    if (a.mode == 0) {
+    if (MODE == 0) {
         for (int round = 0; round < Smem<NW>::kRounds; ++round) {
             __syncthreads();
             if (warp / Smem<NW>::kStageWarps != round)
@@ -682,7 +715,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         p.b_hi = -1;
         p.s_lo = H;
         p.s_hi = -1;
-        if (a.mode == 0) {
+        if (MODE == 0) {
             const int32_t tmin = s.tmin, tmax = s.tmax, dmin = s.dmin, dmax = s.dmax;
             if (tmin <= tmax) {
                 p.b_lo = max(tmin - kMaxDistance, 0);
@@ -708,7 +741,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
             p.b_hi = p.s_hi = min(o_hi + kMaxDistance, H - 1);
         }
         p.whole = o_lo <= o_hi
-            && ((a.mode == 0 && o_hi - o_lo + 1 <= 32 * KB)
+            && ((MODE == 0 && o_hi - o_lo + 1 <= 32 * KB)
                 || (min(o_hi + kMaxDistance, H - 1) - max(o_lo - 16, 0) + 1 <= 32 * KB));
         p.n_win = o_lo > o_hi ? 0 : (p.whole ? 1 : (o_hi - o_lo + kWinRows) / kWinRows);
         p.o_chunks = o_lo > o_hi ? 0u : (((2u << (o_hi >> 4)) - 1u) & ~((1u << (o_lo >> 4)) - 1u));
@@ -720,8 +753,8 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         const int32_t o_lo = p.r_lo, o_hi = p.r_hi;
         int32_t w_hi;
         if (p.whole) {
-            p.w_lo = a.mode == 0 ? o_lo : max(o_lo - 16, 0);
-            w_hi = a.mode == 0 ? o_hi : min(o_hi + kMaxDistance, H - 1);
+            p.w_lo = MODE == 0 ? o_lo : max(o_lo - 16, 0);
+            w_hi = MODE == 0 ? o_hi : min(o_hi + kMaxDistance, H - 1);
         } else {
             p.r_lo = o_lo + kWinRows * wi;
             p.r_hi = min(p.r_lo + kWinRows - 1, o_hi);
@@ -757,7 +790,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                 open_ready = true;
                 __syncthreads();
                 bool go = true;
-                if (a.mode == 1) {
+                if (MODE == 1) {
                     // Any torch in the window? (generation knows from the override lists.)
                     bool any = false;
                     for (int idx = tid; idx < p.nb * kExtCols; idx += kThreads)
@@ -778,7 +811,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                     build(p.w_lo, p.nb, 1);
                 __syncthreads();
                 bool go = true;
-                if (a.mode == 1) {
+                if (MODE == 1) {
                     // Needed if an interior column has an open cell at or below
                     // its top inside the output rows.
                     bool dark = false;
@@ -822,7 +855,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
             if (n_win > 0) {
                 plan_window(p, wi);
                 const uint32_t r_chunks = ((2u << (p.r_hi >> 4)) - 1u) & ~((1u << (p.r_lo >> 4)) - 1u);
-                mask = p.whole ? (a.mode == 0 ? kAllChunks : r_chunks) : r_chunks;
+                mask = p.whole ? (MODE == 0 ? kAllChunks : r_chunks) : r_chunks;
                 band_chunks = (have_block || have_sky) ? r_chunks : 0u;
             } else {
                 p.w_lo = 0;
@@ -861,7 +894,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     }
 
     // Several windows: the chunks outside the output rows (generation only).
-    if (a.mode == 0 && n_win > 1) {
+    if (MODE == 0 && n_win > 1) {
         for (int round = 0; round < Smem<NW>::kRounds; ++round) {
             __syncthreads();
             if (warp / Smem<NW>::kStageWarps != round)
@@ -886,7 +919,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
 }
 
 // Persistent: one CTA per SM walks the tiles.
-template <int NW>
+template <int NW, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -895,7 +928,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
     // (sparse edits), else on the dirty tiles. Every CTA reads the same counts.
     uint32_t n = a.n_tiles;
     bool boxes = false;
-    if (a.mode != 0) {
+    if (MODE != 0) {
         const uint32_t nb = *a.box_count, nt = *a.dirty_count;
         boxes = nb <= a.box_capacity && nb <= nt;
         n = boxes ? nb : nt;
@@ -913,21 +946,21 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
             z0 = static_cast<int>(b.y >> 16);
             win = b.z;
         } else {
-            const uint32_t tile_id = a.mode == 0 && !a.listed ? i : a.dirty_list[i];
+            const uint32_t tile_id = MODE == 0 && !a.listed ? i : a.dirty_list[i];
             if (tile_id == 0xFFFFFFFFu)
                 continue; // uniform over the CTA
             env = tile_id / tiles_per_env;
             const uint32_t t_in_env = tile_id % tiles_per_env;
             x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
             z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
-            if (a.mode != 0)
+            if (MODE != 0)
                 win = a.dirty_window[tile_id];
         }
-        if (a.mode != 0) {
+        if (MODE != 0) {
             wlo_rows = static_cast<int32_t>(win & 0xFFFFu) & ~15;
             whi_rows = min(static_cast<int32_t>(win >> 16) | 15, 32 * NW - 1);
         }
-        process_tile<NW>(a, s, env, x0, z0, wlo_rows, whi_rows);
+        process_tile<NW, MODE>(a, s, env, x0, z0, wlo_rows, whi_rows);
         __syncthreads();
     }
 }
@@ -1016,8 +1049,8 @@ __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds,
     }
 }
 
-template <int NW>
-int launch_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
+template <int NW, int MODE>
+int launch_mode(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
 {
     static bool attr_set[64] = {};
     static int sm_count[64] = {};
@@ -1027,7 +1060,7 @@ int launch_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t st
         return BLK_ERR_INVALID_ARGUMENT;
     }
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tile_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tile_kernel<NW, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
             static_cast<int>(sizeof(Smem<NW>)));
         if (e != cudaSuccess)
             return cuda_fail(e, "cudaFuncSetAttribute(tile_kernel)");
@@ -1041,8 +1074,16 @@ int launch_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t st
     uint32_t grid = n_tiles < static_cast<uint32_t>(sm_count[dev]) ? n_tiles : static_cast<uint32_t>(sm_count[dev]);
     if (grid > ctx->park_ctas)
         grid = ctx->park_ctas;
-    tile_kernel<NW><<<grid, kThreads, sizeof(Smem<NW>), stream>>>(a);
+    tile_kernel<NW, MODE><<<grid, kThreads, sizeof(Smem<NW>), stream>>>(a);
     return cuda_fail(cudaGetLastError(), "tile_kernel launch");
+}
+
+// Generation and relight are separate kernels: each gets the registers of its
+// own code path.
+template <int NW>
+int launch_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
+{
+    return a.mode == 0 ? launch_mode<NW, 0>(ctx, a, n_tiles, stream) : launch_mode<NW, 1>(ctx, a, n_tiles, stream);
 }
 
 } // namespace
