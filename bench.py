@@ -454,18 +454,26 @@ def surface_edits(rng, hm, envs, n, W, D, torch_xyz):
 
 
 def dirty_voxels(before, after, W, H, D):
-    """Voxels within L-inf distance 14 (clipped to the world) of a changed cell,
-    summed over envs: the cells whose light an exact relight must revisit."""
+    """Voxels within L-inf distance 14 (clipped to the world) of a cell whose
+    light class changed (opaque / open / torch), summed over envs: the cells
+    whose light an exact relight must revisit. An opaque block replaced by
+    another opaque block changes no light. Also returns the number of cells
+    whose block id changed."""
     import numpy as np
+    import torch
 
-    changed = (before != after).nonzero().cpu().numpy()  # (env, z, x, y)
+    def light_class(ids):  # 0 opaque, 1 air, 2 torch (ids: Air 0, Torch 4)
+        return (ids == 0).to(torch.uint8) + 2 * (ids == 4).to(torch.uint8)
+
+    n_changed = int((before != after).sum().item())
+    changed = (light_class(before) != light_class(after)).nonzero().cpu().numpy()  # (env, z, x, y)
     total = 0
     for e in np.unique(changed[:, 0]):
         m = np.zeros((D, W, H), bool)
         for _, z, x, y in changed[changed[:, 0] == e]:
             m[max(z - 14, 0):z + 15, max(x - 14, 0):x + 15, max(y - 14, 0):y + 15] = True
         total += int(m.sum())
-    return total, len(changed)
+    return total, n_changed, len(changed)
 
 
 def run_workload(args) -> None:
@@ -505,7 +513,7 @@ def run_workload(args) -> None:
             wb.apply_edits(dev_batches[k])
         before = wb.ids.clone()
         wb.apply_edits(dev_batches[args.warmup])
-        dirty, n_changed = dirty_voxels(before, wb.ids, Wd, Hd, Dd)
+        dirty, n_changed, n_light = dirty_voxels(before, wb.ids, Wd, Hd, Dd)
         del before
         # Timed run on a fresh copy of the same worlds and edit sequence.
         wb.generate(seeds, torches)
@@ -538,7 +546,8 @@ def run_workload(args) -> None:
                          "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": (algo / (relight_ms / 1e3) / 1e9) / peaks["hbm_gbs"] if relight_ms > 0 else None,
                          "algorithmic_bytes_per_step": algo, "dirty_voxels_per_step": dirty,
-                         "changed_cells_per_step": n_changed, "relight_ms": relight_ms, "traffic": None},
+                         "changed_cells_per_step": n_changed, "light_class_changes_per_step": n_light,
+                         "relight_ms": relight_ms, "traffic": None},
             "e2e": {"value": env_steps / (e2e_ms / 1e3), "unit": "env-steps/s",
                     "h2d_bytes_per_step": int(dev_batches[0].numel()), "d2h_bytes_per_step": 0},
             "gpu_launches": None, "clocks": clocks})

@@ -385,7 +385,11 @@ __global__ void apply_edits_kernel(EditArgs a)
                 ylo = min(ylo, min(top, old_top) + 1);
                 yhi = max(yhi, max(top, old_top));
             }
-            mark_dirty(a, env, x, z, max(ylo, 0), min(yhi, H - 1));
+            // Light depends on which cells are opaque and which are torches
+            // only (the height map follows the opaque cells): an opaque cell
+            // replaced by another opaque block changes no light anywhere.
+            if (!(is_opaque(old) && is_opaque(block)))
+                mark_dirty(a, env, x, z, max(ylo, 0), min(yhi, H - 1));
             if (!(is_opaque(old) && !is_opaque(block) && y + 1 < H && ids[col * H + y + 1] == Torch))
                 break;
             y = y + 1;
