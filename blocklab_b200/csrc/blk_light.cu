@@ -163,12 +163,12 @@ __device__ inline void light_bytes(const uint32_t (&b)[4], const uint32_t (&s)[4
     out[5] = __byte_perm(hb, hd, 0x5410);
     out[7] = __byte_perm(hb, hd, 0x7632);
     if (!sky) {
+        // Rows of this word at or below topf keep sky 0: 8 bits of shift per
+        // such row (the funnel shift clamps at 32).
+        const int32_t t8 = 8 * (topf - r0 + 1);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            // Rows of this word at or below topf keep sky 0; the shift clamps at 32.
-            const int32_t d = max(topf - (r0 + 4 * q) + 1, 0);
-            out[q] |= __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(min(d, 4)) * 8u);
-        }
+        for (int q = 0; q < 8; ++q)
+            out[q] |= __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(max(t8 - 32 * q, 0)));
     }
 }
 
@@ -178,23 +178,15 @@ __device__ inline uint8_t entry_block(uint64_t e) { return static_cast<uint8_t>(
 // Bits j of the word starting at row ybase where ybase + j > top.
 __device__ inline uint32_t above_mask(int32_t ybase, int32_t top)
 {
-    const int32_t k = top - ybase + 1; // first open bit
-    if (k <= 0)
-        return 0xFFFFFFFFu;
-    if (k >= 32)
-        return 0u;
-    return 0xFFFFFFFFu << k;
+    // ~0 << k for the first open bit k, clamped to 0..32 (the funnel shift
+    // clamps shifts above 32: k >= 32 gives 0).
+    return __funnelshift_lc(0u, 0xFFFFFFFFu, static_cast<uint32_t>(max(top - ybase + 1, 0)));
 }
 
 // Bits j of the word starting at row ybase with ybase + j < H.
 __device__ inline uint32_t inside_mask(int32_t ybase, int32_t H)
 {
-    const int32_t k = H - ybase;
-    if (k >= 32)
-        return 0xFFFFFFFFu;
-    if (k <= 0)
-        return 0u;
-    return (1u << k) - 1u;
+    return ~above_mask(ybase, H - 1);
 }
 
 // Rows [lo, hi] of the word starting at ybase.
@@ -626,11 +618,12 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     // in sky_rows, trivial sky light (15 above the final top) elsewhere.
     auto emit_trivial = [&](uint8_t* my, int32_t topf, int r0) {
         uint32_t wv[4];
+        // Bytes of rows at or below topf keep sky 0: shift by 8 bits per such
+        // row of the word (the funnel shift clamps at 32).
+        const int32_t t8 = 8 * (topf - r0 + 1);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int32_t d = max(topf - (r0 + 4 * q) + 1, 0);
-            wv[q] = __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(min(d, 4)) * 8u);
-        }
+        for (int q = 0; q < 4; ++q)
+            wv[q] = __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(max(t8 - 32 * q, 0)));
         *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     };
     // One band word (32 rows from r0): block levels from b, sky levels from s
