@@ -57,6 +57,9 @@ constexpr int kSlots = 3;                           // interior + up to 2 halo c
 constexpr int kColIters = (kExtCols + kThreads - 1) / kThreads;
 constexpr uint32_t kCntSat = 31;                    // packed override count saturates here
 constexpr uint32_t kOvrInline = 0x80000000u;        // packed list holds its single entry: y << 8 | block
+// Halo slot without a column: ext column (1, 1) (cone distance 26, never in
+// reach, and neither are its neighbours) with a cone distance no step reaches.
+constexpr int kDummySlot = (1 * kExt + 1) | (0x7FFF << 16);
 
 struct TileArgs {
     uint8_t* ids;
@@ -241,7 +244,7 @@ __device__ inline void id_bits(const uint4 (&v)[2], uint32_t& open, uint32_t& to
 // plane B0 the level-15 sources of every ext column. A thread keeps its slot
 // columns' words in registers for the whole flood. Accumulates the level bit
 // planes of the interior column (slot 0) into cnt[w][p]. slot[k] packs the
-// ext column (low 16 bits) and its cone distance (high bits); -1 = unused.
+// ext column (low 16 bits) and its cone distance (high bits); kDummySlot = unused.
 template <int NW, int NB>
 __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Smem<NW>::kBand][4])
 {
@@ -253,7 +256,7 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
     for (int k = 0; k < kSlots; ++k)
 #pragma unroll
         for (int w = 0; w < NB; ++w)
-            own[k][w] = slot[k] >= 0 ? s.B(0)[w * kExtCols + (slot[k] & 0xFFFF)] : 0u;
+            own[k][w] = s.B(0)[w * kExtCols + (slot[k] & 0xFFFF)];
     // Open masks of the slot columns stay in registers for the whole flood.
     uint32_t open0[NB], openh[kSlots][NB];
 #pragma unroll
@@ -263,7 +266,7 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
     for (int k = 1; k < kSlots; ++k)
 #pragma unroll
         for (int w = 0; w < NB; ++w)
-            openh[k][w] = slot[k] >= 0 ? O[w * kExtCols + (slot[k] & 0xFFFF)] : 0u;
+            openh[k][w] = O[w * kExtCols + (slot[k] & 0xFFFF)];
 #pragma unroll
     for (int w = 0; w < KB; ++w) {
         cnt[w][0] = w < NB ? own[0][w < NB ? w : 0] : 0u;
@@ -281,11 +284,12 @@ __device__ void flood(Smem<NW>& s, const int (&slot)[kSlots], uint32_t (&cnt)[Sm
         const int level = 15 - step;
 #pragma unroll
         for (int k = 0; k < kSlots; ++k) {
-            const bool act = k == 0 || (slot[k] >= 0 && (slot[k] >> 16) <= reach);
-            if (k > 0 && !__any_sync(0xFFFFFFFFu, act))
+            // A warp updates a halo slot while any of its lanes' columns is in
+            // reach; the lanes beyond reach update too. That is harmless: a
+            // column beyond reach at step s is only read by neighbours that are
+            // beyond reach themselves at step s + 1 and later.
+            if (k > 0 && !__any_sync(0xFFFFFFFFu, (slot[k] >> 16) <= reach))
                 continue; // the whole warp skips this slot
-            if (!act)
-                continue;
             const int c = slot[k] & 0xFFFF;
             uint32_t v[NB];
 #pragma unroll
@@ -439,7 +443,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     for (int k = 1; k < kSlots; ++k) {
         const int wk = (k == 2) ? (kWarps - 1 - warp) : warp;
         const int r = (k - 1) * kThreads + wk * 32 + lane;
-        slot[k] = -1;
+        slot[k] = kDummySlot;
         if (r < kHaloCols) {
             const int c = __ldg(a.halo_order + r);
             const int d = cone_distance(c);
@@ -650,8 +654,10 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                 const int32_t top = s.top_t[c0];
                 uint8_t* my = stage_of();
                 a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(s.top_f[c0] + a.origin_y);
-                // Layer rule branch-free: id = [y <= top] + [y <= top-1] + [y <= top-4],
-                // compared chunk-relative in signed bytes (y - r0 is 0..15).
+                // Layer rule: id = [y <= top] + [y <= top-1] + [y <= top-4]
+                // = 3 - (number of those thresholds below y). U(t) holds 0x01 in
+                // the bytes of a 4-row word whose row is above t: 0x01010101
+                // shifted by 8 bits per row at or below t (clamped at 32).
 #pragma unroll
                 for (int ch = 0; ch < kChunks; ++ch) {
                     const int r0 = ch * 16;
@@ -661,15 +667,13 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                     } else if (r0 + 15 <= top - 4) {
                         wv[0] = wv[1] = wv[2] = wv[3] = 0x03030303u;
                     } else {
-                        const int d = top - r0; // -4 .. 15 here
-                        const uint32_t t0 = static_cast<uint32_t>(d & 0xFF) * 0x01010101u;
-                        const uint32_t t1 = static_cast<uint32_t>((d - 1) & 0xFF) * 0x01010101u;
-                        const uint32_t t4 = static_cast<uint32_t>((d - 4) & 0xFF) * 0x01010101u;
+                        const int32_t a0 = 8 * (top - r0 + 1);
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            const uint32_t y4 = static_cast<uint32_t>(4 * q) * 0x01010101u + 0x03020100u;
-                            wv[q] = (__vcmples4(y4, t0) & 0x01010101u) + (__vcmples4(y4, t1) & 0x01010101u)
-                                + (__vcmples4(y4, t4) & 0x01010101u);
+                            const int32_t a = a0 - 32 * q;
+                            wv[q] = 0x03030303u - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(a, 0)))
+                                - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(a - 8, 0)))
+                                - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(a - 32, 0)));
                         }
                     }
                     *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
