@@ -165,6 +165,27 @@ def cpu_sample(kind_pref: str = "reference"):
     return dt, SAMPLE_W * SAMPLE_H * SAMPLE_D, "port", 1, desc
 
 
+def gpu_reference_sample():
+    """Times the reference's own CUDA kernels (its src/world/WorldGenerator.cu
+    built for sm_100a under oracle/_ref) on one region of the benchmark's size,
+    driven one region per call as its renderer drives them. Returns
+    (seconds, voxels, description), or None when that build is absent."""
+    from oracle.oracle import TERRAIN_REFERENCE, Oracle, Reference, WorldSpec, ref_available
+    import numpy as np
+
+    if not ref_available("cuda"):
+        return None
+    R = Reference("cuda")
+    spec = WorldSpec(BASE_SEED, W, H, D, terrain=TERRAIN_REFERENCE)
+    torches = Oracle().place_torches(spec, TORCHES, 0x5EED)
+    timing = []
+    R.generate(BASE_SEED, (0, 0, 0), (W, H, D), torches, np.full(len(torches), 4, np.uint8), runs=3, timing=timing)
+    desc = (f"reference WorldGenerator::generate, its CUDA kernels built for sm_100a, on this GPU: one {W}x{H}x{D} "
+            f"region with {len(torches)} surface torches, reference terrain formula; converged third generation "
+            f"timed by wall clock (block cache + light + render list + its readback of the block cache)")
+    return timing[-1] / 1e3, W * H * D, desc
+
+
 def run_reference(args) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
@@ -365,6 +386,10 @@ def run_ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, vox, kind, cores, desc = cpu_sample("reference")
         line["cpu_baseline"] = {"value": vox / dt, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc}
+        ref_gpu = gpu_reference_sample()
+        if ref_gpu is not None:
+            dt, vox, desc = ref_gpu
+            line["reference_gpu"] = {"value": vox / dt, "unit": UNIT, "sample": desc}
     wb.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
