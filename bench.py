@@ -576,6 +576,27 @@ def run_workload(args) -> None:
             "e2e": {"value": env_steps / (e2e_ms / 1e3), "unit": "env-steps/s",
                     "h2d_bytes_per_step": int(dev_batches[0].numel()), "d2h_bytes_per_step": 0},
             "gpu_launches": None, "clocks": clocks})
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            # The reference regenerates and relights a region for every edit
+            # (src/graphics/Renderer.cpp:1121-1141): its own CUDA kernels on
+            # this GPU, one region per env-step.
+            from oracle.oracle import TERRAIN_REFERENCE, Oracle, Reference, WorldSpec, ref_available
+
+            if ref_available("cuda"):
+                R = Reference("cuda")
+                rspec = WorldSpec(BASE_SEED, Wd, Hd, Dd, terrain=TERRAIN_REFERENCE)
+                rt = Oracle().place_torches(rspec, c["torches"], 0x5EED)
+                times = []
+                for _ in range(5):
+                    timing = []
+                    R.generate(BASE_SEED, (0, 0, 0), (Wd, Hd, Dd), rt, np.full(len(rt), 4, np.uint8), runs=2,
+                               timing=timing)
+                    times.append(timing[-1] / 1e3)
+                line["reference_gpu"] = {
+                    "value": len(times) / sum(times), "unit": "env-steps/s",
+                    "sample": f"reference WorldGenerator::generate, its CUDA kernels built for sm_100a, on this GPU: "
+                              f"one {Wd}x{Hd}x{Dd} region with {len(rt)} torches regenerated per env-step (reference "
+                              f"terrain; converged generation by wall clock, including its block-cache readback)"}
         wb.close()
     elif args.workload == "daynight":
         c = dict(DAYNIGHT)
