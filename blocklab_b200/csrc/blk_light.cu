@@ -88,6 +88,15 @@ struct TileArgs {
     int32_t listed; // mode 0: tiles from dirty_list (0xFFFFFFFF = skip) instead of all
 };
 
+// Rows a tile lights (see plan_tile in process_tile).
+struct TilePlan {
+    int32_t r_lo, r_hi, w_lo, nb;
+    int32_t b_lo, b_hi, s_lo, s_hi;
+    uint32_t o_chunks;
+    int n_win;
+    bool whole;
+};
+
 template <int NW>
 struct Smem {
     // Max words of one flood band: 3 keeps the flood's registers unspilled;
@@ -108,6 +117,7 @@ struct Smem {
     uint32_t ovr[kExtCols];    // override list: begin << 5 | min(count, 31)
     int32_t tmin, tmax, dmin, dmax;
     int32_t omin;              // generation: lowest open row of the ext region (rows below are opaque everywhere)
+    TilePlan plan;             // the tile's plan, computed once per tile by thread 0
 
     __device__ uint32_t* O() { return pool; }
     __device__ uint32_t* B(int i) { return pool + (1 + i) * kPlane; }
@@ -699,14 +709,8 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     // 16-row chunk, so its band words split into whole chunks) and 14 above.
     // The plan reads shared memory only, so it is recomputed after each flood
     // instead of being held in registers across it.
-    struct Plan {
-        int32_t r_lo, r_hi, w_lo, nb;
-        int32_t b_lo, b_hi, s_lo, s_hi;
-        uint32_t o_chunks;
-        int n_win;
-        bool whole;
-    };
-    auto plan_tile = [&](Plan& p) {
+    using Plan = TilePlan;
+    auto compute_plan = [&](Plan& p) {
         int32_t o_lo = 0, o_hi = -1;
         p.b_lo = H;
         p.b_hi = -1;
@@ -745,6 +749,16 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         p.r_lo = o_lo;
         p.r_hi = o_hi;
     };
+    // Generation: every thread reads the tile's plan from shared memory
+    // (computed once by thread 0) instead of keeping it in registers across the
+    // floods. Relight (one short box per change) recomputes it per thread,
+    // which costs less than the extra barrier.
+    auto plan_tile = [&](Plan& p) {
+        if (MODE == 0)
+            p = s.plan;
+        else
+            compute_plan(p);
+    };
     auto plan_window = [&](Plan& p, int wi) {
         plan_tile(p);
         const int32_t o_lo = p.r_lo, o_hi = p.r_hi;
@@ -763,6 +777,11 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
 
     uint32_t* park = a.park + static_cast<uint64_t>(blockIdx.x) * (KB * 4 * kThreads);
     constexpr uint32_t kAllChunks = (1u << kChunks) - 1u;
+    if (MODE == 0) {
+        if (tid == 0)
+            compute_plan(s.plan);
+        __syncthreads();
+    }
     int n_win;
     {
         Plan p;
