@@ -17,7 +17,7 @@ namespace blk {
 namespace {
 thread_local std::string g_last_error;
 constexpr int kScanThreads = 1024;
-constexpr int kScanItems = 4; // per thread
+constexpr int kScanItems = 8; // per thread: two 16-byte loads / stores
 constexpr uint32_t kScanTile = kScanThreads * kScanItems;
 
 inline cudaStream_t as_stream(uintptr_t s) { return reinterpret_cast<cudaStream_t>(s); }
@@ -53,15 +53,32 @@ __device__ inline uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sums,
     return warp_prefix + x - v;
 }
 
+// A thread's kScanItems consecutive items from `base`: two 16-byte loads when
+// the array is 16-byte aligned and the items are all in range, else one by one.
+__device__ inline void scan_load(const uint32_t* in, uint64_t n, uint64_t base, uint32_t (&v)[kScanItems])
+{
+    if ((reinterpret_cast<uintptr_t>(in) & 15u) == 0u && base + kScanItems <= n) {
+        const uint4 a = *reinterpret_cast<const uint4*>(in + base);
+        const uint4 b = *reinterpret_cast<const uint4*>(in + base + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k)
+            v[k] = base + k < n ? in[base + k] : 0u;
+    }
+}
+
 __global__ void scan_reduce_kernel(const uint32_t* in, uint64_t n, uint32_t* partials)
 {
     __shared__ uint32_t ws[32];
     const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kScanTile + threadIdx.x * kScanItems;
+    uint32_t v[kScanItems];
+    scan_load(in, n, base, v);
     uint32_t sum = 0;
 #pragma unroll
     for (int k = 0; k < kScanItems; ++k)
-        if (base + k < n)
-            sum += in[base + k];
+        sum += v[k];
     uint32_t total;
     block_exclusive_scan(sum, ws, total);
     if (threadIdx.x == 0)
@@ -88,20 +105,28 @@ __global__ void scan_final_kernel(const uint32_t* in, uint64_t n, const uint32_t
     __shared__ uint32_t ws[32];
     const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kScanTile + threadIdx.x * kScanItems;
     uint32_t v[kScanItems];
+    scan_load(in, n, base, v);
     uint32_t sum = 0;
 #pragma unroll
-    for (int k = 0; k < kScanItems; ++k) {
-        v[k] = base + k < n ? in[base + k] : 0u;
+    for (int k = 0; k < kScanItems; ++k)
         sum += v[k];
-    }
     uint32_t total;
     uint32_t run = partials[blockIdx.x] + block_exclusive_scan(sum, ws, total);
+    uint32_t o[kScanItems];
 #pragma unroll
-    for (int k = 0; k < kScanItems; ++k)
-        if (base + k < n) {
-            out[base + k] = run;
-            run += v[k];
-        }
+    for (int k = 0; k < kScanItems; ++k) {
+        o[k] = run;
+        run += v[k];
+    }
+    if ((reinterpret_cast<uintptr_t>(out) & 15u) == 0u && base + kScanItems <= n) {
+        *reinterpret_cast<uint4*>(out + base) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(out + base + 4) = make_uint4(o[4], o[5], o[6], o[7]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k)
+            if (base + k < n)
+                out[base + k] = o[k];
+    }
 }
 
 // Exclusive scan of n uint32 (n <= scan capacity of the context).
