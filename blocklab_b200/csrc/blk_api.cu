@@ -1011,7 +1011,6 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
     const uint64_t n_cols = envs * ctx->columns_per_env;
     const RegionDims r = region(ctx);
     const int mark = prof_begin(ctx, 0, st);
-    BLK_CHECK(launch_terrain(ctx, st));
     BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
     if (n_overrides)
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
@@ -1025,7 +1024,7 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
         BLK_CUDA(cudaGetLastError(), "override kernels");
     }
     const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;
-    BLK_CHECK(launch_column_summary(ctx, st));
+    BLK_CHECK(launch_surface(ctx, st));
     prof_mark(ctx, mark, 1, st);
     BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_tiles), st));
     prof_mark(ctx, mark, 2, st);
@@ -1069,7 +1068,6 @@ int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, co
     r.env_mask = ctx->env_mask;
     const uint64_t n_cols = envs * ctx->columns_per_env;
     const int mark = prof_begin(ctx, 0, st);
-    BLK_CHECK(launch_terrain(ctx, st, ctx->env_mask));
     BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
     if (n_overrides)
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
@@ -1082,7 +1080,7 @@ int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, co
             ctx->ovr_owner);
         BLK_CUDA(cudaGetLastError(), "override kernels");
     }
-    BLK_CHECK(launch_column_summary(ctx, st, ctx->env_mask));
+    BLK_CHECK(launch_surface(ctx, st, ctx->env_mask));
     prof_mark(ctx, mark, 1, st);
     BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_items), st, true));
     prof_mark(ctx, mark, 2, st);

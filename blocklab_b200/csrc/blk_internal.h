@@ -85,6 +85,8 @@ int launch_relight(blk_ctx* ctx, cudaStream_t stream);
 // env_mask (device, one byte per env) restricts the work to the envs set in it; nullptr = all.
 int launch_terrain(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask = nullptr);
 int launch_column_summary(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask = nullptr);
+// Terrain surfaces plus generation column summaries; needs the override CSR.
+int launch_surface(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask = nullptr);
 // Mode 0 over a tile list (ctx->dirty_list, n_tiles entries, 0xFFFFFFFF = skip) when `listed`.
 int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed = false);
 int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,

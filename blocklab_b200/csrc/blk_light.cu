@@ -1005,8 +1005,81 @@ __global__ void terrain_kernel(const uint32_t* seeds, TerrainParams t, int32_t W
 // meets at most 64 / 8 + 1 cells) are hashed once into shared memory instead
 // of four times per column; the per-column arithmetic is fbm()'s.
 constexpr int kFbmBlock = 64;
+// Generation summary of one column from its terrain surface `top` and its
+// override CSR slice (see column_summary_kernel for the fields).
+__device__ inline uint4 summarize_column(int32_t top, uint64_t col, const uint32_t* col_offset, const uint64_t* entries,
+    int32_t H)
+{
+    constexpr uint32_t kEmpty = 0x7FFFu | (0x8000u << 16);
+    const int32_t tc = min(top, H - 1);
+    const uint32_t beg = col_offset[col];
+    const uint32_t n = col_offset[col + 1] - beg;
+    int32_t topf = tc;
+    int32_t tlo = 1 << 20, thi = -(1 << 20), dlo = 1 << 20, dhi = -(1 << 20);
+    if (n > 0) {
+        const uint64_t* e = entries + beg;
+        int32_t hi_opaque = -1;
+        // Winners: the last entry of each y run (entries sorted by y, then input order).
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint64_t v = e[i];
+            const int32_t y = static_cast<int32_t>(entry_y(v));
+            if (i + 1 < n && static_cast<int32_t>(entry_y(e[i + 1])) == y)
+                continue;
+            const uint8_t b = entry_block(v);
+            if (is_opaque(b))
+                hi_opaque = max(hi_opaque, y);
+            if (b == Torch) {
+                tlo = min(tlo, y);
+                thi = max(thi, y);
+            }
+        }
+        // Terrain part of the height map: walk down through cells whose
+        // winning override is non-opaque.
+        int32_t yt = tc;
+        int32_t i = static_cast<int32_t>(n) - 1;
+        while (yt >= 0) {
+            while (i >= 0 && static_cast<int32_t>(entry_y(e[i])) > yt)
+                --i;
+            if (i >= 0 && static_cast<int32_t>(entry_y(e[i])) == yt && !is_opaque(entry_block(e[i]))) {
+                --yt;
+                continue;
+            }
+            break;
+        }
+        topf = max(hi_opaque, yt);
+        // Open cells below the final top: non-opaque overrides there, and
+        // terrain air between the terrain surface and a higher opaque override.
+        for (uint32_t k = 0; k < n; ++k) {
+            const uint64_t v = e[k];
+            const int32_t y = static_cast<int32_t>(entry_y(v));
+            if (k + 1 < n && static_cast<int32_t>(entry_y(e[k + 1])) == y)
+                continue;
+            if (!is_opaque(entry_block(v)) && y < topf) {
+                dlo = min(dlo, y);
+                dhi = max(dhi, y);
+            }
+        }
+        if (tc + 1 < topf) {
+            dlo = min(dlo, tc + 1);
+            dhi = max(dhi, topf - 1);
+        }
+    }
+    uint4 r;
+    r.x = static_cast<uint32_t>(static_cast<uint16_t>(top)) | (static_cast<uint32_t>(static_cast<uint16_t>(topf)) << 16);
+    // A single override (a torch, mostly) is stored inline: its cell needs no
+    // entry load later.
+    r.y = n == 1 ? kOvrInline | (entry_y(entries[beg]) << 8) | entry_block(entries[beg])
+                 : (beg << 5) | (n < kCntSat ? n : kCntSat);
+    r.z = tlo <= thi ? static_cast<uint32_t>(static_cast<uint16_t>(tlo)) | (static_cast<uint32_t>(thi) << 16) : kEmpty;
+    r.w = dlo <= dhi ? static_cast<uint32_t>(static_cast<uint16_t>(dlo)) | (static_cast<uint32_t>(dhi) << 16) : kEmpty;
+    return r;
+}
+
+// With `summary` set it also writes each column's generation summary
+// (summarize_column), which needs the override CSR built first.
 __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds, TerrainParams t, int32_t W,
-    int32_t D, uint32_t num_envs, const uint8_t* env_mask, int16_t* out)
+    int32_t D, uint32_t num_envs, const uint8_t* env_mask, int16_t* out, const uint32_t* col_offset,
+    const uint64_t* entries, uint4* summary)
 {
     __shared__ float lat[4][100];
     __shared__ int32_t lat_ix[4], lat_iz[4], lat_nx[4], lat_nz[4];
@@ -1060,7 +1133,10 @@ __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds,
             const float f = __fdiv_rn(acc, 1.875f);
             int32_t top = t.base + static_cast<int32_t>(roundf(__fmul_rn(t.amplitude, f))) - t.origin_y;
             top = top < -1 ? -1 : (top > t.height + 4 ? t.height + 4 : top);
-            out[env_col0 + static_cast<uint64_t>(z) * W + x] = static_cast<int16_t>(top);
+            const uint64_t col = env_col0 + static_cast<uint64_t>(z) * W + x;
+            out[col] = static_cast<int16_t>(top);
+            if (summary)
+                summary[col] = summarize_column(top, col, col_offset, entries, t.height);
         }
     }
 }
@@ -1157,74 +1233,11 @@ int halo_order_size() { return kHaloCols; }
 __global__ void column_summary_kernel(const int16_t* terrain_top, const uint32_t* col_offset, const uint64_t* entries,
     int32_t H, uint64_t total, uint64_t columns, const uint8_t* env_mask, uint4* out)
 {
-    constexpr uint32_t kEmpty = 0x7FFFu | (0x8000u << 16);
     for (uint64_t col = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; col < total;
          col += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         if (env_mask && !env_mask[col / columns])
             continue;
-        const int32_t top = terrain_top[col];
-        const int32_t tc = min(top, H - 1);
-        const uint32_t beg = col_offset[col];
-        const uint32_t n = col_offset[col + 1] - beg;
-        int32_t topf = tc;
-        int32_t tlo = 1 << 20, thi = -(1 << 20), dlo = 1 << 20, dhi = -(1 << 20);
-        if (n > 0) {
-            const uint64_t* e = entries + beg;
-            int32_t hi_opaque = -1;
-            // Winners: the last entry of each y run (entries sorted by y, then input order).
-            for (uint32_t i = 0; i < n; ++i) {
-                const uint64_t v = e[i];
-                const int32_t y = static_cast<int32_t>(entry_y(v));
-                if (i + 1 < n && static_cast<int32_t>(entry_y(e[i + 1])) == y)
-                    continue;
-                const uint8_t b = entry_block(v);
-                if (is_opaque(b))
-                    hi_opaque = max(hi_opaque, y);
-                if (b == Torch) {
-                    tlo = min(tlo, y);
-                    thi = max(thi, y);
-                }
-            }
-            // Terrain part of the height map: walk down through cells whose
-            // winning override is non-opaque.
-            int32_t yt = tc;
-            int32_t i = static_cast<int32_t>(n) - 1;
-            while (yt >= 0) {
-                while (i >= 0 && static_cast<int32_t>(entry_y(e[i])) > yt)
-                    --i;
-                if (i >= 0 && static_cast<int32_t>(entry_y(e[i])) == yt && !is_opaque(entry_block(e[i]))) {
-                    --yt;
-                    continue;
-                }
-                break;
-            }
-            topf = max(hi_opaque, yt);
-            // Open cells below the final top: non-opaque overrides there, and
-            // terrain air between the terrain surface and a higher opaque override.
-            for (uint32_t k = 0; k < n; ++k) {
-                const uint64_t v = e[k];
-                const int32_t y = static_cast<int32_t>(entry_y(v));
-                if (k + 1 < n && static_cast<int32_t>(entry_y(e[k + 1])) == y)
-                    continue;
-                if (!is_opaque(entry_block(v)) && y < topf) {
-                    dlo = min(dlo, y);
-                    dhi = max(dhi, y);
-                }
-            }
-            if (tc + 1 < topf) {
-                dlo = min(dlo, tc + 1);
-                dhi = max(dhi, topf - 1);
-            }
-        }
-        uint4 r;
-        r.x = static_cast<uint32_t>(static_cast<uint16_t>(top)) | (static_cast<uint32_t>(static_cast<uint16_t>(topf)) << 16);
-        // A single override (a torch, mostly) is stored inline: its cell needs no
-        // entry load later.
-        r.y = n == 1 ? kOvrInline | (entry_y(entries[beg]) << 8) | entry_block(entries[beg])
-                     : (beg << 5) | (n < kCntSat ? n : kCntSat);
-        r.z = tlo <= thi ? static_cast<uint32_t>(static_cast<uint16_t>(tlo)) | (static_cast<uint32_t>(thi) << 16) : kEmpty;
-        r.w = dlo <= dhi ? static_cast<uint32_t>(static_cast<uint16_t>(dlo)) | (static_cast<uint32_t>(dhi) << 16) : kEmpty;
-        out[col] = r;
+        out[col] = summarize_column(terrain_top[col], col, col_offset, entries, H);
     }
 }
 
@@ -1246,7 +1259,7 @@ int launch_terrain(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
             std::min<uint32_t>(ctx->cfg.num_envs, 65535));
         terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
             static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), ctx->cfg.num_envs, env_mask,
-            ctx->terrain_top);
+            ctx->terrain_top, nullptr, nullptr, nullptr);
         return cuda_fail(cudaGetLastError(), "terrain_fbm_kernel launch");
     }
     const uint64_t total = static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->columns_per_env;
@@ -1256,6 +1269,21 @@ int launch_terrain(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
     terrain_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
         static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), total, env_mask, ctx->terrain_top);
     return cuda_fail(cudaGetLastError(), "terrain_kernel launch");
+}
+
+int launch_surface(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
+{
+    if (ctx->cfg.terrain_mode == BLK_TERRAIN_FBM) {
+        // One pass: each column's fBm surface and, from it, its summary.
+        const dim3 grid((ctx->cfg.width + kFbmBlock - 1) / kFbmBlock, (ctx->cfg.depth + kFbmBlock - 1) / kFbmBlock,
+            std::min<uint32_t>(ctx->cfg.num_envs, 65535));
+        terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
+            static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), ctx->cfg.num_envs, env_mask,
+            ctx->terrain_top, ctx->col_offset, ctx->entries, ctx->col_summary);
+        return cuda_fail(cudaGetLastError(), "terrain_fbm_kernel launch");
+    }
+    const int rc = launch_terrain(ctx, stream, env_mask);
+    return rc != BLK_OK ? rc : launch_column_summary(ctx, stream, env_mask);
 }
 
 int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed)
