@@ -38,8 +38,8 @@ BASE_SEED = 1
 # reference's torch density (1000 per 256 x 256 columns).
 SAMPLE_W, SAMPLE_H, SAMPLE_D, SAMPLE_TORCHES = 128, 128, 128, 250
 # Our kernel launches per step: place_torches, override count/scan(3)/scatter/sort,
-# terrain surface, column summaries, tile kernel, conversion.
-LAUNCHES_PER_STEP = 11
+# fBm surface with the column summaries, tile kernel, conversion.
+LAUNCHES_PER_STEP = 10
 
 
 def parse_args():
