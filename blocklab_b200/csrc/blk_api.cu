@@ -318,6 +318,7 @@ struct EditArgs {
     const blk_override* edits;
     const uint32_t* env_offset;
     uint32_t* order;
+    uint4* changes;    // 2 per edit: the cells it changed (x | z << 16, y | old << 16 | new << 24, rows ylo | yhi << 16, valid)
     uint8_t* ids;
     int16_t* hmap;
     uint32_t* win_lo;  // per env tile, atomicMin
@@ -376,6 +377,8 @@ __global__ void apply_edits_kernel(EditArgs a)
     int16_t* hm = a.hmap + static_cast<uint64_t>(env) * a.r.W * a.r.D;
     const int32_t H = a.r.H;
     for (uint32_t k = beg; k < end; ++k) {
+        a.changes[2 * static_cast<uint64_t>(k)].w = 0u;
+        a.changes[2 * static_cast<uint64_t>(k) + 1].w = 0u;
         const blk_override e = a.edits[a.order[k]];
         int32_t x = e.x - a.r.ox, y = e.y - a.r.oy, z = e.z - a.r.oz;
         uint8_t block = e.kind == 1 ? Air : e.block;
@@ -413,13 +416,43 @@ __global__ void apply_edits_kernel(EditArgs a)
             // Light depends on which cells are opaque and which are torches
             // only (the height map follows the opaque cells): an opaque cell
             // replaced by another opaque block changes no light anywhere.
+            // Other changes are recorded and marked for relight below, once
+            // the env's last edit is in.
             if (!(is_opaque(old) && is_opaque(block)))
-                mark_dirty(a, env, x, z, max(ylo, 0), min(yhi, H - 1));
+                a.changes[2 * static_cast<uint64_t>(k) + pass] = make_uint4(
+                    static_cast<uint32_t>(x) | (static_cast<uint32_t>(z) << 16),
+                    static_cast<uint32_t>(y) | (static_cast<uint32_t>(old) << 16) | (static_cast<uint32_t>(block) << 24),
+                    static_cast<uint32_t>(max(ylo, 0)) | (static_cast<uint32_t>(min(yhi, H - 1)) << 16), 1u);
             if (!(is_opaque(old) && !is_opaque(block) && y + 1 < H && ids[col * H + y + 1] == Torch))
                 break;
             y = y + 1;
             block = Air;
         }
+    }
+    // Mark the recorded changes, except an air <-> opaque change of a cell
+    // that ends the step enclosed: below its column's final top and with all
+    // six neighbours opaque (or outside the region) once every edit of the
+    // env is in. Such a cell has light 0 and carries no light both before and
+    // after the step, so the light field equals the one without its change;
+    // the other changes, marked as usual, cover every cell whose light moves.
+    auto opaque_at = [&](int32_t x, int32_t y, int32_t z) {
+        if (x < 0 || z < 0 || y < 0 || x >= a.r.W || z >= a.r.D || y >= H)
+            return true;
+        return is_opaque(ids[(static_cast<uint64_t>(z) * a.r.W + x) * H + y]);
+    };
+    for (uint64_t i = 2 * static_cast<uint64_t>(beg); i < 2 * static_cast<uint64_t>(end); ++i) {
+        const uint4 c = a.changes[i];
+        if (!c.w)
+            continue;
+        const int32_t x = static_cast<int32_t>(c.x & 0xFFFFu), z = static_cast<int32_t>(c.x >> 16);
+        const int32_t y = static_cast<int32_t>(c.y & 0xFFFFu);
+        const uint8_t old = static_cast<uint8_t>((c.y >> 16) & 0xFFu), now = static_cast<uint8_t>(c.y >> 24);
+        const int32_t top = hm[static_cast<uint64_t>(z) * a.r.W + x] - a.r.oy;
+        const bool enclosed = old != Torch && now != Torch && y < top && opaque_at(x - 1, y, z)
+            && opaque_at(x + 1, y, z) && opaque_at(x, y - 1, z) && opaque_at(x, y + 1, z) && opaque_at(x, y, z - 1)
+            && opaque_at(x, y, z + 1);
+        if (!enclosed)
+            mark_dirty(a, env, x, z, static_cast<int32_t>(c.z & 0xFFFFu), static_cast<int32_t>(c.z >> 16));
     }
 }
 
@@ -892,6 +925,7 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->edit_env_count, envs + 1, "edit counts"));
     A(dalloc(&ctx->edit_env_offset, envs + 1, "edit offsets"));
     A(dalloc(&ctx->edit_order, ctx->cfg.max_edits, "edit order"));
+    A(dalloc(&ctx->edit_changes, 2ull * ctx->cfg.max_edits, "edit changes"));
     A(dalloc(&ctx->dirty_window, 2 * n_tiles, "dirty windows"));
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
@@ -954,7 +988,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
         for (cudaEvent_t ev : m.e)
             cudaEventDestroy(ev);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
-        ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order,
+        ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order, ctx->edit_changes,
         ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
@@ -1150,6 +1184,7 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     a.edits = e;
     a.env_offset = ctx->edit_env_offset;
     a.order = ctx->edit_order;
+    a.changes = ctx->edit_changes;
     a.ids = ctx->ids;
     a.hmap = ctx->hmap;
     a.win_lo = win_lo;

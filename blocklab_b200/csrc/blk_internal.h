@@ -45,6 +45,7 @@ struct blk_ctx {
     uint32_t* edit_env_count = nullptr;   // [num_envs + 1]
     uint32_t* edit_env_offset = nullptr;  // [num_envs + 1]
     uint32_t* edit_order = nullptr;       // [max_edits] edit indices grouped by env, stable
+    uint4* edit_changes = nullptr;        // [2 * max_edits] cells each edit changed (see apply_edits_kernel)
     uint32_t* dirty_window = nullptr;     // [num_envs * tiles] packed ylo | yhi<<16, 0xFFFFFFFF = clean
     uint32_t* dirty_list = nullptr;       // [num_envs * tiles] dirty tile ids
     uint32_t* dirty_count = nullptr;      // [1]
