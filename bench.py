@@ -482,23 +482,42 @@ def dirty_voxels(before, after, W, H, D):
     """Voxels within L-inf distance 14 (clipped to the world) of a cell whose
     light class changed (opaque / open / torch), summed over envs: the cells
     whose light an exact relight must revisit. An opaque block replaced by
-    another opaque block changes no light. Also returns the number of cells
-    whose block id changed."""
+    another opaque block changes no light, and neither does an air <-> opaque
+    change of a cell that ends the step enclosed (below its column's top, six
+    opaque neighbours, no torch before or after). Also returns the number of
+    cells whose block id changed and the number of light-class changes."""
     import numpy as np
     import torch
+    import torch.nn.functional as F
 
     def light_class(ids):  # 0 opaque, 1 air, 2 torch (ids: Air 0, Torch 4)
         return (ids == 0).to(torch.uint8) + 2 * (ids == 4).to(torch.uint8)
 
     n_changed = int((before != after).sum().item())
-    changed = (light_class(before) != light_class(after)).nonzero().cpu().numpy()  # (env, z, x, y)
+    rows = []
+    n_light = 0
+    for e0 in range(0, before.shape[0], 64):  # ids [env][z][x][y], 64 envs at a time
+        b, a = before[e0:e0 + 64], after[e0:e0 + 64]
+        moved = light_class(b) != light_class(a)
+        n_light += int(moved.sum().item())
+        opaque = ((a != 0) & (a != 4)).to(torch.uint8)
+        y = torch.arange(H, device=a.device, dtype=torch.int32)
+        top = torch.where(opaque.bool(), y, torch.full_like(y, -1)).amax(dim=3, keepdim=True)
+        p = F.pad(opaque, (1, 1, 1, 1, 1, 1), value=1)
+        nb = (p[:, :-2, 1:-1, 1:-1] & p[:, 2:, 1:-1, 1:-1] & p[:, 1:-1, :-2, 1:-1] & p[:, 1:-1, 2:, 1:-1]
+              & p[:, 1:-1, 1:-1, :-2] & p[:, 1:-1, 1:-1, 2:]).bool()
+        enclosed = nb & (y < top) & (b != 4) & (a != 4)
+        idx = (moved & ~enclosed).nonzero()
+        idx[:, 0] += e0
+        rows.append(idx.cpu().numpy())
+    changed = np.concatenate(rows) if rows else np.zeros((0, 4), np.int64)  # (env, z, x, y)
     total = 0
     for e in np.unique(changed[:, 0]):
         m = np.zeros((D, W, H), bool)
         for _, z, x, y in changed[changed[:, 0] == e]:
             m[max(z - 14, 0):z + 15, max(x - 14, 0):x + 15, max(y - 14, 0):y + 15] = True
         total += int(m.sum())
-    return total, n_changed, len(changed)
+    return total, n_changed, n_light, len(changed)
 
 
 def run_workload(args) -> None:
@@ -538,7 +557,7 @@ def run_workload(args) -> None:
             wb.apply_edits(dev_batches[k])
         before = wb.ids.clone()
         wb.apply_edits(dev_batches[args.warmup])
-        dirty, n_changed, n_light = dirty_voxels(before, wb.ids, Wd, Hd, Dd)
+        dirty, n_changed, n_light, n_relit = dirty_voxels(before, wb.ids, Wd, Hd, Dd)
         del before
         # Timed run on a fresh copy of the same worlds and edit sequence.
         wb.generate(seeds, torches)
@@ -572,6 +591,7 @@ def run_workload(args) -> None:
                          "frac": (algo / (relight_ms / 1e3) / 1e9) / peaks["hbm_gbs"] if relight_ms > 0 else None,
                          "algorithmic_bytes_per_step": algo, "dirty_voxels_per_step": dirty,
                          "changed_cells_per_step": n_changed, "light_class_changes_per_step": n_light,
+                         "relit_changes_per_step": n_relit,
                          "relight_ms": relight_ms, "traffic": None},
             "e2e": {"value": env_steps / (e2e_ms / 1e3), "unit": "env-steps/s",
                     "h2d_bytes_per_step": int(dev_batches[0].numel()), "d2h_bytes_per_step": 0},
