@@ -121,3 +121,25 @@ def test_overlay_holds_only_overrides_inside_a_requested_region(B):
     assert inside == [(1, 30, 1), (9, 30, 1)]
     _assert_equals_regeneration(B, wb, cfg, seed, edits)
     wb.close()
+
+
+def test_enclosed_dig_opened_later_in_the_same_step_is_relit(B):
+    """An edit step digs a cell deep in the ground (enclosed when dug) and then
+    the cells that connect it to the surface: judged by the step's final cells,
+    it is no longer enclosed, so its light (now reached from the sky) must be
+    relit. A second deep dig that stays enclosed changes no light. Both against
+    a full regeneration with the same edits as overrides."""
+    seed, x, z = 17, 5, -3
+    wb, cfg = _world(B, seed, (x, 0, z))
+    top = _cell(wb, (x, 0, z))[2]
+    assert top >= 4
+    shaft = [((x, y, z), AIR) for y in range(top - 3, top + 1)]  # deepest first: enclosed when dug
+    sealed = [((x + 6, top - 3, z + 6), AIR)]                       # stays enclosed
+    edits = shaft + sealed
+    wb.apply_edits(B.make_overrides(np.array([e[0] for e in edits]), np.array([e[1] for e in edits], np.uint8),
+                                    env=0))
+    wb.sync()
+    light = _cell(wb, (x, top - 3, z))[1]
+    assert light >> 4 == 15  # the shaft bottom sees the sky
+    _assert_equals_regeneration(B, wb, cfg, seed, edits)
+    wb.close()
