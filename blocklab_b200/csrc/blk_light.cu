@@ -146,6 +146,14 @@ __device__ inline void level_nibbles(uint32_t p0, uint32_t p1, uint32_t p2, uint
 __device__ inline void light_bytes(const uint32_t (&b)[4], const uint32_t (&s)[4], bool sky, int32_t topf, int32_t r0,
     uint32_t (&out)[8])
 {
+    if (!sky && !__any_sync(__activemask(), (b[0] | b[1] | b[2] | b[3]) != 0u)) {
+        // No block light in this word for any active lane: sky bytes only.
+        const int32_t t8 = 8 * (topf - r0 + 1);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            out[q] = __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(max(t8 - 32 * q, 0)));
+        return;
+    }
     uint32_t n[4], l[4], h[4];
     level_nibbles(b[0], b[1], b[2], b[3], n[0], n[1], n[2], n[3]);
     if (sky) {
