@@ -416,8 +416,8 @@ __global__ void apply_edits_kernel(EditArgs a)
             // Light depends on which cells are opaque and which are torches
             // only (the height map follows the opaque cells): an opaque cell
             // replaced by another opaque block changes no light anywhere.
-            // Other changes are recorded and marked for relight below, once
-            // the env's last edit is in.
+            // Other changes are recorded and marked for relight by
+            // mark_changes_kernel once every env's last edit is in.
             if (!(is_opaque(old) && is_opaque(block)))
                 a.changes[2 * static_cast<uint64_t>(k) + pass] = make_uint4(
                     static_cast<uint32_t>(x) | (static_cast<uint32_t>(z) << 16),
@@ -429,21 +429,32 @@ __global__ void apply_edits_kernel(EditArgs a)
             block = Air;
         }
     }
-    // Mark the recorded changes, except an air <-> opaque change of a cell
-    // that ends the step enclosed: below its column's final top and with all
-    // six neighbours opaque (or outside the region) once every edit of the
-    // env is in. Such a cell has light 0 and carries no light both before and
-    // after the step, so the light field equals the one without its change;
-    // the other changes, marked as usual, cover every cell whose light moves.
-    auto opaque_at = [&](int32_t x, int32_t y, int32_t z) {
-        if (x < 0 || z < 0 || y < 0 || x >= a.r.W || z >= a.r.D || y >= H)
-            return true;
-        return is_opaque(ids[(static_cast<uint64_t>(z) * a.r.W + x) * H + y]);
-    };
-    for (uint64_t i = 2 * static_cast<uint64_t>(beg); i < 2 * static_cast<uint64_t>(end); ++i) {
+}
+
+// Marks the changes apply_edits_kernel recorded, except an air <-> opaque
+// change of a cell that ends the step enclosed: below its column's final top
+// and with all six neighbours opaque (or outside the region) once every edit
+// of its env is in. Such a cell has light 0 and carries no light both before
+// and after the step, so the light field equals the one without its change;
+// the other changes, marked as usual, cover every cell whose light moves. One
+// thread per record (two per edit position of the env-grouped list).
+__global__ void mark_changes_kernel(EditArgs a)
+{
+    const uint64_t n_rec = 2ull * a.env_offset[a.r.num_envs]; // edits grouped to an env
+    const int32_t H = a.r.H;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n_rec;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const uint4 c = a.changes[i];
         if (!c.w)
             continue;
+        const uint32_t env = a.edits[a.order[i / 2]].env;
+        const uint8_t* ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
+        const int16_t* hm = a.hmap + static_cast<uint64_t>(env) * a.r.W * a.r.D;
+        auto opaque_at = [&](int32_t x, int32_t y, int32_t z) {
+            if (x < 0 || z < 0 || y < 0 || x >= a.r.W || z >= a.r.D || y >= H)
+                return true;
+            return is_opaque(ids[(static_cast<uint64_t>(z) * a.r.W + x) * H + y]);
+        };
         const int32_t x = static_cast<int32_t>(c.x & 0xFFFFu), z = static_cast<int32_t>(c.x >> 16);
         const int32_t y = static_cast<int32_t>(c.y & 0xFFFFu);
         const uint8_t old = static_cast<uint8_t>((c.y >> 16) & 0xFFu), now = static_cast<uint8_t>(c.y >> 24);
@@ -1198,6 +1209,7 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     a.tiles_z = ctx->tiles_z;
     BLK_CUDA(cudaMemsetAsync(ctx->box_count, 0, sizeof(uint32_t), st), "memset box count");
     apply_edits_kernel<<<(envs + 127) / 128, 128, 0, st>>>(a);
+    mark_changes_kernel<<<grid_for(2ull * n_edits, 256), 256, 0, st>>>(a);
     BLK_CUDA(cudaGetLastError(), "apply edits launch");
     prof_mark(ctx, mark, 1, st);
     BLK_CHECK(launch_relight(ctx, st));
