@@ -483,8 +483,8 @@ def dirty_voxels(before, after, W, H, D):
     light class changed (opaque / open / torch), summed over envs: the cells
     whose light an exact relight must revisit. An opaque block replaced by
     another opaque block changes no light, and neither does an air <-> opaque
-    change of a cell that ends the step enclosed (below its column's top, six
-    opaque neighbours, no torch before or after). Also returns the number of
+    change of a cell that ends the step enclosed (below its column's top before
+    and after the step, six opaque neighbours, no torch before or after). Also returns the number of
     cells whose block id changed and the number of light-class changes."""
     import numpy as np
     import torch
@@ -503,10 +503,11 @@ def dirty_voxels(before, after, W, H, D):
         opaque = ((a != 0) & (a != 4)).to(torch.uint8)
         y = torch.arange(H, device=a.device, dtype=torch.int32)
         top = torch.where(opaque.bool(), y, torch.full_like(y, -1)).amax(dim=3, keepdim=True)
+        top_before = torch.where((b != 0) & (b != 4), y, torch.full_like(y, -1)).amax(dim=3, keepdim=True)
         p = F.pad(opaque, (1, 1, 1, 1, 1, 1), value=1)
         nb = (p[:, :-2, 1:-1, 1:-1] & p[:, 2:, 1:-1, 1:-1] & p[:, 1:-1, :-2, 1:-1] & p[:, 1:-1, 2:, 1:-1]
               & p[:, 1:-1, 1:-1, :-2] & p[:, 1:-1, 1:-1, 2:]).bool()
-        enclosed = nb & (y < top) & (b != 4) & (a != 4)
+        enclosed = nb & (y < top) & (y < top_before) & (b != 4) & (a != 4)
         idx = (moved & ~enclosed).nonzero()
         idx[:, 0] += e0
         rows.append(idx.cpu().numpy())

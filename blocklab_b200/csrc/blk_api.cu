@@ -416,13 +416,15 @@ __global__ void apply_edits_kernel(EditArgs a)
             // Light depends on which cells are opaque and which are torches
             // only (the height map follows the opaque cells): an opaque cell
             // replaced by another opaque block changes no light anywhere.
-            // Other changes are recorded and marked for relight by
-            // mark_changes_kernel once every env's last edit is in.
+            // Other changes are recorded, with the column's top just before
+            // the change (w = 1 | (old_top + 2) << 8), and marked for relight
+            // by mark_changes_kernel once every env's last edit is in.
             if (!(is_opaque(old) && is_opaque(block)))
                 a.changes[2 * static_cast<uint64_t>(k) + pass] = make_uint4(
                     static_cast<uint32_t>(x) | (static_cast<uint32_t>(z) << 16),
                     static_cast<uint32_t>(y) | (static_cast<uint32_t>(old) << 16) | (static_cast<uint32_t>(block) << 24),
-                    static_cast<uint32_t>(max(ylo, 0)) | (static_cast<uint32_t>(min(yhi, H - 1)) << 16), 1u);
+                    static_cast<uint32_t>(max(ylo, 0)) | (static_cast<uint32_t>(min(yhi, H - 1)) << 16),
+                    1u | (static_cast<uint32_t>(old_top + 2) << 8));
             if (!(is_opaque(old) && !is_opaque(block) && y + 1 < H && ids[col * H + y + 1] == Torch))
                 break;
             y = y + 1;
@@ -432,11 +434,17 @@ __global__ void apply_edits_kernel(EditArgs a)
 }
 
 // Marks the changes apply_edits_kernel recorded, except an air <-> opaque
-// change of a cell that ends the step enclosed: below its column's final top
-// and with all six neighbours opaque (or outside the region) once every edit
-// of its env is in. Such a cell has light 0 and carries no light both before
-// and after the step, so the light field equals the one without its change;
-// the other changes, marked as usual, cover every cell whose light moves. One
+// change of a cell that lay below its column's top when it changed and ends
+// the step enclosed: below its column's final top and with all six neighbours
+// opaque (or outside the region) once every edit of its env is in, no torch
+// before or after. Every change that moves a column's top is then marked with
+// the span it moved, so a skipped cell was no sky source before the step
+// unless a marked span covers it. A light path of the old world into a skipped
+// cell enters it from a neighbour that is opaque at the end of the step, i.e.
+// from a changed cell: marked (its window covers the path's end) or skipped
+// (then the path came through an earlier skipped cell, back to a source, which
+// no skipped cell is). So outside the marked windows no light path and no
+// source differs between the two worlds, and their light agrees there. One
 // thread per record (two per edit position of the env-grouped list).
 __global__ void mark_changes_kernel(EditArgs a)
 {
@@ -459,7 +467,8 @@ __global__ void mark_changes_kernel(EditArgs a)
         const int32_t y = static_cast<int32_t>(c.y & 0xFFFFu);
         const uint8_t old = static_cast<uint8_t>((c.y >> 16) & 0xFFu), now = static_cast<uint8_t>(c.y >> 24);
         const int32_t top = hm[static_cast<uint64_t>(z) * a.r.W + x] - a.r.oy;
-        const bool enclosed = old != Torch && now != Torch && y < top && opaque_at(x - 1, y, z)
+        const int32_t top_then = static_cast<int32_t>(c.w >> 8) - 2; // the column's top just before the change
+        const bool enclosed = old != Torch && now != Torch && y < top && y < top_then && opaque_at(x - 1, y, z)
             && opaque_at(x + 1, y, z) && opaque_at(x, y - 1, z) && opaque_at(x, y + 1, z) && opaque_at(x, y, z - 1)
             && opaque_at(x, y, z + 1);
         if (!enclosed)

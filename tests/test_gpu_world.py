@@ -411,6 +411,37 @@ def test_edits_support_removal_and_heightmap(B, oracle):
     wb.close()
 
 
+def test_shaft_filled_bottom_up_in_one_step(B, oracle):
+    """A 1-wide shaft open to the sky (26 deep, opaque walls) is filled with
+    stone from the bottom up in one step. Each filled cell ends the step
+    enclosed, but each one raised its column's top when it was placed, so all
+    of them must be relit: the lit shaft cells go dark. A second env fills a
+    sealed cave pocket, whose changes need no relight, beside an open one."""
+    W, H, D = 40, 64, 40
+    cfg = B.WorldConfig(num_envs=2, width=W, height=H, depth=D, terrain=TERRAIN_FLAT, base=40)
+    wb = B.WorldBatch(cfg)
+    wb.generate([1, 2])
+    state = [list(oracle.build_blocks(WorldSpec(s, W, H, D, terrain=TERRAIN_FLAT, base=40))) for s in (1, 2)]
+    shaft = np.array([[20, y, 20] for y in range(15, 41)])
+    pocket = np.array([[x, 20, 10] for x in range(8, 12)] + [[30, 25, 30], [30, 26, 30]])
+    steps = [
+        [(shaft[::-1], 0), (pocket, 0)],  # dig the shaft top-down; dig a pocket and a 2-cell void
+        [(shaft, 3), (pocket[::-1], 3)],  # fill both bottom-up / in reverse, one step
+    ]
+    for k, per_env in enumerate(steps):
+        lists = []
+        for e, (xyz, blk) in enumerate(per_env):
+            lists.append(B.make_overrides(xyz, np.full(len(xyz), blk, np.uint8), env=e))
+            oracle.apply_edits(state[e][0], state[e][1], xyz, np.zeros(len(xyz), np.uint8),
+                               np.full(len(xyz), blk, np.uint8))
+        wb.apply_edits(np.concatenate(lists))
+        wb.sync()
+        for e in range(2):
+            bl, sl = oracle.light(state[e][0], state[e][1], 0, "multi")
+            _assert_world(wb, e, state[e][0], bl, sl, state[e][1], f"step{k} env{e}")
+    wb.close()
+
+
 def test_apply_edits_requires_generate_and_capacity(B):
     cfg = B.WorldConfig(num_envs=1, width=32, height=32, depth=32, max_overrides=4, max_edits=2)
     wb = B.WorldBatch(cfg)
