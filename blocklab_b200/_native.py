@@ -69,6 +69,7 @@ class WorldViewsC(ctypes.Structure):
         ("ids", ctypes.c_void_p),
         ("light", ctypes.c_void_p),
         ("height_map", ctypes.c_void_p),
+        ("env_origins", ctypes.c_void_p),
         ("env_stride", ctypes.c_uint64),
         ("num_envs", ctypes.c_uint32),
         ("width", ctypes.c_uint32),
@@ -97,7 +98,7 @@ SIGNATURES = {
     "blk_ctx_destroy": (ctypes.c_int, [_VP]),
     "blk_last_error": (ctypes.c_char_p, []),
     "blk_views": (ctypes.c_int, [_VP, ctypes.POINTER(WorldViewsC)]),
-    "blk_generate": (ctypes.c_int, [_VP, _VP, _VP, _U32, _UP]),
+    "blk_generate": (ctypes.c_int, [_VP, _VP, _VP, _VP, _U32, _UP]),
     "blk_place_torches": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _UP]),
     "blk_apply_edits": (ctypes.c_int, [_VP, _VP, _U32, _UP]),
     "blk_build_render_voxels": (ctypes.c_int, [_VP, _U32, _VP, _U32, _VP, _VP, _UP]),
@@ -116,7 +117,7 @@ SIGNATURES = {
     "blk_render_params_at": (None, [ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                     _U32, _VP]),
     "blk_render_frames": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _UP]),
-    "blk_generate_envs": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _U32, _UP]),
+    "blk_generate_envs": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _VP, _U32, _UP]),
     "blk_render_observations": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _VP, _UP]),
 }
 

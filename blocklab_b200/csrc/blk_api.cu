@@ -145,7 +145,7 @@ int exclusive_scan(blk_ctx* ctx, const uint32_t* in, uint32_t* out, uint64_t n, 
 
 // ------------------------------------------------------------ overrides --
 struct RegionDims {
-    int32_t ox, oy, oz;
+    const int4* origin;      // [env] world coordinates of each env's local (0, 0, 0)
     int32_t W, H, D;
     uint32_t num_envs;
     const uint8_t* env_mask; // override kernels: only envs set here (nullptr = all)
@@ -153,11 +153,13 @@ struct RegionDims {
 
 __device__ inline bool local_cell(const RegionDims& r, const blk_override& o, int32_t& x, int32_t& y, int32_t& z)
 {
-    x = o.x - r.ox;
-    y = o.y - r.oy;
-    z = o.z - r.oz;
-    return o.env < r.num_envs && (!r.env_mask || r.env_mask[o.env]) && x >= 0 && y >= 0 && z >= 0 && x < r.W
-        && y < r.H && z < r.D && o.block <= Torch;
+    if (o.env >= r.num_envs || (r.env_mask && !r.env_mask[o.env]) || o.block > Torch)
+        return false;
+    const int4 org = r.origin[o.env];
+    x = o.x - org.x;
+    y = o.y - org.y;
+    z = o.z - org.z;
+    return x >= 0 && y >= 0 && z >= 0 && x < r.W && y < r.H && z < r.D;
 }
 
 __global__ void ovr_count_kernel(const blk_override* ovr, uint32_t n, RegionDims r, uint32_t* col_count)
@@ -244,11 +246,12 @@ __global__ void place_torches_kernel(const uint32_t* seeds, uint32_t num_envs, u
                 atomicOr(flags, kFlagPermuteGuard);
             const int32_t x = static_cast<int32_t>(c % static_cast<uint32_t>(r.W));
             const int32_t z = static_cast<int32_t>(c / static_cast<uint32_t>(r.W));
-            const int32_t top = clamp_top(terrain_top_local(t, seed, r.ox + x, r.oz + z), r.H);
+            const int4 org = r.origin[env];
+            const int32_t top = clamp_top(terrain_top_local(t, seed, org.x + x, org.z + z, org.y), r.H);
             if (top + 1 < r.H) {
-                o.x = r.ox + x;
-                o.y = r.oy + top + 1;
-                o.z = r.oz + z;
+                o.x = org.x + x;
+                o.y = org.y + top + 1;
+                o.z = org.z + z;
             }
         }
         out[g] = o;
@@ -376,11 +379,12 @@ __global__ void apply_edits_kernel(EditArgs a)
     uint8_t* ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
     int16_t* hm = a.hmap + static_cast<uint64_t>(env) * a.r.W * a.r.D;
     const int32_t H = a.r.H;
+    const int4 org = a.r.origin[env];
     for (uint32_t k = beg; k < end; ++k) {
         a.changes[2 * static_cast<uint64_t>(k)].w = 0u;
         a.changes[2 * static_cast<uint64_t>(k) + 1].w = 0u;
         const blk_override e = a.edits[a.order[k]];
-        int32_t x = e.x - a.r.ox, y = e.y - a.r.oy, z = e.z - a.r.oz;
+        int32_t x = e.x - org.x, y = e.y - org.y, z = e.z - org.z;
         uint8_t block = e.kind == 1 ? Air : e.block;
         if (x < 0 || z < 0 || y < 0 || x >= a.r.W || z >= a.r.D || y >= H || block > Torch)
             continue;
@@ -395,7 +399,7 @@ __global__ void apply_edits_kernel(EditArgs a)
             if (old == block)
                 break;
             cell = block;
-            const int32_t old_top = hm[col] - a.r.oy;
+            const int32_t old_top = hm[col] - org.y;
             int32_t top = old_top;
             if (is_opaque(block) && y > top)
                 top = y;
@@ -407,7 +411,7 @@ __global__ void apply_edits_kernel(EditArgs a)
                         break;
                     }
             }
-            hm[col] = static_cast<int16_t>(top + a.r.oy);
+            hm[col] = static_cast<int16_t>(top + org.y);
             int32_t ylo = y, yhi = y;
             if (top != old_top) {
                 ylo = min(ylo, min(top, old_top) + 1);
@@ -466,7 +470,7 @@ __global__ void mark_changes_kernel(EditArgs a)
         const int32_t x = static_cast<int32_t>(c.x & 0xFFFFu), z = static_cast<int32_t>(c.x >> 16);
         const int32_t y = static_cast<int32_t>(c.y & 0xFFFFu);
         const uint8_t old = static_cast<uint8_t>((c.y >> 16) & 0xFFu), now = static_cast<uint8_t>(c.y >> 24);
-        const int32_t top = hm[static_cast<uint64_t>(z) * a.r.W + x] - a.r.oy;
+        const int32_t top = hm[static_cast<uint64_t>(z) * a.r.W + x] - a.r.origin[env].y;
         const int32_t top_then = static_cast<int32_t>(c.w >> 8) - 2; // the column's top just before the change
         const bool enclosed = old != Torch && now != Torch && y < top && y < top_then && opaque_at(x - 1, y, z)
             && opaque_at(x + 1, y, z) && opaque_at(x, y - 1, z) && opaque_at(x, y + 1, z) && opaque_at(x, y, z - 1)
@@ -558,12 +562,16 @@ __global__ void voxel_count_kernel(VoxelArgs a)
     a.row_count[row] = n;
 }
 
+// The header's origin comes from `origin_dev` (device, one record) when it
+// is given, else from `origin`.
 __global__ void voxel_write_kernel(VoxelArgs a, const uint32_t* row_offset, uint32_t* voxels, uint32_t max_voxels,
-    uint32_t* count, int32_t* header, int3 origin)
+    uint32_t* count, int32_t* header, const int4* origin_dev, int3 origin)
 {
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     const int rows = a.D * a.H;
     if (row == 0) {
+        if (origin_dev)
+            origin = make_int3(origin_dev->x, origin_dev->y, origin_dev->z);
         header[0] = origin.x;
         header[1] = origin.y;
         header[2] = origin.z;
@@ -632,11 +640,22 @@ __global__ void __launch_bounds__(1024) row_scan_one_block(const uint32_t* in, u
         }
 }
 
+// ---------------------------------------------------------- region origins --
+// origins[i] = (xyz[3i], xyz[3i + 1], xyz[3i + 2]) for the n envs.
+__global__ void set_origins_kernel(const int32_t* xyz, uint32_t n, int4* origins)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        origins[i] = make_int4(xyz[3 * static_cast<uint64_t>(i)], xyz[3 * static_cast<uint64_t>(i) + 1],
+            xyz[3 * static_cast<uint64_t>(i) + 2], 0);
+}
+
 // ---------------------------------------------------------- partial reset --
-// Marks the listed envs, installs their seeds and lists their tiles
-// (0xFFFFFFFF for an out-of-range env id, which also raises a flag).
-__global__ void env_select_kernel(const uint32_t* env_ids, const uint32_t* seeds, uint32_t n, uint32_t num_envs,
-    uint32_t tiles_per_env, uint8_t* mask, uint32_t* env_seeds, uint32_t* tile_list, uint32_t* flags)
+// Marks the listed envs, installs their seeds (and origins, when given) and
+// lists their tiles (0xFFFFFFFF for an out-of-range env id, which also raises
+// a flag).
+__global__ void env_select_kernel(const uint32_t* env_ids, const uint32_t* seeds, const int32_t* origin_xyz,
+    uint32_t n, uint32_t num_envs, uint32_t tiles_per_env, uint8_t* mask, uint32_t* env_seeds, int4* origins,
+    uint32_t* tile_list, uint32_t* flags)
 {
     const uint64_t total = static_cast<uint64_t>(n) * tiles_per_env;
     for (uint64_t k = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; k < total;
@@ -653,6 +672,9 @@ __global__ void env_select_kernel(const uint32_t* env_ids, const uint32_t* seeds
         if (t == 0) {
             mask[e] = 1;
             env_seeds[e] = seeds[i];
+            if (origin_xyz)
+                origins[e] = make_int4(origin_xyz[3 * static_cast<uint64_t>(i)],
+                    origin_xyz[3 * static_cast<uint64_t>(i) + 1], origin_xyz[3 * static_cast<uint64_t>(i) + 2], 0);
         }
     }
 }
@@ -664,7 +686,8 @@ __global__ void query_cells_kernel(const blk_cell_query* q, uint32_t n, const ui
 {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const blk_cell_query c = q[i];
-        const int32_t x = c.x - r.ox, y = c.y - r.oy, z = c.z - r.oz;
+        const int4 org = c.env < r.num_envs ? r.origin[c.env] : make_int4(0, 0, 0, 0);
+        const int32_t x = c.x - org.x, y = c.y - org.y, z = c.z - org.z;
         const bool column = c.env < r.num_envs && x >= 0 && x < r.W && z >= 0 && z < r.D;
         const bool inside = column && y >= 0 && y < r.H;
         const uint64_t col = static_cast<uint64_t>(z) * r.W + x;
@@ -692,9 +715,10 @@ __global__ void query_solid_kernel(const blk_box_query* q, uint32_t n, const uin
     const uint32_t warps = gridDim.x * (blockDim.x / 32);
     for (uint32_t i = (blockIdx.x * blockDim.x + threadIdx.x) / 32; i < n; i += warps) {
         const blk_box_query b = q[i];
-        const int32_t x0 = max(b.min_x - r.ox, 0), x1 = min(b.max_x - r.ox, r.W - 1);
-        const int32_t y0 = max(b.min_y - r.oy, 0), y1 = min(b.max_y - r.oy, r.H - 1);
-        const int32_t z0 = max(b.min_z - r.oz, 0), z1 = min(b.max_z - r.oz, r.D - 1);
+        const int4 org = b.env < r.num_envs ? r.origin[b.env] : make_int4(0, 0, 0, 0);
+        const int32_t x0 = max(b.min_x - org.x, 0), x1 = min(b.max_x - org.x, r.W - 1);
+        const int32_t y0 = max(b.min_y - org.y, 0), y1 = min(b.max_y - org.y, r.H - 1);
+        const int32_t z0 = max(b.min_z - org.z, 0), z1 = min(b.max_z - org.z, r.D - 1);
         bool found = false;
         if (b.env < r.num_envs && x0 <= x1 && y0 <= y1 && z0 <= z1) {
             const uint64_t ny = y1 - y0 + 1, nx = x1 - x0 + 1;
@@ -749,14 +773,15 @@ __global__ void snapshot_write_kernel(const uint8_t* ids, const int16_t* terrain
             continue;
         const int32_t top = terrain_top[col];
         const int32_t x = static_cast<int32_t>(col % r.W), z = static_cast<int32_t>(col / r.W);
+        const int4 org = r.origin[env];
         for (int32_t y = 0; y < r.H && pos < capacity; ++y) {
             const uint8_t b = ids[col * r.H + y];
             if (b == layer_block(y, top))
                 continue;
             blk_override o;
-            o.x = x + r.ox;
-            o.y = y + r.oy;
-            o.z = z + r.oz;
+            o.x = x + org.x;
+            o.y = y + org.y;
+            o.z = z + org.z;
             o.env = static_cast<uint16_t>(env);
             o.block = b;
             o.kind = 0;
@@ -794,9 +819,7 @@ int grid_for(uint64_t work, int threads)
 RegionDims region(const blk_ctx* ctx)
 {
     RegionDims r;
-    r.ox = ctx->cfg.origin_x;
-    r.oy = ctx->cfg.origin_y;
-    r.oz = ctx->cfg.origin_z;
+    r.origin = ctx->origins;
     r.W = static_cast<int32_t>(ctx->cfg.width);
     r.H = static_cast<int32_t>(ctx->cfg.height);
     r.D = static_cast<int32_t>(ctx->cfg.depth);
@@ -869,9 +892,6 @@ TerrainParams terrain_params(const blk_ctx* ctx)
     t.mode = ctx->cfg.terrain_mode;
     t.base = ctx->cfg.fbm_base;
     t.amplitude = ctx->cfg.fbm_amplitude;
-    t.origin_x = ctx->cfg.origin_x;
-    t.origin_y = ctx->cfg.origin_y;
-    t.origin_z = ctx->cfg.origin_z;
     t.height = static_cast<int32_t>(ctx->cfg.height);
     return t;
 }
@@ -933,6 +953,8 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->light, envs * ctx->env_stride, "light"));
     A(dalloc(&ctx->hmap, envs * ctx->columns_per_env, "height map"));
     A(dalloc(&ctx->seeds, envs, "seeds"));
+    A(dalloc(&ctx->origins, envs, "region origins"));
+    A(dalloc(&ctx->origin_stage, 3 * envs, "region origin staging"));
     A(dalloc(&ctx->terrain_top, envs * ctx->columns_per_env, "terrain heights"));
     A(dalloc(&ctx->halo_order, static_cast<size_t>(halo_order_size()), "halo order"));
     A(dalloc(&ctx->ovr, ctx->cfg.max_overrides, "override staging"));
@@ -982,6 +1004,12 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
                            cudaMemcpyHostToDevice),
             "halo order upload");
     }
+    if (rc == BLK_OK) {
+        // Every env starts at the configuration's origin.
+        const std::vector<int4> org(envs, make_int4(c.origin_x, c.origin_y, c.origin_z, 0));
+        rc = cuda_fail(cudaMemcpy(ctx->origins, org.data(), envs * sizeof(int4), cudaMemcpyHostToDevice),
+            "origin upload");
+    }
     if (rc == BLK_OK)
         rc = cuda_fail(cudaMemset(ctx->flags, 0, sizeof(uint32_t)), "cudaMemset flags");
     if (rc == BLK_OK)
@@ -1007,7 +1035,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
     for (auto& m : ctx->marks)
         for (cudaEvent_t ev : m.e)
             cudaEventDestroy(ev);
-    void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
+    void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->origins, ctx->origin_stage, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order, ctx->edit_changes,
         ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
     for (void* b : bufs)
@@ -1031,6 +1059,7 @@ int blk_views(blk_ctx* ctx, blk_world_views* out)
     out->ids = ctx->ids;
     out->light = ctx->light;
     out->height_map = ctx->hmap;
+    out->env_origins = reinterpret_cast<const int32_t*>(ctx->origins);
     out->env_stride = ctx->env_stride;
     out->num_envs = ctx->cfg.num_envs;
     out->width = ctx->cfg.width;
@@ -1039,8 +1068,8 @@ int blk_views(blk_ctx* ctx, blk_world_views* out)
     return BLK_OK;
 }
 
-int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* overrides, uint32_t n_overrides,
-    uintptr_t stream_handle)
+int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const int32_t* env_origins, const blk_override* overrides,
+    uint32_t n_overrides, uintptr_t stream_handle)
 {
     if (!ctx || !env_seeds || (n_overrides && !overrides)) {
         set_error("blk_generate: null argument");
@@ -1059,6 +1088,13 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
     if (seeds_dev != ctx->seeds)
         BLK_CUDA(cudaMemcpyAsync(ctx->seeds, seeds_dev, envs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st),
             "seed copy");
+    if (env_origins) {
+        const void* org_dev = nullptr;
+        BLK_CHECK(stage_input(env_origins, envs * 3 * sizeof(int32_t), ctx->origin_stage, st, &org_dev));
+        set_origins_kernel<<<grid_for(envs, 256), 256, 0, st>>>(static_cast<const int32_t*>(org_dev),
+            static_cast<uint32_t>(envs), ctx->origins);
+        BLK_CUDA(cudaGetLastError(), "origin install launch");
+    }
     const void* ovr_dev = nullptr;
     BLK_CHECK(stage_input(overrides, static_cast<size_t>(n_overrides) * sizeof(blk_override), ctx->ovr, st, &ovr_dev));
     const auto* ovr = static_cast<const blk_override*>(ovr_dev);
@@ -1087,7 +1123,7 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* ov
 }
 
 int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, const uint32_t* env_seeds,
-    const blk_override* overrides, uint32_t n_overrides, uintptr_t stream_handle)
+    const int32_t* env_origins, const blk_override* overrides, uint32_t n_overrides, uintptr_t stream_handle)
 {
     if (!ctx || (n_envs && (!env_ids || !env_seeds)) || (n_overrides && !overrides)) {
         set_error("blk_generate_envs: null argument");
@@ -1106,17 +1142,19 @@ int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, co
     cudaStream_t st = as_stream(stream_handle);
     BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     const uint64_t envs = ctx->cfg.num_envs;
-    const void *ids_dev = nullptr, *seeds_dev = nullptr, *ovr_dev = nullptr;
+    const void *ids_dev = nullptr, *seeds_dev = nullptr, *ovr_dev = nullptr, *org_dev = nullptr;
     BLK_CHECK(stage_input(env_ids, n_envs * sizeof(uint32_t), ctx->env_list, st, &ids_dev));
     BLK_CHECK(stage_input(env_seeds, n_envs * sizeof(uint32_t), ctx->seed_list, st, &seeds_dev));
+    if (env_origins)
+        BLK_CHECK(stage_input(env_origins, n_envs * 3 * sizeof(int32_t), ctx->origin_stage, st, &org_dev));
     BLK_CHECK(stage_input(overrides, static_cast<size_t>(n_overrides) * sizeof(blk_override), ctx->ovr, st, &ovr_dev));
     const auto* ovr = static_cast<const blk_override*>(ovr_dev);
     const uint32_t tiles_per_env = ctx->tiles_x * ctx->tiles_z;
     const uint64_t n_items = static_cast<uint64_t>(n_envs) * tiles_per_env;
     BLK_CUDA(cudaMemsetAsync(ctx->env_mask, 0, envs, st), "memset env mask");
     env_select_kernel<<<grid_for(n_items, 256), 256, 0, st>>>(static_cast<const uint32_t*>(ids_dev),
-        static_cast<const uint32_t*>(seeds_dev), n_envs, ctx->cfg.num_envs, tiles_per_env, ctx->env_mask, ctx->seeds,
-        ctx->dirty_list, ctx->flags);
+        static_cast<const uint32_t*>(seeds_dev), static_cast<const int32_t*>(org_dev), n_envs, ctx->cfg.num_envs,
+        tiles_per_env, ctx->env_mask, ctx->seeds, ctx->origins, ctx->dirty_list, ctx->flags);
     BLK_CUDA(cudaGetLastError(), "env select launch");
     RegionDims r = region(ctx);
     r.env_mask = ctx->env_mask;
@@ -1255,8 +1293,7 @@ int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t m
     voxel_count_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, st>>>(a);
     BLK_CHECK(exclusive_scan(ctx, a.row_count, row_offset, rows, st));
     voxel_write_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, st>>>(a, row_offset,
-        static_cast<uint32_t*>(voxels), max_voxels, count, header,
-        make_int3(ctx->cfg.origin_x, ctx->cfg.origin_y, ctx->cfg.origin_z));
+        static_cast<uint32_t*>(voxels), max_voxels, count, header, ctx->origins + env, make_int3(0, 0, 0));
     return cuda_fail(cudaGetLastError(), "render voxel launch");
 }
 
@@ -1671,7 +1708,7 @@ int blk_build_render_voxels_static(const uint8_t* ids, const uint8_t* light, uin
     row_scan_one_block<<<1, 1024, 0, st>>>(a.row_count, row_offset, rows);
     BLK_CUDA(cudaGetLastError(), "render voxel scan launch");
     voxel_write_kernel<<<(rows + 127) / 128, 128, 0, st>>>(a, row_offset, static_cast<uint32_t*>(voxels), max_voxels,
-        count, header, make_int3(origin_x, origin_y, origin_z));
+        count, header, nullptr, make_int3(origin_x, origin_y, origin_z));
     return cuda_fail(cudaGetLastError(), "render voxel launch");
 }
 

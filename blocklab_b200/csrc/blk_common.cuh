@@ -133,14 +133,14 @@ struct TerrainParams {
     int32_t mode;       // blk_terrain_mode
     int32_t base;
     float amplitude;
-    int32_t origin_x, origin_y, origin_z;
     int32_t height;     // H
 };
 
-// Surface (highest terrain block) of world column (wx, wz) as a LOCAL y, not
-// clamped: the layer rule needs the true surface even when it lies outside
-// the region. Callers clamp to [-1, H-1] where they need a cell index.
-__device__ inline int32_t terrain_top_local(const TerrainParams& t, uint32_t seed, int32_t wx, int32_t wz)
+// Surface (highest terrain block) of world column (wx, wz) as a y local to a
+// region whose cell 0 lies at world y `oy`, not clamped: the layer rule needs
+// the true surface even when it lies outside the region. Callers clamp to
+// [-1, H-1] where they need a cell index.
+__device__ inline int32_t terrain_top_local(const TerrainParams& t, uint32_t seed, int32_t wx, int32_t wz, int32_t oy)
 {
     int32_t h;
     if (t.mode == 0)
@@ -149,7 +149,7 @@ __device__ inline int32_t terrain_top_local(const TerrainParams& t, uint32_t see
         h = t.base + static_cast<int32_t>(roundf(__fmul_rn(t.amplitude, fbm(seed, wx, wz))));
     else
         h = t.base;
-    return h - t.origin_y;
+    return h - oy;
 }
 
 __device__ inline int32_t clamp_top(int32_t top, int32_t height)

@@ -23,6 +23,8 @@ struct blk_ctx {
     int16_t* hmap = nullptr;          // [env][z][x], world y
 
     uint32_t* seeds = nullptr;        // [env]
+    int4* origins = nullptr;          // [env] world coordinates of each env's local (0, 0, 0); w unused
+    int32_t* origin_stage = nullptr;  // [env * 3] staging of host-resident origin lists
     int16_t* terrain_top = nullptr;   // [env][z][x] local terrain surface, clamped to [-1, H+4]
     uint16_t* halo_order = nullptr;   // halo columns of a tile by cone distance
     bool generated = false;

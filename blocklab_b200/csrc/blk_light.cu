@@ -78,8 +78,8 @@ struct TileArgs {
     uint32_t box_capacity;
     uint32_t* flags;
     uint32_t* park;                 // per-CTA scratch for block planes during a sky flood
+    const int4* origins;            // [env] world coordinates of each env's local (0, 0, 0)
     uint32_t n_tiles;
-    int32_t origin_y;
     int32_t W, D;
     int32_t tiles_x, tiles_z;
     uint64_t env_stride;
@@ -374,6 +374,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     const int lane = tid & 31, warp = tid >> 5;
     const uint64_t env_col0 = static_cast<uint64_t>(env) * a.columns;
     uint8_t* env_ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
+    const int32_t origin_y = __ldg(&a.origins[env].y);
 
     if (tid == 0) {
         s.tmin = 1 << 20;
@@ -440,7 +441,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                 open_lo = min(open_lo, dlo);
         } else {
             s.top_t[c] = -1;
-            s.top_f[c] = static_cast<int16_t>(clamp_top(static_cast<int16_t>(pa[it].x) - a.origin_y, H));
+            s.top_f[c] = static_cast<int16_t>(clamp_top(static_cast<int16_t>(pa[it].x) - origin_y, H));
             s.ovr[c] = 0;
         }
     }
@@ -671,7 +672,7 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
                 const int c0 = slot[0];
                 const int32_t top = s.top_t[c0];
                 uint8_t* my = stage_of();
-                a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(s.top_f[c0] + a.origin_y);
+                a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(s.top_f[c0] + origin_y);
                 // Layer rule: id = [y <= top] + [y <= top-1] + [y <= top-4]
                 // = 3 - (number of those thresholds below y). U(t) holds 0x01 in
                 // the bytes of a 4-row word whose row is above t: 0x01010101
@@ -991,8 +992,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
 
 // Terrain surface of every column of every env (local y, clamped to
 // [-1, H+4], which preserves the layer rule inside the region).
-__global__ void terrain_kernel(const uint32_t* seeds, TerrainParams t, int32_t W, int32_t D, uint64_t total,
-    const uint8_t* env_mask, int16_t* out)
+__global__ void terrain_kernel(const uint32_t* seeds, const int4* origins, TerrainParams t, int32_t W, int32_t D,
+    uint64_t total, const uint8_t* env_mask, int16_t* out)
 {
     const uint64_t columns = static_cast<uint64_t>(W) * D;
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -1002,7 +1003,8 @@ __global__ void terrain_kernel(const uint32_t* seeds, TerrainParams t, int32_t W
             continue;
         const uint64_t col = i - env * columns;
         const int32_t x = static_cast<int32_t>(col % W), z = static_cast<int32_t>(col / W);
-        int32_t top = terrain_top_local(t, seeds[env], t.origin_x + x, t.origin_z + z);
+        const int4 org = origins[env];
+        int32_t top = terrain_top_local(t, seeds[env], org.x + x, org.z + z, org.y);
         top = top < -1 ? -1 : (top > t.height + 4 ? t.height + 4 : top);
         out[i] = static_cast<int16_t>(top);
     }
@@ -1085,31 +1087,34 @@ __device__ inline uint4 summarize_column(int32_t top, uint64_t col, const uint32
 
 // With `summary` set it also writes each column's generation summary
 // (summarize_column), which needs the override CSR built first.
-__global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds, TerrainParams t, int32_t W,
-    int32_t D, uint32_t num_envs, const uint8_t* env_mask, int16_t* out, const uint32_t* col_offset,
-    const uint64_t* entries, uint4* summary)
+__global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds, const int4* origins,
+    TerrainParams t, int32_t W, int32_t D, uint32_t num_envs, const uint8_t* env_mask, int16_t* out,
+    const uint32_t* col_offset, const uint64_t* entries, uint4* summary)
 {
     __shared__ float lat[4][100];
     __shared__ int32_t lat_ix[4], lat_iz[4], lat_nx[4], lat_nz[4];
     const int bx = blockIdx.x * kFbmBlock, bz = blockIdx.y * kFbmBlock;
     const int ex = min(bx + kFbmBlock - 1, W - 1), ez = min(bz + kFbmBlock - 1, D - 1);
-    if (threadIdx.x < 4) {
-        const int o = threadIdx.x;
-        int32_t i0, i1, k0, k1;
-        float w;
-        fbm_cell(o, t.origin_x + bx, i0, w);
-        fbm_cell(o, t.origin_x + ex, i1, w);
-        fbm_cell(o, t.origin_z + bz, k0, w);
-        fbm_cell(o, t.origin_z + ez, k1, w);
-        lat_ix[o] = i0;
-        lat_iz[o] = k0;
-        lat_nx[o] = i1 - i0 + 2; // corners ix .. ix + 1 of every cell met
-        lat_nz[o] = k1 - k0 + 2;
-    }
     for (uint32_t env = blockIdx.z; env < num_envs; env += gridDim.z) {
         if (env_mask && !env_mask[env])
             continue; // uniform over the block
         const uint32_t seed = seeds[env];
+        const int4 org = origins[env];
+        __syncthreads();
+        if (threadIdx.x < 4) {
+            // Lattice cells of octave o met by the block's columns (world x, z).
+            const int o = threadIdx.x;
+            int32_t i0, i1, k0, k1;
+            float w;
+            fbm_cell(o, org.x + bx, i0, w);
+            fbm_cell(o, org.x + ex, i1, w);
+            fbm_cell(o, org.z + bz, k0, w);
+            fbm_cell(o, org.z + ez, k1, w);
+            lat_ix[o] = i0;
+            lat_iz[o] = k0;
+            lat_nx[o] = i1 - i0 + 2; // corners ix .. ix + 1 of every cell met
+            lat_nz[o] = k1 - k0 + 2;
+        }
         __syncthreads();
 #pragma unroll
         for (int o = 0; o < 4; ++o) {
@@ -1130,8 +1135,8 @@ __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds,
             for (int o = 0; o < 4; ++o) {
                 int32_t ix, iz;
                 float wx, wz;
-                fbm_cell(o, t.origin_x + x, ix, wx);
-                fbm_cell(o, t.origin_z + z, iz, wz);
+                fbm_cell(o, org.x + x, ix, wx);
+                fbm_cell(o, org.z + z, iz, wz);
                 const int nx = lat_nx[o];
                 const float* L = lat[o] + (iz - lat_iz[o]) * nx + (ix - lat_ix[o]);
                 const float n = fbm_mix(L[0], L[1], L[nx], L[nx + 1], wx, wz);
@@ -1139,7 +1144,7 @@ __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds,
                 amp = __fmul_rn(amp, 0.5f);
             }
             const float f = __fdiv_rn(acc, 1.875f);
-            int32_t top = t.base + static_cast<int32_t>(roundf(__fmul_rn(t.amplitude, f))) - t.origin_y;
+            int32_t top = t.base + static_cast<int32_t>(roundf(__fmul_rn(t.amplitude, f))) - org.y;
             top = top < -1 ? -1 : (top > t.height + 4 ? t.height + 4 : top);
             const uint64_t col = env_col0 + static_cast<uint64_t>(z) * W + x;
             out[col] = static_cast<int16_t>(top);
@@ -1265,7 +1270,7 @@ int launch_terrain(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
     if (ctx->cfg.terrain_mode == BLK_TERRAIN_FBM) {
         const dim3 grid((ctx->cfg.width + kFbmBlock - 1) / kFbmBlock, (ctx->cfg.depth + kFbmBlock - 1) / kFbmBlock,
             std::min<uint32_t>(ctx->cfg.num_envs, 65535));
-        terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
+        terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, ctx->origins, terrain_params(ctx),
             static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), ctx->cfg.num_envs, env_mask,
             ctx->terrain_top, nullptr, nullptr, nullptr);
         return cuda_fail(cudaGetLastError(), "terrain_fbm_kernel launch");
@@ -1274,7 +1279,7 @@ int launch_terrain(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
     uint64_t blocks = (total + 255) / 256;
     if (blocks > 148ull * 32)
         blocks = 148ull * 32;
-    terrain_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
+    terrain_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ctx->seeds, ctx->origins, terrain_params(ctx),
         static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), total, env_mask, ctx->terrain_top);
     return cuda_fail(cudaGetLastError(), "terrain_kernel launch");
 }
@@ -1285,7 +1290,7 @@ int launch_surface(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
         // One pass: each column's fBm surface and, from it, its summary.
         const dim3 grid((ctx->cfg.width + kFbmBlock - 1) / kFbmBlock, (ctx->cfg.depth + kFbmBlock - 1) / kFbmBlock,
             std::min<uint32_t>(ctx->cfg.num_envs, 65535));
-        terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, terrain_params(ctx),
+        terrain_fbm_kernel<<<grid, 256, 0, stream>>>(ctx->seeds, ctx->origins, terrain_params(ctx),
             static_cast<int32_t>(ctx->cfg.width), static_cast<int32_t>(ctx->cfg.depth), ctx->cfg.num_envs, env_mask,
             ctx->terrain_top, ctx->col_offset, ctx->entries, ctx->col_summary);
         return cuda_fail(cudaGetLastError(), "terrain_fbm_kernel launch");
@@ -1314,7 +1319,7 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, 
     a.flags = ctx->flags;
     a.park = ctx->park;
     a.n_tiles = n_tiles;
-    a.origin_y = ctx->cfg.origin_y;
+    a.origins = ctx->origins;
     a.W = static_cast<int32_t>(ctx->cfg.width);
     a.D = static_cast<int32_t>(ctx->cfg.depth);
     a.tiles_x = static_cast<int32_t>(ctx->tiles_x);

@@ -25,7 +25,7 @@ struct RenderArgs {
     const uint8_t* light;
     const blk_render_params* params;
     int32_t W, H, D;
-    int32_t ox, oy, oz;
+    const int4* origins; // [env] world coordinates of each env's local (0, 0, 0)
     uint64_t env_stride;
     uint32_t width, height, num_envs;
     uint8_t* out;     // RGBA8 (env, y, x, 4), or nullptr
@@ -220,7 +220,8 @@ __global__ void __launch_bounds__(128) render_kernel(RenderArgs a)
     const float d[3] = { p.right[0] * vx + p.up[0] * vy + p.forward[0], p.right[1] * vx + p.up[1] * vy + p.forward[1],
         p.right[2] * vx + p.up[2] * vy + p.forward[2] };
     // Local coordinates: region cell (0, 0, 0) spans [0, 1)^3.
-    const float o[3] = { p.origin[0] - a.ox, p.origin[1] - a.oy, p.origin[2] - a.oz };
+    const int4 org = a.origins[env];
+    const float o[3] = { p.origin[0] - org.x, p.origin[1] - org.y, p.origin[2] - org.z };
     const int dims[3] = { a.W, a.H, a.D };
     constexpr float kNear = 0.05f;
     // Past the fog end a face takes the sky colour (fog factor 1), which is
@@ -419,7 +420,7 @@ __global__ void __launch_bounds__(128) render_kernel(RenderArgs a)
             / 15.0f;
         float u, v;
         face_uv(hit.face, hit.lx, hit.ly, hit.lz, u, v);
-        const float wx = o[0] + d[0] * hit.s + a.ox, wz = o[2] + d[2] * hit.s + a.oz;
+        const float wx = o[0] + d[0] * hit.s + org.x, wz = o[2] + d[2] * hit.s + org.z;
         float ar, ag, ab;
         texel_color(face_material(hit.block, hit.face), u, v, wx, wz, ar, ag, ab);
         const float fog = saturate_((hit.s - p.fog_start) / fmaxf(p.fog_end - p.fog_start, 0.001f));
@@ -454,9 +455,7 @@ int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width,
     a.W = static_cast<int32_t>(ctx->cfg.width);
     a.H = static_cast<int32_t>(ctx->cfg.height);
     a.D = static_cast<int32_t>(ctx->cfg.depth);
-    a.ox = ctx->cfg.origin_x;
-    a.oy = ctx->cfg.origin_y;
-    a.oz = ctx->cfg.origin_z;
+    a.origins = ctx->origins;
     a.env_stride = ctx->env_stride;
     a.width = width;
     a.height = height;

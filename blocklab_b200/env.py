@@ -57,22 +57,24 @@ class WorldEnv:
         self._version += 1
         return out
 
-    def reset(self, *, seed: int = 1, overrides=None, frames: Optional[torch.Tensor] = None):
+    def reset(self, *, seed: int = 1, overrides=None, frames: Optional[torch.Tensor] = None, origins=None):
         """Regenerates and fully relights every owned world. World i (global
         index) gets the seed of `seed_policy`; overrides are blk_override
-        records with env indices local to this process."""
+        records with env indices local to this process; `origins` (local envs,
+        3) places each world's region (None keeps the current ones)."""
         seeds = env_seeds(seed, self.env_begin, self.config.num_envs, self.seed_policy)
-        self.world.generate(seeds, overrides)
+        self.world.generate(seeds, overrides, origins=origins)
         self._reset_done = True
         obs = self._next_obs(frames)
         return obs, {"observation_version": self._version, "env_begin": self.env_begin}
 
-    def reset_envs(self, env_ids, *, seed: int = 1, overrides=None):
+    def reset_envs(self, env_ids, *, seed: int = 1, overrides=None, origins=None):
         """Regenerates only the listed worlds (indices local to this process);
-        world i gets the seed of its global index, as in reset()."""
+        world i gets the seed of its global index, as in reset(), and, when
+        given, the region origin origins[k] of its list position k."""
         ids = np.asarray(env_ids, np.int64)
         seeds = np.array([env_seeds(seed, self.env_begin + int(i), 1, self.seed_policy)[0] for i in ids], np.uint32)
-        self.world.generate_envs(ids.astype(np.uint32), seeds, overrides)
+        self.world.generate_envs(ids.astype(np.uint32), seeds, overrides, origins=origins)
 
     def render(self, params) -> torch.Tensor:
         """Observation rendered by the library itself: ray-cast RGBA8 frames of

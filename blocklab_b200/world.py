@@ -11,7 +11,11 @@ semantics (src/world/World.cpp:239-287) are applied on the device by
 Device arrays are exposed zero-copy as torch tensors:
     ids, light   (num_envs, D, W, H) uint8   — column-major, y fastest
     height_map   (num_envs, D, W)    int16   — world y of the top solid block
-``light`` packs sky << 4 | block.
+    origins      (num_envs, 4)       int32   — x, y, z of each env's region
+                                               corner (world coordinates), 0
+``light`` packs sky << 4 | block. Every env has its own region origin, set by
+``generate`` / ``generate_envs`` (the reference centres the region on the
+agent on every generation, src/world/WorldGenerator.cpp:13-21).
 """
 from __future__ import annotations
 
@@ -78,6 +82,20 @@ def _stream_handle(stream: Optional[torch.cuda.Stream], device: int) -> int:
     return int(s.cuda_stream)
 
 
+def _origins_ptr(origins, n: int):
+    """(pointer, keep-alive) of an (n, 3) int32 origin list, or (None, None)."""
+    if origins is None:
+        return None, None
+    if isinstance(origins, torch.Tensor):
+        if origins.dtype != torch.int32 or origins.shape != (n, 3):
+            raise ValueError(f"origins must be an ({n}, 3) int32 tensor")
+        return _ptr(origins)
+    arr = np.ascontiguousarray(np.asarray(origins, np.int64).reshape(-1, 3), np.int32)
+    if arr.shape != (n, 3):
+        raise ValueError(f"origins must be ({n}, 3)")
+    return _ptr(arr)
+
+
 def _ptr(obj) -> tuple[int, object]:
     """Pointer + keep-alive for a numpy array or torch tensor (host or device)."""
     if isinstance(obj, torch.Tensor):
@@ -107,6 +125,7 @@ class WorldBatch:
         self.ids = torch.as_tensor(_CudaArray(self, v.ids, (E, D, W, H), "|u1"), device=dev)
         self.light = torch.as_tensor(_CudaArray(self, v.light, (E, D, W, H), "|u1"), device=dev)
         self.height_map = torch.as_tensor(_CudaArray(self, v.height_map, (E, D, W), "<i2"), device=dev)
+        self.origins = torch.as_tensor(_CudaArray(self, v.env_origins, (E, 4), "<i4"), device=dev)
 
     # -- lifetime -------------------------------------------------------------
     def close(self) -> None:
@@ -121,10 +140,13 @@ class WorldBatch:
             pass
 
     # -- the hot path -----------------------------------------------------------
-    def generate(self, env_seeds, overrides=None, stream: Optional[torch.cuda.Stream] = None) -> None:
-        """Full generation + light of every env (reference WorldGenerator::generate)."""
+    def generate(self, env_seeds, overrides=None, origins=None, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Full generation + light of every env (reference WorldGenerator::generate).
+        ``origins`` (num_envs, 3) int32 world coordinates of each env's region
+        corner; None keeps the current ones."""
         seeds_p, keep1 = _ptr(np.asarray(env_seeds, np.uint32) if not isinstance(env_seeds, torch.Tensor)
                               else env_seeds)
+        org_p, keep_o = _origins_ptr(origins, self.config.num_envs)
         if overrides is None:
             ovr_p, n, keep2 = 0, 0, None
         elif isinstance(overrides, torch.Tensor):
@@ -134,18 +156,21 @@ class WorldBatch:
             arr = np.ascontiguousarray(overrides, OVERRIDE_DTYPE)
             ovr_p, keep2 = _ptr(arr)
             n = len(arr)
-        check(N.lib.blk_generate(self._ctx, seeds_p, ovr_p, n, _stream_handle(stream, self.device)))
-        del keep1, keep2
+        check(N.lib.blk_generate(self._ctx, seeds_p, org_p, ovr_p, n, _stream_handle(stream, self.device)))
+        del keep1, keep2, keep_o
 
-    def generate_envs(self, env_ids, env_seeds, overrides=None, stream: Optional[torch.cuda.Stream] = None) -> None:
-        """Regenerates only the listed envs (distinct indices) with their seeds and
-        overrides; the other envs keep their state."""
+    def generate_envs(self, env_ids, env_seeds, overrides=None, origins=None,
+                      stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Regenerates only the listed envs (distinct indices) with their seeds,
+        overrides and, when given, new region origins (len(env_ids), 3); the
+        other envs keep their state."""
         ids_p, keep1 = _ptr(np.asarray(env_ids, np.uint32) if not isinstance(env_ids, torch.Tensor) else env_ids)
         seeds_p, keep2 = _ptr(np.asarray(env_seeds, np.uint32) if not isinstance(env_seeds, torch.Tensor)
                               else env_seeds)
         n_envs = len(env_ids)
         if len(env_seeds) != n_envs:
             raise ValueError("one seed per listed env")
+        org_p, keep_o = _origins_ptr(origins, n_envs)
         if overrides is None:
             ovr_p, n, keep3 = 0, 0, None
         elif isinstance(overrides, torch.Tensor):
@@ -155,8 +180,9 @@ class WorldBatch:
             arr = np.ascontiguousarray(overrides, OVERRIDE_DTYPE)
             ovr_p, keep3 = _ptr(arr)
             n = len(arr)
-        check(N.lib.blk_generate_envs(self._ctx, ids_p, n_envs, seeds_p, ovr_p, n, _stream_handle(stream, self.device)))
-        del keep1, keep2, keep3
+        check(N.lib.blk_generate_envs(self._ctx, ids_p, n_envs, seeds_p, org_p, ovr_p, n,
+                                      _stream_handle(stream, self.device)))
+        del keep1, keep2, keep3, keep_o
 
     def place_torches(self, env_seeds, per_env: int, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """Device override list of `per_env` torches per env on the terrain surface."""

@@ -75,8 +75,8 @@ typedef struct blk_world_config {
     uint32_t width;    /* W: x extent, 1..4096 */
     uint32_t height;   /* H: y extent, multiple of 32, 32..256 */
     uint32_t depth;    /* D: z extent, 1..4096 */
-    int32_t origin_x;  /* world coordinate of local (0, 0, 0), shared by all envs */
-    int32_t origin_y;
+    int32_t origin_x;  /* world coordinate of local (0, 0, 0) of every env until */
+    int32_t origin_y;  /* blk_generate / blk_generate_envs gives it its own      */
     int32_t origin_z;
     int32_t terrain_mode;   /* blk_terrain_mode */
     int32_t fbm_base;
@@ -99,6 +99,8 @@ typedef struct blk_world_views {
     uint8_t* ids;          /* device, num_envs * D * W * H */
     uint8_t* light;        /* device, same shape, sky<<4 | block */
     int16_t* height_map;   /* device, num_envs * D * W */
+    const int32_t* env_origins; /* device, num_envs * 4: x, y, z (world coordinates of
+                                   the env's local (0, 0, 0)) and one unused word */
     uint64_t env_stride;   /* bytes between envs in ids/light */
     uint32_t num_envs, width, height, depth;
 } blk_world_views;
@@ -122,18 +124,27 @@ int blk_views(blk_ctx* ctx, blk_world_views* out);
  * latest in list order wins), height map, sky column fill, block and sky
  * flood fill. Replaces WorldGenerator::generate
  * (src/world/WorldGenerator.h:79-82, src/world/WorldGenerator.cu:673-829) for
- * a whole batch at once. Overrides outside the region are ignored. */
-int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const blk_override* overrides, uint32_t n_overrides,
-    uintptr_t stream);
+ * a whole batch at once. env_origins, when not NULL, holds num_envs * 3
+ * int32 (x, y, z): the world coordinates of each env's region corner, which
+ * the reference sets per call to the agent's block minus the half extent
+ * (src/world/WorldGenerator.cpp:13-21); the origins stay until the next call
+ * that gives them. NULL keeps every env's current origin (initially the
+ * configuration's). Override, edit and query coordinates are world
+ * coordinates; overrides outside their env's region are ignored. */
+int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const int32_t* env_origins, const blk_override* overrides,
+    uint32_t n_overrides, uintptr_t stream);
 
 /* Regenerates and relights only the envs listed in env_ids[n_envs] (distinct
  * indices; out-of-range ones are skipped and reported by blk_sync), with
- * seeds env_seeds[n_envs] and the overrides of those envs (records of other
- * envs are ignored); every other env keeps its state. The batched per-env
- * reset the reference leaves for later (include/blocklab/environment/Environment.h:33);
- * requires a prior blk_generate. Arrays may be host or device memory. */
+ * seeds env_seeds[n_envs], origins env_origins[n_envs * 3] (NULL keeps their
+ * current origins) and the overrides of those envs (records of other envs are
+ * ignored); every other env keeps its state. The batched per-env reset the
+ * reference leaves for later (include/blocklab/environment/Environment.h:33),
+ * and the regeneration of an env whose agent left its cached region
+ * (src/graphics/Renderer.cpp:1115-1141); requires a prior blk_generate. Arrays
+ * may be host or device memory. */
 int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, const uint32_t* env_seeds,
-    const blk_override* overrides, uint32_t n_overrides, uintptr_t stream);
+    const int32_t* env_origins, const blk_override* overrides, uint32_t n_overrides, uintptr_t stream);
 
 /* Writes up to `per_env` torch overrides per env at distinct pseudo-random
  * columns, one cell above the terrain surface (benchmark world construction).
@@ -152,7 +163,8 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
  * TerrainHeader (src/world/WorldGenerator.cu:27-67, :171-178, :221-303;
  * shaders/voxel.vert.hlsl:14-24). Voxels are written in ascending
  * (z, y, x) order. `voxels`, `count` and `header` are device memory. The
- * packing holds x, z < 64 and y < 512, as in the reference. */
+ * packing holds x, z < 64 and y < 512, as in the reference. The header holds
+ * the env's current origin. */
 int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t max_voxels, uint32_t* count,
     int32_t* header, uintptr_t stream);
 

@@ -261,6 +261,20 @@ class Reference:
                     height_map=hm.reshape(D, W).astype(np.int16), voxel_count=int(cnt[0]),
                     voxels=vox.reshape(-1, 3)[:n].copy(), header=tuple(int(v) for v in hdr))
 
+    def light_blocks(self, blocks: np.ndarray, origin=(0, 0, 0), runs: int = 2, timing: Optional[list] = None):
+        """The reference's generator run over a given block volume (D, H, W):
+        every cell is passed as an override, so its terrain formula is bypassed
+        and its block cache, height map and light are computed on these blocks
+        (src/world/WorldGenerator.cu:142-219, :364-588). Needs W, D <= 256 and
+        H <= 128 (uchar3 light-source coordinates, int8 height map); the render
+        voxel list is skipped (its packing needs W, D <= 64)."""
+        D, H, W = blocks.shape
+        z, y, x = np.meshgrid(np.arange(D, dtype=np.int32), np.arange(H, dtype=np.int32),
+                              np.arange(W, dtype=np.int32), indexing="ij")
+        xyz = np.stack([x.ravel() + origin[0], y.ravel() + origin[1], z.ravel() + origin[2]], 1)
+        return self.generate(0, origin, (W, H, D), xyz, np.ascontiguousarray(blocks.ravel(), np.uint8), runs=runs,
+                             max_voxels=0, timing=timing)
+
     def convert_rgba8(self, rgba: np.ndarray) -> np.ndarray:
         n, h, w, _ = rgba.shape
         out = np.zeros((n, 3, h, w), np.float32)

@@ -53,7 +53,7 @@ def test_invalid_config_rejected_without_device():
 def test_null_context_errors():
     from blocklab_b200 import _native as N
 
-    assert N.lib.blk_generate(None, None, None, 0, 0) == 1
+    assert N.lib.blk_generate(None, None, None, None, 0, 0) == 1
     assert N.lib.blk_sync(None, 0) == 1
     assert N.lib.blk_apply_edits(None, None, 0, 0) == 1
     assert N.lib.blk_ctx_destroy(None) == 0

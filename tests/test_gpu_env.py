@@ -30,10 +30,15 @@ def _env(B, **kw):
     return WorldEnv(**args)
 
 
+def _batch_world(wb, e):
+    """(ids, block light, sky light, height map) of env e in the oracle's layout."""
+    ids = wb.ids[e].cpu().numpy().transpose(0, 2, 1)
+    light = wb.light[e].cpu().numpy().transpose(0, 2, 1)
+    return ids, light & 15, light >> 4, wb.height_map[e].cpu().numpy()
+
+
 def _world(env, e):
-    ids = env.world.ids[e].cpu().numpy().transpose(0, 2, 1)
-    light = env.world.light[e].cpu().numpy().transpose(0, 2, 1)
-    return ids, light & 15, light >> 4, env.world.height_map[e].cpu().numpy()
+    return _batch_world(env.world, e)
 
 
 def test_reset_and_step_match_oracle(B, oracle):
@@ -178,3 +183,57 @@ def test_env_renders_its_observations(B):
     assert obs.shape == (3, 3, 24, 32)
     assert torch.equal(obs[:, 1], frames[..., 1].float() * np.float32(1.0 / 255.0))
     env.close()
+
+
+def test_partial_reset_matches_oracle_with_new_origins(B, oracle):
+    """blk_generate_envs against the oracle: a ragged, unordered env list with
+    new seeds and new region origins per listed env, overrides of listed and
+    unlisted envs (the unlisted ones are ignored), then an empty list and a
+    list holding an out-of-range id (its valid entries are still reset)."""
+    W2, H2, D2, E2 = 45, 96, 38, 5
+    base = dict(terrain=TERRAIN_FBM, base=40, amplitude=30.0)
+    cfg = B.WorldConfig(num_envs=E2, width=W2, height=H2, depth=D2, origin=(0, 0, 0), **base)
+    rng = np.random.default_rng(21)
+    wb = B.WorldBatch(cfg)
+    seeds = np.arange(31, 31 + E2, dtype=np.uint32)
+    wb.generate(seeds)
+
+    def random_overrides(e, origin, n=400):
+        cells = rng.choice(W2 * H2 * D2, n, replace=False)
+        xyz = np.stack([cells % W2, (cells // W2) % H2, cells // (W2 * H2)], 1) + np.array(origin)
+        blk = rng.choice([0, 3, 4, 1, 2], n, p=[0.45, 0.3, 0.15, 0.05, 0.05]).astype(np.uint8)
+        return xyz, blk
+
+    listed = [4, 0, 2]
+    new_seeds = np.array([501, 502, 503], np.uint32)
+    new_origins = np.array([[-100, -8, 7], [3, 5, -2000], [64, 0, 64]], np.int32)
+    per, lists = {}, []
+    for k, e in enumerate(listed):
+        per[e] = random_overrides(e, new_origins[k])
+        lists.append(B.make_overrides(*per[e], env=e))
+    for e in (1, 3):  # records of envs that are not reset
+        lists.append(B.make_overrides(*random_overrides(e, (0, 0, 0)), env=e))
+    ovr = np.concatenate(lists)
+    rng.shuffle(ovr)
+    before = (wb.ids[[1, 3]].clone(), wb.light[[1, 3]].clone(), wb.height_map[[1, 3]].clone())
+    wb.generate_envs(listed, new_seeds, ovr, origins=new_origins)
+    wb.sync()
+    for k, e in enumerate(listed):
+        spec = WorldSpec(int(new_seeds[k]), W2, H2, D2, origin=tuple(int(v) for v in new_origins[k]), **base)
+        blocks, bl, sl, hm = oracle.generate(spec, *per[e], method="multi")
+        got = _batch_world(wb, e)
+        assert np.array_equal(got[0], blocks) and np.array_equal(got[3], hm), e
+        assert np.array_equal(got[1], bl) and np.array_equal(got[2], sl), e
+        assert wb.origins[e, :3].tolist() == new_origins[k].tolist()
+    assert torch.equal(wb.ids[[1, 3]], before[0]) and torch.equal(wb.light[[1, 3]], before[1])
+    assert torch.equal(wb.height_map[[1, 3]], before[2])
+    wb.generate_envs([], [])
+    wb.sync()
+    wb.generate_envs([7, 1], [900, 901])
+    with pytest.raises(B.BlkError):
+        wb.sync()
+    spec = WorldSpec(901, W2, H2, D2, origin=(0, 0, 0), **base)
+    blocks, bl, sl, hm = oracle.generate(spec, method="multi")
+    got = _batch_world(wb, 1)
+    assert np.array_equal(got[0], blocks) and np.array_equal(got[1], bl) and np.array_equal(got[2], sl)
+    wb.close()

@@ -131,3 +131,45 @@ def test_snapshot_restores_world(B, oracle, tmp_path):
     assert N.lib.blk_snapshot_overrides(wb._ctx, 0, out.data_ptr(), 5, host.ctypes.data, 0) == 1
     for w in (wb, wb2, wb3):
         w.close()
+
+
+def test_readback_ranges(B, oracle):
+    """blk_readback copies an env range of the resident arrays to host memory
+    (the reference copies its whole block cache after every generation,
+    src/world/WorldGenerator.cu:798-815): equal to the device arrays and to
+    the oracle's world; outputs left out stay untouched; bad ranges fail."""
+    rng = np.random.default_rng(5)
+    cfg = B.WorldConfig(num_envs=4, width=W, height=H, depth=D, origin=ORIGIN, terrain=TERRAIN_FBM, base=30,
+                        amplitude=18.0)
+    wb = B.WorldBatch(cfg)
+    seeds = rng.integers(1, 1 << 31, 4).astype(np.uint32)
+    wb.generate(seeds, wb.place_torches(seeds, 40))
+    wb.sync()
+    ids, light, hm = wb.readback(1, 2)
+    torch.cuda.synchronize()
+    assert ids.shape == (2, D, W, H) and hm.shape == (2, D, W)
+    assert torch.equal(ids, wb.ids[1:3].cpu()) and torch.equal(light, wb.light[1:3].cpu())
+    assert torch.equal(hm, wb.height_map[1:3].cpu())
+    tl = wb.place_torches(seeds, 40).cpu().numpy().view(B.OVERRIDE_DTYPE)
+    for k, e in enumerate((1, 2)):
+        sel = tl[(tl["env"] == e) & (tl["y"] > -(1 << 30))]
+        spec = WorldSpec(int(seeds[e]), W, H, D, origin=ORIGIN, terrain=TERRAIN_FBM, base=30, amplitude=18.0)
+        blocks, bl, sl, hmap = oracle.generate(spec, np.stack([sel["x"], sel["y"], sel["z"]], 1), sel["block"],
+                                               method="multi")
+        l = light[k].numpy().transpose(0, 2, 1)
+        assert np.array_equal(ids[k].numpy().transpose(0, 2, 1), blocks)
+        assert np.array_equal(l & 15, bl) and np.array_equal(l >> 4, sl)
+        assert np.array_equal(hm[k].numpy(), hmap)
+    _, light_only, _ = wb.readback(3, 1, ids=False, height_map=False)
+    torch.cuda.synchronize()
+    assert torch.equal(light_only, wb.light[3:4].cpu())
+    # device destination through the C ABI
+    dst = torch.zeros((1, D, W, H), dtype=torch.uint8, device="cuda")
+    from blocklab_b200 import _native as N
+
+    N.check(N.lib.blk_readback(wb._ctx, 0, 1, dst.data_ptr(), None, None, 0))
+    torch.cuda.synchronize()
+    assert torch.equal(dst, wb.ids[0:1])
+    with pytest.raises(B.BlkError):
+        wb.readback(3, 2)
+    wb.close()

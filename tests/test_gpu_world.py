@@ -284,6 +284,57 @@ def test_reference_terrain_matches_reference_cuda_build(B):
     wb.close()
 
 
+def test_reference_terrain_with_torches_per_env_origins(B, oracle):
+    """Config 0's region (64 x 128 x 64) in reference-terrain mode with 200
+    surface torches, one batch whose envs each sit at their own origin (as the
+    reference centres each env's region on its agent,
+    src/world/WorldGenerator.cpp:13-21), against the reference's own sm_100a
+    build per env: ids, height map, both lights and the render voxel list
+    (src/world/WorldGenerator.cu:171-588, :221-303)."""
+    from oracle.oracle import Reference, ref_available
+
+    if not ref_available("cuda"):
+        pytest.skip("reference CUDA build not present")
+    R = Reference("cuda")
+    W, H, D = 64, 128, 64
+    seeds = [1, 23, 4242, 77]
+    origins = np.array([[-32, 0, -32], [1000, -6, -77], [-4083, 3, 2048], [37, -20, 91]], np.int32)
+    cfg = B.WorldConfig(num_envs=len(seeds), width=W, height=H, depth=D, terrain=B.TERRAIN_REFERENCE,
+                        max_overrides=4096)
+    wb = B.WorldBatch(cfg)
+    torches = [oracle.place_torches(WorldSpec(s, W, H, D, origin=tuple(o), terrain=TERRAIN_REFERENCE), 200,
+                                    B.torch_key(s)) for s, o in zip(seeds, origins)]
+    assert all(len(t) == 200 for t in torches)
+    ovr = np.concatenate([B.make_overrides(t, B.TORCH, env=e) for e, t in enumerate(torches)])
+    wb.generate(np.array(seeds, np.uint32), ovr, origins=origins)
+    wb.sync()
+    assert np.array_equal(wb.origins.cpu().numpy()[:, :3], origins)
+    for e, s in enumerate(seeds):
+        r = R.generate(s, tuple(origins[e]), (W, H, D), torches[e], np.full(200, 4, np.uint8), runs=2,
+                       max_voxels=W * H * D)
+        _assert_world(wb, e, r["blocks"], r["block_light"], r["sky_light"], r["height_map"], f"env{e}")
+        assert (r["block_light"] > 0).sum() > 10000
+        vox, n, hdr = wb.render_voxels(e)
+        assert hdr == tuple(int(v) for v in origins[e]) == r["header"]
+        v = vox.cpu().numpy().view(np.uint32)
+        key = lambda a: a[np.lexsort((a[:, 2], a[:, 1], a[:, 0]))]
+        assert n == r["voxel_count"] and np.array_equal(key(v), key(r["voxels"]))
+    # Moving two envs' regions (their agents walked off): the other envs keep
+    # their worlds, the moved ones match the reference at the new origins.
+    moved = np.array([[-28, 0, -40], [995, -6, -60]], np.int32)
+    before = wb.ids[[0, 3]].clone()
+    t_new = [oracle.place_torches(WorldSpec(seeds[e], W, H, D, origin=tuple(o), terrain=TERRAIN_REFERENCE), 200,
+                                  B.torch_key(seeds[e])) for e, o in zip((1, 2), moved)]
+    wb.generate_envs([1, 2], [seeds[1], seeds[2]], np.concatenate(
+        [B.make_overrides(t, B.TORCH, env=e) for e, t in zip((1, 2), t_new)]), origins=moved)
+    wb.sync()
+    assert torch.equal(wb.ids[[0, 3]], before)
+    for k, e in enumerate((1, 2)):
+        r = R.generate(seeds[e], tuple(moved[k]), (W, H, D), t_new[k], np.full(200, 4, np.uint8), runs=2)
+        _assert_world(wb, e, r["blocks"], r["block_light"], r["sky_light"], r["height_map"], f"moved env{e}")
+    wb.close()
+
+
 # ------------------------------------------------------ edits and relight --
 def _edit_batch(rng, E, W, H, D, n, origin, hm_list):
     lists, local = [], []
@@ -547,6 +598,76 @@ def test_full_size_config1(B, oracle):
         spec = WorldSpec(int(seeds[e]), 256, 128, 256)
         blocks, bl, sl, hm = oracle.generate(spec, _xyz(sel), sel["block"], method="multi")
         _assert_world(wb, e, blocks, bl, sl, hm, f"env{e}")
+    wb.close()
+
+
+def test_daynight_shape_cell_for_cell(B, oracle):
+    """The day/night workload's worlds (128 x 96 x 128 with 300 surface torches),
+    six envs of the benchmark's seeds, cell for cell against the oracle."""
+    E, W, H, D = 6, 128, 96, 128
+    cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, max_overrides=E * 300)
+    wb = B.WorldBatch(cfg)
+    seeds = np.arange(1, 1 + E, dtype=np.uint32)
+    t = wb.place_torches(seeds, 300)
+    wb.generate(seeds, t)
+    wb.sync()
+    tn = t.cpu().numpy().view(B.OVERRIDE_DTYPE)
+    for e in range(E):
+        sel = tn[(tn["env"] == e) & (tn["y"] > -(1 << 30))]
+        assert len(sel) == 300
+        blocks, bl, sl, hm = oracle.generate(WorldSpec(int(seeds[e]), W, H, D), _xyz(sel), sel["block"],
+                                             method="multi")
+        _assert_world(wb, e, blocks, bl, sl, hm, f"env{e}")
+    wb.close()
+
+
+def test_relight_shape_edit_steps_cell_for_cell(B, oracle):
+    """The relight workload's worlds (128^3, 200 surface torches) through six
+    steps of its edit mix (45 % dig, 45 % stone, 5 % torch, 5 % removal of an
+    existing torch, within 8 of the surface): four steps at its density (about
+    ten edits per env: relight boxes) and two dense ones (whole dirty tiles),
+    every env cell for cell against the oracle's full relight."""
+    E, W, H, D = 5, 128, 128, 128
+    cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, max_overrides=E * 200, max_edits=E * 400)
+    wb = B.WorldBatch(cfg)
+    seeds = np.arange(1, 1 + E, dtype=np.uint32)
+    t = wb.place_torches(seeds, 200)
+    wb.generate(seeds, t)
+    tn = t.cpu().numpy().view(B.OVERRIDE_DTYPE)
+    state, torches = [], []
+    for e in range(E):
+        sel = tn[(tn["env"] == e) & (tn["y"] > -(1 << 30))]
+        torches.append(_xyz(sel))
+        state.append(list(oracle.build_blocks(WorldSpec(int(seeds[e]), W, H, D), _xyz(sel), sel["block"])))
+    rng = np.random.default_rng(17)
+    for step, per_env in enumerate([10, 10, 10, 10, 400, 400]):
+        lists, local = [], []
+        for e in range(E):
+            x, z = rng.integers(0, W, per_env), rng.integers(0, D, per_env)
+            y = state[e][1][z, x].astype(np.int64) + rng.integers(-8, 9, per_env)
+            r = rng.random(per_env)
+            blk = np.where(r < 0.45, 0, np.where(r < 0.9, 3, 4)).astype(np.uint8)
+            kind = np.zeros(per_env, np.uint8)
+            rm = r >= 0.95
+            pick = torches[e][rng.integers(0, len(torches[e]), int(rm.sum()))]
+            x[rm], y[rm], z[rm] = pick[:, 0], pick[:, 1], pick[:, 2]
+            blk[rm], kind[rm] = 0, 1
+            xyz = np.stack([x, y, z], 1)
+            local.append((xyz, kind, blk))
+            lists.append(B.make_overrides(xyz, blk, env=e, kind=kind))
+        ovr = np.concatenate(lists)
+        # Envs interleaved at random, each env's edits kept in their order.
+        slots = ovr["env"][rng.permutation(len(ovr))]
+        mixed = np.empty_like(ovr)
+        for e in range(E):
+            mixed[slots == e] = ovr[ovr["env"] == e]
+        wb.apply_edits(mixed)
+        wb.sync()
+        for e in range(E):
+            xyz, kind, blk = local[e]
+            oracle.apply_edits(state[e][0], state[e][1], xyz, kind, blk)
+            bl, sl = oracle.light(state[e][0], state[e][1], 0, "multi")
+            _assert_world(wb, e, state[e][0], bl, sl, state[e][1], f"step{step} env{e}")
     wb.close()
 
 
