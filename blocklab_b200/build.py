@@ -17,8 +17,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libblk_world.so")
-SOURCES = ["blk_light.cu", "blk_api.cu", "blk_render.cu"]
-HEADERS = ["blk_common.cuh", "blk_internal.h"]
+SOURCES = ["blk_light.cu", "blk_relight.cu", "blk_api.cu", "blk_render.cu"]
+HEADERS = ["blk_common.cuh", "blk_bits.cuh", "blk_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -321,42 +321,12 @@ struct EditArgs {
     const blk_override* edits;
     const uint32_t* env_offset;
     uint32_t* order;
-    uint4* changes;    // 2 per edit: the cells it changed (x | z << 16, y | old << 16 | new << 24, rows ylo | yhi << 16, valid)
+    uint4* changes;    // 2 per edit: the cells it changed (x | z << 16, y | old << 16 | new << 24, rows ylo | yhi << 16, flags)
     uint8_t* ids;
     int16_t* hmap;
-    uint32_t* win_lo;  // per env tile, atomicMin
-    uint32_t* win_hi;  // per env tile, atomicMax
-    uint4* boxes;      // one relight box per changed cell
-    uint32_t* box_count;
-    uint32_t box_capacity;
     RegionDims r;
     uint64_t env_stride;
-    uint32_t tiles_x, tiles_z;
 };
-
-// Records the cells whose light a change at (x, z), rows ylo..yhi, can alter:
-// rows ylo - 14 .. yhi + 14 of the columns within 14 of (x, z). Two forms are
-// kept and the relight uses the smaller: per-tile row windows (every tile the
-// columns touch), and a 32 x 32-column box around the change (x0 = x - 15
-// clamped to the region holds x - 14 .. x + 14).
-__device__ void mark_dirty(const EditArgs& a, uint32_t env, int32_t x, int32_t z, int32_t ylo, int32_t yhi)
-{
-    const int32_t lo = max(ylo - kMaxDistance, 0), hi = min(yhi + kMaxDistance, a.r.H - 1);
-    const uint32_t b = atomicAdd(a.box_count, 1u);
-    if (b < a.box_capacity) {
-        const int32_t bx = max(min(x - 15, a.r.W - 32), 0), bz = max(min(z - 15, a.r.D - 32), 0);
-        a.boxes[b] = make_uint4(env, static_cast<uint32_t>(bx) | (static_cast<uint32_t>(bz) << 16),
-            static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16), 0u);
-    }
-    const int32_t tx0 = max(x - kMaxDistance, 0) / 32, tx1 = min(x + kMaxDistance, a.r.W - 1) / 32;
-    const int32_t tz0 = max(z - kMaxDistance, 0) / 32, tz1 = min(z + kMaxDistance, a.r.D - 1) / 32;
-    for (int32_t tz = tz0; tz <= tz1; ++tz)
-        for (int32_t tx = tx0; tx <= tx1; ++tx) {
-            const uint64_t t = static_cast<uint64_t>(env) * a.tiles_x * a.tiles_z + static_cast<uint64_t>(tz) * a.tiles_x + tx;
-            atomicMin(a.win_lo + t, static_cast<uint32_t>(lo));
-            atomicMax(a.win_hi + t, static_cast<uint32_t>(hi));
-        }
-}
 
 // One thread per env: sort the env's edit indices (insertion sort restores
 // input order after the atomic scatter), then apply them sequentially with
@@ -476,20 +446,7 @@ __global__ void mark_changes_kernel(EditArgs a)
             && opaque_at(x + 1, y, z) && opaque_at(x, y - 1, z) && opaque_at(x, y + 1, z) && opaque_at(x, y, z - 1)
             && opaque_at(x, y, z + 1);
         if (!enclosed)
-            mark_dirty(a, env, x, z, static_cast<int32_t>(c.z & 0xFFFFu), static_cast<int32_t>(c.z >> 16));
-    }
-}
-
-__global__ void dirty_compact_kernel(const uint32_t* win_lo, const uint32_t* win_hi, uint64_t n_tiles,
-    uint32_t* window, uint32_t* list, uint32_t* count)
-{
-    for (uint64_t t = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; t < n_tiles;
-         t += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        const uint32_t lo = win_lo[t], hi = win_hi[t];
-        if (lo <= hi && hi != 0xFFFFFFFFu) {
-            window[t] = lo | (hi << 16);
-            list[atomicAdd(count, 1u)] = static_cast<uint32_t>(t);
-        }
+            a.changes[i].w = c.w | 2u; // marked: its dirty cube joins the env's relight regions
     }
 }
 
@@ -972,8 +929,8 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
     ctx->box_capacity = 2 * std::max<uint32_t>(c.max_edits, 1);
-    A(dalloc(&ctx->boxes, ctx->box_capacity, "relight boxes"));
-    A(dalloc(&ctx->box_count, 1, "relight box count"));
+    A(dalloc(&ctx->region_lists, 4ull * ctx->box_capacity, "relight region lists"));
+    A(dalloc(&ctx->region_counts, 4, "relight region counts"));
     A(dalloc(&ctx->render_params, envs, "render parameters"));
     A(dalloc(&ctx->col_summary, envs * ctx->columns_per_env, "column summaries"));
     A(dalloc(&ctx->env_mask, envs, "partial reset env mask"));
@@ -988,6 +945,7 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
         }
         ctx->park_ctas = static_cast<uint32_t>(sms);
         A(dalloc(&ctx->park, static_cast<size_t>(sms) * 16 * 1024, "tile scratch"));
+        A(dalloc(&ctx->region_park, static_cast<size_t>(sms) * region_park_words_per_sm(), "region relight scratch"));
     }
     if (rc == BLK_OK) {
         if (cudaMallocHost(reinterpret_cast<void**>(&ctx->h_flags), sizeof(uint32_t)) != cudaSuccess
@@ -1037,7 +995,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
             cudaEventDestroy(ev);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->origins, ctx->origin_stage, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order, ctx->edit_changes,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->boxes, ctx->box_count, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->region_lists, ctx->region_counts, ctx->region_park, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -1233,11 +1191,6 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     BLK_CUDA(cudaMemsetAsync(ctx->edit_env_count, 0, (envs + 1) * sizeof(uint32_t), st), "memset edit cursors");
     edit_scatter_kernel<<<grid_for(n_edits, 256), 256, 0, st>>>(e, n_edits, envs, ctx->edit_env_offset,
         ctx->edit_env_count, ctx->edit_order);
-    const uint64_t n_tiles = static_cast<uint64_t>(envs) * ctx->tiles_x * ctx->tiles_z;
-    uint32_t* win_lo = ctx->dirty_window;
-    uint32_t* win_hi = ctx->dirty_window + n_tiles;
-    BLK_CUDA(cudaMemsetAsync(win_lo, 0xFF, n_tiles * sizeof(uint32_t), st), "memset windows");
-    BLK_CUDA(cudaMemsetAsync(win_hi, 0, n_tiles * sizeof(uint32_t), st), "memset windows");
     EditArgs a;
     a.edits = e;
     a.env_offset = ctx->edit_env_offset;
@@ -1245,16 +1198,8 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     a.changes = ctx->edit_changes;
     a.ids = ctx->ids;
     a.hmap = ctx->hmap;
-    a.win_lo = win_lo;
-    a.win_hi = win_hi;
-    a.boxes = ctx->boxes;
-    a.box_count = ctx->box_count;
-    a.box_capacity = ctx->box_capacity;
     a.r = region(ctx);
     a.env_stride = ctx->env_stride;
-    a.tiles_x = ctx->tiles_x;
-    a.tiles_z = ctx->tiles_z;
-    BLK_CUDA(cudaMemsetAsync(ctx->box_count, 0, sizeof(uint32_t), st), "memset box count");
     apply_edits_kernel<<<(envs + 127) / 128, 128, 0, st>>>(a);
     mark_changes_kernel<<<grid_for(2ull * n_edits, 256), 256, 0, st>>>(a);
     BLK_CUDA(cudaGetLastError(), "apply edits launch");
@@ -1736,21 +1681,6 @@ void prof_mark(blk_ctx* ctx, int mark, int which, cudaStream_t stream)
 {
     if (mark >= 0 && mark < static_cast<int>(ctx->marks.size()))
         cudaEventRecord(ctx->marks[mark].e[which], stream);
-}
-
-int launch_relight(blk_ctx* ctx, cudaStream_t st)
-{
-    const uint64_t n_tiles = static_cast<uint64_t>(ctx->cfg.num_envs) * ctx->tiles_x * ctx->tiles_z;
-    uint32_t* win_lo = ctx->dirty_window;
-    uint32_t* win_hi = ctx->dirty_window + n_tiles;
-    BLK_CUDA(cudaMemsetAsync(ctx->dirty_count, 0, sizeof(uint32_t), st), "memset dirty count");
-    // Pack windows in place into win_lo's slots: window[t] = lo | hi << 16.
-    dirty_compact_kernel<<<grid_for(n_tiles, 256), 256, 0, st>>>(win_lo, win_hi, n_tiles, win_lo, ctx->dirty_list,
-        ctx->dirty_count);
-    BLK_CUDA(cudaGetLastError(), "dirty compact launch");
-    // One CTA per tile of the batch; CTAs past the device-side dirty count exit
-    // at once, so no host round trip is needed.
-    return launch_tiles(ctx, 1, static_cast<uint32_t>(n_tiles), st);
 }
 
 } // namespace blk

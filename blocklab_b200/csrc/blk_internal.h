@@ -51,8 +51,9 @@ struct blk_ctx {
     uint32_t* dirty_window = nullptr;     // [num_envs * tiles] packed ylo | yhi<<16, 0xFFFFFFFF = clean
     uint32_t* dirty_list = nullptr;       // [num_envs * tiles] dirty tile ids
     uint32_t* dirty_count = nullptr;      // [1]
-    uint4* boxes = nullptr;               // [box_capacity] relight boxes: env, x0 | z0 << 16, ylo | yhi << 16
-    uint32_t* box_count = nullptr;        // [1]
+    uint4* region_lists = nullptr;        // [4][box_capacity] relight regions by size class (see blk_relight.cu)
+    uint32_t* region_counts = nullptr;    // [4]
+    uint32_t* region_park = nullptr;      // region kernels' scratch: parked block counters per CTA
     uint32_t box_capacity = 0;            // 2 * max_edits (an edit changes at most two cells)
     uint32_t* h_dirty_count = nullptr;    // pinned [1]
 
@@ -73,6 +74,39 @@ struct blk_ctx {
 };
 
 namespace blk {
+
+// Region relight (blk_relight.cu): inputs of the per-env region build.
+struct RegionBuildArgs {
+    const uint4* changes;       // change records of the edit step (two per env-grouped edit position)
+    const uint32_t* env_offset; // [num_envs + 1] edit positions per env
+    uint32_t num_envs;
+    int32_t W, H, D;
+    uint4* lists[4];            // region lists by size class
+    uint32_t* counts;           // [4]
+    uint32_t capacity;          // entries per list
+    uint32_t* win_lo;           // tile path: per env tile dirty rows (atomicMin / atomicMax)
+    uint32_t* win_hi;
+    int32_t tiles_x, tiles_z;
+    uint32_t* flags;
+};
+
+struct RegionRelightArgs {
+    const uint8_t* ids;
+    uint8_t* light;
+    const int16_t* hmap;
+    const int4* origins;
+    int32_t W, H, D;
+    uint64_t env_stride;
+    uint64_t columns;           // per env
+    const uint4* regions;       // this kernel's list and its count
+    const uint32_t* count;
+    uint32_t capacity;
+    uint32_t* park;
+};
+
+uint64_t region_park_words_per_sm();
+int launch_region_build(blk_ctx* ctx, const RegionBuildArgs& a, cudaStream_t stream);
+int launch_region_relight(blk_ctx* ctx, cudaStream_t stream);
 
 void set_error(const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);

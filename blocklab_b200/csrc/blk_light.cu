@@ -1,6 +1,6 @@
 // Fused world generation + exact sky/block light for one 32x32-column tile
-// per CTA step, and the same kernel in relight mode over dirty tiles or over
-// 32x32-column boxes around changed cells.
+// per CTA step, and the same kernel in relight mode over the dirty tiles of
+// relight regions too large for the region kernels (blk_relight.cu).
 //
 // Light model (reference: src/world/WorldGenerator.cu:364-588). The reference
 // runs one breadth-first search per light source over a 29^3 cube and
@@ -42,6 +42,7 @@
 // walking the tiles), and every warp writes its 32 finished columns
 // (contiguous in memory) with coalesced 16-byte stores from a shared staging
 // area.
+#include "blk_bits.cuh"
 #include "blk_internal.h"
 
 namespace blk {
@@ -73,9 +74,6 @@ struct TileArgs {
     const uint32_t* dirty_list;
     const uint32_t* dirty_window;
     const uint32_t* dirty_count;
-    const uint4* boxes;             // relight boxes (see mark_dirty) and their count
-    const uint32_t* box_count;
-    uint32_t box_capacity;
     uint32_t* flags;
     uint32_t* park;                 // per-CTA scratch for block planes during a sky flood
     const int4* origins;            // [env] world coordinates of each env's local (0, 0, 0)
@@ -84,7 +82,7 @@ struct TileArgs {
     int32_t tiles_x, tiles_z;
     uint64_t env_stride;
     uint64_t columns;
-    int32_t mode; // 0 = generate, 1 = relight dirty tiles or boxes from the resident ids
+    int32_t mode; // 0 = generate, 1 = relight dirty tiles from the resident ids
     int32_t listed; // mode 0: tiles from dirty_list (0xFFFFFFFF = skip) instead of all
 };
 
@@ -122,22 +120,6 @@ struct Smem {
     __device__ uint32_t* O() { return pool; }
     __device__ uint32_t* B(int i) { return pool + (1 + i) * kPlane; }
 };
-
-// Rows r of 32 as 4-bit levels given as bit planes (bit r of p_k = bit k of the
-// level of row r): nibble j of n_k = level of row 4j + k. Pairs bits of even and
-// odd rows, then pairs of pairs (a bit-matrix transpose by masked shifts).
-__device__ inline void level_nibbles(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3, uint32_t& n0, uint32_t& n1,
-    uint32_t& n2, uint32_t& n3)
-{
-    const uint32_t e01 = (p0 & 0x55555555u) | ((p1 << 1) & 0xAAAAAAAAu); // pair i: row 2i, bits 0, 1
-    const uint32_t o01 = ((p0 >> 1) & 0x55555555u) | (p1 & 0xAAAAAAAAu); // pair i: row 2i + 1
-    const uint32_t e23 = (p2 & 0x55555555u) | ((p3 << 1) & 0xAAAAAAAAu);
-    const uint32_t o23 = ((p2 >> 1) & 0x55555555u) | (p3 & 0xAAAAAAAAu);
-    n0 = (e01 & 0x33333333u) | ((e23 << 2) & 0xCCCCCCCCu);
-    n2 = ((e01 >> 2) & 0x33333333u) | (e23 & 0xCCCCCCCCu);
-    n1 = (o01 & 0x33333333u) | ((o23 << 2) & 0xCCCCCCCCu);
-    n3 = ((o01 >> 2) & 0x33333333u) | (o23 & 0xCCCCCCCCu);
-}
 
 // Light bytes of 32 rows (out[q] holds rows 4q .. 4q + 3, one byte each) from
 // the block level bit planes b and either the sky level bit planes s
@@ -196,14 +178,6 @@ __device__ inline void light_bytes(const uint32_t (&b)[4], const uint32_t (&s)[4
 __device__ inline uint32_t entry_y(uint64_t e) { return static_cast<uint32_t>(e >> 40); }
 __device__ inline uint8_t entry_block(uint64_t e) { return static_cast<uint8_t>(e & 0xFF); }
 
-// Bits j of the word starting at row ybase where ybase + j > top.
-__device__ inline uint32_t above_mask(int32_t ybase, int32_t top)
-{
-    // ~0 << k for the first open bit k, clamped to 0..32 (the funnel shift
-    // clamps shifts above 32: k >= 32 gives 0).
-    return __funnelshift_lc(0u, 0xFFFFFFFFu, static_cast<uint32_t>(max(top - ybase + 1, 0)));
-}
-
 // Bits j of the word starting at row ybase with ybase + j < H.
 __device__ inline uint32_t inside_mask(int32_t ybase, int32_t H)
 {
@@ -234,12 +208,6 @@ __device__ inline int cone_distance(int c)
 }
 
 __device__ inline bool in_world(const TileArgs& a, int gx, int gz) { return gx >= 0 && gz >= 0 && gx < a.W && gz < a.D; }
-
-// 0x80 in every byte of x that is zero (bytes below 0x80: adding 0x7F carries
-// into bit 7 exactly when the byte is non-zero, and never into the next byte).
-__device__ inline uint32_t zero_bytes(uint32_t x) { return ((x + 0x7F7F7F7Fu) & 0x80808080u) ^ 0x80808080u; }
-// Bit 7 of each byte -> 4 packed bits.
-__device__ inline uint32_t pack4_hi(uint32_t m) { return ((m >> 7) * 0x10204080u) >> 28; }
 
 // Open-cell and torch bits of the 32 rows held in v (two 16-byte chunks of a
 // resident id column, ids 0..4): open = Air or Torch (id & ~4 == 0).
@@ -949,38 +917,22 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem<NW>& s = *reinterpret_cast<Smem<NW>*>(smem_raw);
-    // Relight works on boxes when there are no more of them than dirty tiles
-    // (sparse edits), else on the dirty tiles. Every CTA reads the same counts.
-    uint32_t n = a.n_tiles;
-    bool boxes = false;
-    if (MODE != 0) {
-        const uint32_t nb = *a.box_count, nt = *a.dirty_count;
-        boxes = nb <= a.box_capacity && nb <= nt;
-        n = boxes ? nb : nt;
-    }
+    // Relight works on the dirty tiles (regions too large for the region
+    // kernels). Every CTA reads the same count.
+    const uint32_t n = MODE != 0 ? *a.dirty_count : a.n_tiles;
     const uint32_t tiles_per_env = static_cast<uint32_t>(a.tiles_x * a.tiles_z);
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
-        uint32_t env;
-        int x0, z0;
         int32_t wlo_rows = 0, whi_rows = 32 * NW - 1;
         uint32_t win = 0;
-        if (boxes) {
-            const uint4 b = a.boxes[i];
-            env = b.x;
-            x0 = static_cast<int>(b.y & 0xFFFFu);
-            z0 = static_cast<int>(b.y >> 16);
-            win = b.z;
-        } else {
-            const uint32_t tile_id = MODE == 0 && !a.listed ? i : a.dirty_list[i];
-            if (tile_id == 0xFFFFFFFFu)
-                continue; // uniform over the CTA
-            env = tile_id / tiles_per_env;
-            const uint32_t t_in_env = tile_id % tiles_per_env;
-            x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
-            z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
-            if (MODE != 0)
-                win = a.dirty_window[tile_id];
-        }
+        const uint32_t tile_id = MODE == 0 && !a.listed ? i : a.dirty_list[i];
+        if (tile_id == 0xFFFFFFFFu)
+            continue; // uniform over the CTA
+        const uint32_t env = tile_id / tiles_per_env;
+        const uint32_t t_in_env = tile_id % tiles_per_env;
+        const int x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
+        const int z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
+        if (MODE != 0)
+            win = a.dirty_window[tile_id];
         if (MODE != 0) {
             wlo_rows = static_cast<int32_t>(win & 0xFFFFu) & ~15;
             whi_rows = min(static_cast<int32_t>(win >> 16) | 15, 32 * NW - 1);
@@ -1313,9 +1265,6 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, 
     a.dirty_list = ctx->dirty_list;
     a.dirty_window = ctx->dirty_window;
     a.dirty_count = ctx->dirty_count;
-    a.boxes = ctx->boxes;
-    a.box_count = ctx->box_count;
-    a.box_capacity = ctx->box_capacity;
     a.flags = ctx->flags;
     a.park = ctx->park;
     a.n_tiles = n_tiles;

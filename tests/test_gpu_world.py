@@ -493,6 +493,35 @@ def test_shaft_filled_bottom_up_in_one_step(B, oracle):
     wb.close()
 
 
+@pytest.mark.parametrize("axis", [0, 1, 2])
+def test_relight_regions_at_merge_distance(B, oracle, axis):
+    """Changes whose dirty cubes (L-inf 14 around each) are 28 .. 31 cells
+    apart along one axis: at 29 and closer the cubes touch and their regions
+    merge; at 30 and 31 they stay apart and share (30) or neighbour (31) a
+    boundary layer whose light no change can reach. Torches and digs in open
+    air and under ground, at the world's edges too, over three steps."""
+    W, H, D = 100, 96, 100
+    cfg = B.WorldConfig(num_envs=4, width=W, height=H, depth=D, terrain=TERRAIN_FLAT, base=40)
+    wb = B.WorldBatch(cfg)
+    wb.generate([1, 2, 3, 4])
+    state = [list(oracle.build_blocks(WorldSpec(s, W, H, D, terrain=TERRAIN_FLAT, base=40))) for s in (1, 2, 3, 4)]
+    for step, (y_a, blk) in enumerate([(48, 4), (40, 0), (48, 0)]):  # torches in air, dig the top, remove
+        lists, local = [], []
+        for e, gap in enumerate((28, 29, 30, 31)):
+            xyz = np.array([[20, y_a, 20], [20, y_a, 20], [0, y_a, 99]])
+            xyz[1, axis] += gap if axis != 1 else -gap  # vertical pairs go down, staying in the world
+            b = np.full(len(xyz), blk, np.uint8)
+            local.append((xyz, b))
+            lists.append(B.make_overrides(xyz, b, env=e))
+            oracle.apply_edits(state[e][0], state[e][1], xyz, np.zeros(len(xyz), np.uint8), b)
+        wb.apply_edits(np.concatenate(lists))
+        wb.sync()
+        for e in range(4):
+            bl, sl = oracle.light(state[e][0], state[e][1], 0, "multi")
+            _assert_world(wb, e, state[e][0], bl, sl, state[e][1], f"axis{axis} step{step} env{e}")
+    wb.close()
+
+
 def test_apply_edits_requires_generate_and_capacity(B):
     cfg = B.WorldConfig(num_envs=1, width=32, height=32, depth=32, max_overrides=4, max_edits=2)
     wb = B.WorldBatch(cfg)
