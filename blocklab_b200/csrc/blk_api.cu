@@ -929,7 +929,8 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
     ctx->box_capacity = 2 * std::max<uint32_t>(c.max_edits, 1);
-    A(dalloc(&ctx->region_lists, 4ull * ctx->box_capacity, "relight region lists"));
+    ctx->region_capacity = ctx->box_capacity + static_cast<uint32_t>(std::min<uint64_t>(n_tiles, 1u << 24));
+    A(dalloc(&ctx->region_lists, 8ull * ctx->region_capacity, "relight region lists"));
     A(dalloc(&ctx->region_counts, 4, "relight region counts"));
     A(dalloc(&ctx->render_params, envs, "render parameters"));
     A(dalloc(&ctx->col_summary, envs * ctx->columns_per_env, "column summaries"));
@@ -945,7 +946,18 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
         }
         ctx->park_ctas = static_cast<uint32_t>(sms);
         A(dalloc(&ctx->park, static_cast<size_t>(sms) * 16 * 1024, "tile scratch"));
-        A(dalloc(&ctx->region_park, static_cast<size_t>(sms) * region_park_words_per_sm(), "region relight scratch"));
+        A(dalloc(&ctx->region_park, 4ull * sms * region_park_words_per_sm(), "region relight scratch"));
+    }
+    if (rc == BLK_OK) {
+        bool ok = cudaEventCreateWithFlags(&ctx->relight_fork, cudaEventDisableTiming) == cudaSuccess;
+        for (int k = 0; k < 4 && ok; ++k)
+            ok = cudaStreamCreateWithFlags(&ctx->relight_streams[k], cudaStreamNonBlocking) == cudaSuccess
+                && cudaEventCreateWithFlags(&ctx->relight_join[k], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            rc = cuda_fail(cudaGetLastError(), "relight streams");
+            if (rc == BLK_OK)
+                rc = BLK_ERR_CUDA;
+        }
     }
     if (rc == BLK_OK) {
         if (cudaMallocHost(reinterpret_cast<void**>(&ctx->h_flags), sizeof(uint32_t)) != cudaSuccess
@@ -993,6 +1005,14 @@ int blk_ctx_destroy(blk_ctx* ctx)
     for (auto& m : ctx->marks)
         for (cudaEvent_t ev : m.e)
             cudaEventDestroy(ev);
+    for (int k = 0; k < 4; ++k) {
+        if (ctx->relight_streams[k])
+            cudaStreamDestroy(ctx->relight_streams[k]);
+        if (ctx->relight_join[k])
+            cudaEventDestroy(ctx->relight_join[k]);
+    }
+    if (ctx->relight_fork)
+        cudaEventDestroy(ctx->relight_fork);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->origins, ctx->origin_stage, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order, ctx->edit_changes,
         ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->region_lists, ctx->region_counts, ctx->region_park, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };

@@ -51,9 +51,13 @@ struct blk_ctx {
     uint32_t* dirty_window = nullptr;     // [num_envs * tiles] packed ylo | yhi<<16, 0xFFFFFFFF = clean
     uint32_t* dirty_list = nullptr;       // [num_envs * tiles] dirty tile ids
     uint32_t* dirty_count = nullptr;      // [1]
-    uint4* region_lists = nullptr;        // [4][box_capacity] relight regions by size class (see blk_relight.cu)
+    uint4* region_lists = nullptr;        // [4][region_capacity][2] relight items by size class (see blk_relight.cu)
+    uint32_t region_capacity = 0;         // items per list
     uint32_t* region_counts = nullptr;    // [4]
-    uint32_t* region_park = nullptr;      // region kernels' scratch: parked block counters per CTA
+    uint32_t* region_park = nullptr;      // region kernels' scratch: parked block counters per CTA, one area per list
+    cudaStream_t relight_streams[4] = {}; // side streams of the region kernels (forked from the caller's stream)
+    cudaEvent_t relight_fork = nullptr;
+    cudaEvent_t relight_join[4] = {};
     uint32_t box_capacity = 0;            // 2 * max_edits (an edit changes at most two cells)
     uint32_t* h_dirty_count = nullptr;    // pinned [1]
 
@@ -81,7 +85,7 @@ struct RegionBuildArgs {
     const uint32_t* env_offset; // [num_envs + 1] edit positions per env
     uint32_t num_envs;
     int32_t W, H, D;
-    uint4* lists[4];            // region lists by size class
+    uint4* lists[4];            // relight item lists by size class, two uint4 per item
     uint32_t* counts;           // [4]
     uint32_t capacity;          // entries per list
     uint32_t* win_lo;           // tile path: per env tile dirty rows (atomicMin / atomicMax)
@@ -98,7 +102,7 @@ struct RegionRelightArgs {
     int32_t W, H, D;
     uint64_t env_stride;
     uint64_t columns;           // per env
-    const uint4* regions;       // this kernel's list and its count
+    const uint4* regions;       // this kernel's item list (two uint4 per item) and its count
     const uint32_t* count;
     uint32_t capacity;
     uint32_t* park;
@@ -106,7 +110,7 @@ struct RegionRelightArgs {
 
 uint64_t region_park_words_per_sm();
 int launch_region_build(blk_ctx* ctx, const RegionBuildArgs& a, cudaStream_t stream);
-int launch_region_relight(blk_ctx* ctx, cudaStream_t stream);
+int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[4]);
 
 void set_error(const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
