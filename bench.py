@@ -1,23 +1,32 @@
 #!/usr/bin/env python
-"""World-state reset benchmark: batched generation + full sky/block light +
-RGBA8 -> float32 NCHW observation conversion, one batch of 128 worlds per GPU.
+"""World-state benchmark of the B200 world library.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload reset|relight|daynight|scaleout|render]
 
-Workload per GPU (per step): 128 envs of 256 x 256 x 128 voxels (fBm terrain,
-per-env seed = base_seed + env_id, 1000 surface torches per env), full
-generation + light, and conversion of 128 RGBA8 160x90 frames to a
-(128, 3, 90, 160) float32 tensor. Multi-GPU runs are weak-scaled: every rank
-owns its own 128 envs (global env ids rank*128 ...), no data-path collective.
+Default (one JSON line, rank 0): the reset workload, whose metric is the
+headline. Per GPU and step: 128 envs of 256 x 256 x 128 voxels (fBm terrain,
+per-env seed = base seed + global env id, 1000 surface torches per env), full
+generation + sky/block light, and conversion of 128 RGBA8 160x90 frames to a
+(128, 3, 90, 160) float32 tensor. K steps are timed exactly; a `sustained`
+record repeats the step for at least half a second. The line also carries one
+record per other configuration (`configs`: relight, daynight, scaleout), each
+timed for at least half a second with its own clocks, roofline and end-to-end
+figure. Multi-GPU runs are weak-scaled: every rank owns its own envs (global
+env ids rank * envs ...), with no data-path collective.
 
-Prints one JSON line (rank 0). ``--impl reference`` times the reference's own
-CPU implementation of the path (its CUDA CPU-fallback build, compiled from the
-reference sources into oracle/_ref) on a bounded sample of the same workload.
+`--workload X` prints only configuration X's record as the line. `--impl
+reference` times the reference's own CPU implementation of the path (its CUDA
+CPU-fallback build, compiled from the reference sources into oracle/_ref) on a
+bounded sample of the benchmark's own world, given to it as a dense override
+list (its generator has no fBm terrain).
 """
 from __future__ import annotations
 
 import argparse
+import csv
 import json
+import math
 import os
 import statistics
 import sys
@@ -27,19 +36,22 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "voxels lit+generated/s"
-UNIT = "voxels/s"
-ENVS_PER_GPU = 128
-W, H, D = 256, 128, 256
-TORCHES = 1000
-FRAME_H, FRAME_W = 90, 160
 BASE_SEED = 1
-# Bounded CPU sample: a quarter env (128 x 128 x 128) with 250 torches keeps the
-# reference's torch density (1000 per 256 x 256 columns).
-SAMPLE_W, SAMPLE_H, SAMPLE_D, SAMPLE_TORCHES = 128, 128, 128, 250
-# Our kernel launches per step: place_torches, override count/scan(3)/scatter/sort,
-# fBm surface with the column summaries, tile kernel, conversion.
-LAUNCHES_PER_STEP = 10
+RESET = dict(envs=128, W=256, H=128, D=256, torches=1000, frame=(90, 160))
+RELIGHT = dict(envs=1024, W=128, H=128, D=128, torches=200, edits=10000)
+DAYNIGHT = dict(envs=4096, W=128, H=96, D=128, torches=300, frame=84, steps_per_sweep=256)
+SCALEOUT = dict(envs=1024, W=256, H=256, D=256, torches=2000, amplitude=120.0, edits_total=5000, envs_total=8192)
+# Bounded sample of the reset world for the reference's CPU build: a 128^3
+# corner of env 0 keeps the benchmark's torch density (1000 per 256 x 256).
+SAMPLE = dict(W=128, H=128, D=128)
+SUSTAINED_S = 0.5  # every configuration is timed for at least this long
+# This library's kernel launches per step (from the launch lists in profiles/):
+# reset: torch placement, override count / scan (3) / scatter / sort, fBm
+# surface with the column summaries, tile kernel, conversion; relight: edit
+# count / scan (3) / scatter, setBlock application, change marking, region
+# build, dirty-tile compaction, four region kernels, tile kernel.
+LAUNCHES = dict(reset=10, relight=14, daynight=1, scaleout=15, render=1)
+TRAFFIC_CSV = os.path.join(ROOT, "profiles", "tile_kernel_reset_traffic.csv")
 
 
 def parse_args():
@@ -49,20 +61,17 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="reset line without the other configurations")
     ap.add_argument("--envs", type=int, default=None,
                     help="envs per GPU (default: the workload's; smaller batches are for profiler captures)")
-    ap.add_argument("--workload", choices=["reset", "relight", "daynight", "scaleout", "render"], default="reset",
-                    help="reset (default): 128 worlds 256x256x128 regenerated + lit + frames converted per step; "
-                         "relight: 1024 worlds 128^3, 10k edits per step + exact relight; daynight: 4096 worlds "
-                         "128x128x96, sky sweep + 84x84 frame conversion per step; scaleout: 1024 worlds 256^3 per "
-                         "GPU, 5000x1024/8192 edits per GPU per step + 90x160 frames, optional NCCL gather; "
-                         "render: the reset worlds rendered to 160x90 RGBA8 frames and converted each step")
+    ap.add_argument("--workload", choices=["reset", "relight", "daynight", "scaleout", "render"], default="reset")
     ap.add_argument("--gather", action="store_true", help="scaleout: gather observations to rank 0 every step")
     ap.add_argument("--materialize", action="store_true",
                     help="daynight: also materialise the effective light of every cell each step")
     return ap.parse_args()
 
 
+# ------------------------------------------------------------ plumbing --
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -70,11 +79,44 @@ def dist_env():
     return rank, world, local
 
 
-# ---------------------------------------------------------------- clocks --
+def init_dist():
+    import datetime
+
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    return rank, world, local, dev, pg
+
+
+def barrier(dev, pg):
+    import torch
+
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+
+
+def max_over_ranks(values, dev, pg):
+    import torch
+
+    if pg is None:
+        return [float(v) for v in values]
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
 class ClockSampler:
-    """SM clock and clock-event (throttle) reasons sampled during the timed
-    region through NVML read-only queries (every ~2 ms in a thread), falling
-    back to `nvidia-smi -lms` when NVML is unavailable."""
+    """SM clock and clock-event (throttle) reasons sampled during a timed
+    region through NVML read-only queries (every ~2 ms in a thread)."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
@@ -126,103 +168,34 @@ class ClockSampler:
                 "samples": len(self.samples), "source": "nvml"}
 
 
-def workload_config(world: int) -> dict:
-    return {"workload": "world reset: generation + full sky/block light + RGBA8->NCHW conversion",
-            "envs_per_gpu": ENVS_PER_GPU, "world": [W, H, D], "torches_per_env": TORCHES,
-            "terrain": "fBm 40+round(50*fbm)", "frames": [ENVS_PER_GPU, 3, FRAME_H, FRAME_W],
-            "l2": f"outputs {2 * ENVS_PER_GPU * W * H * D / 1e9:.2f} GB per step per GPU rewritten every step "
-                  f"(> 126 MB L2)",
-            "parallelism": f"env shards x{world}"}
+def time_steps(fn, steps, warmup, dev, pg, clock_gpu, stream=None):
+    """W untimed calls of fn(k), then `steps` calls timed with CUDA events on
+    the current stream between barrier + synchronize, clocks sampled meanwhile;
+    returns (ms, clocks) with ms the max over ranks."""
+    import torch
+
+    for k in range(warmup):
+        fn(k)
+    barrier(dev, pg)
+    clocks = ClockSampler(clock_gpu)
+    clocks.start()
+    st = stream if stream is not None else torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for k in range(steps):
+        fn(warmup + k)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    barrier(dev, pg)
+    info = clocks.stop()
+    (ms,) = max_over_ranks([e0.elapsed_time(e1)], dev, pg)
+    return ms, info
 
 
-# ------------------------------------------------------------ CPU samples --
-def cpu_sample(kind_pref: str = "reference"):
-    """Times one bounded sample of the workload on the host cores.
-
-    Returns (seconds, voxels, kind, cores, description)."""
-    from oracle.oracle import TERRAIN_FBM, TERRAIN_REFERENCE, Oracle, Reference, WorldSpec, ref_available
-    import numpy as np
-
-    O = Oracle()
-    if kind_pref == "reference" and ref_available("cpu"):
-        R = Reference("cpu")
-        spec = WorldSpec(BASE_SEED, SAMPLE_W, SAMPLE_H, SAMPLE_D, terrain=TERRAIN_REFERENCE)
-        torches = O.place_torches(spec, SAMPLE_TORCHES, 0x5EED)
-        timing = []
-        R.generate(BASE_SEED, (0, 0, 0), (SAMPLE_W, SAMPLE_H, SAMPLE_D), torches,
-                   np.full(len(torches), 4, np.uint8), runs=2, timing=timing)
-        desc = (f"reference WorldGenerator::generate (CUDA CPU-fallback build) on one {SAMPLE_W}x{SAMPLE_H}x{SAMPLE_D} "
-                f"region with {len(torches)} surface torches, reference terrain formula; converged second "
-                f"generation timed (block cache + light + render list + cache readback)")
-        return timing[-1] / 1e3, SAMPLE_W * SAMPLE_H * SAMPLE_D, "reference", os.cpu_count() or 1, desc
-    spec = WorldSpec(BASE_SEED, SAMPLE_W, SAMPLE_H, SAMPLE_D, terrain=TERRAIN_FBM)
-    torches = O.place_torches(spec, SAMPLE_TORCHES, 0x5EED)
-    t0 = time.perf_counter()
-    O.generate(spec, torches, np.full(len(torches), 4, np.uint8), method="per_source")
-    dt = time.perf_counter() - t0
-    desc = (f"oracle restatement (single thread) on one {SAMPLE_W}x{SAMPLE_H}x{SAMPLE_D} fBm region with "
-            f"{len(torches)} torches")
-    return dt, SAMPLE_W * SAMPLE_H * SAMPLE_D, "port", 1, desc
-
-
-def gpu_reference_sample():
-    """Times the reference's own CUDA kernels (its src/world/WorldGenerator.cu
-    built for sm_100a under oracle/_ref) on one region of the benchmark's size,
-    driven one region per call as its renderer drives them. Returns
-    (seconds, voxels, description), or None when that build is absent."""
-    from oracle.oracle import TERRAIN_REFERENCE, Oracle, Reference, WorldSpec, ref_available
-    import numpy as np
-
-    if not ref_available("cuda"):
-        return None
-    R = Reference("cuda")
-    spec = WorldSpec(BASE_SEED, W, H, D, terrain=TERRAIN_REFERENCE)
-    torches = Oracle().place_torches(spec, TORCHES, 0x5EED)
-    timing = []
-    R.generate(BASE_SEED, (0, 0, 0), (W, H, D), torches, np.full(len(torches), 4, np.uint8), runs=3, timing=timing)
-    desc = (f"reference WorldGenerator::generate, its CUDA kernels built for sm_100a, on this GPU: one {W}x{H}x{D} "
-            f"region with {len(torches)} surface torches, reference terrain formula; converged third generation "
-            f"timed by wall clock (block cache + light + render list + its readback of the block cache)")
-    return timing[-1] / 1e3, W * H * D, desc
-
-
-def run_reference(args) -> None:
-    rank, world, _ = dist_env()
-    if rank != 0:
-        return
-    times = []
-    vox = 0
-    info = None
-    for i in range(args.warmup + args.steps):
-        dt, vox, kind, cores, desc = cpu_sample("reference")
-        info = (kind, cores, desc)
-        if i >= args.warmup:
-            times.append(dt)
-    total = sum(times)
-    value = vox * len(times) / total
-    kind, cores, desc = info
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": workload_config(args.gpus),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-
-
-# ------------------------------------------------------------------- ours --
-def load_traffic():
-    """DRAM read+write bytes of one benchmark launch of the tile kernel, from
-    the committed ncu summary (a 16-env capture scaled to the launch)."""
-    path = os.path.join(ROOT, "profiles", "tile_kernel_reset_16envs_256x128x256.md")
-    if os.path.exists(path):
-        with open(path) as f:
-            for line in f:
-                if line.startswith("traffic_bytes_per_launch_scaled:"):
-                    return int(line.split(":", 1)[1])
-    return None
+def sustained_steps(ms_per_step, minimum, dev, pg):
+    """Steps that fill SUSTAINED_S at the measured step time (same on every rank)."""
+    (ms,) = max_over_ranks([ms_per_step], dev, pg)
+    return max(minimum, int(math.ceil(SUSTAINED_S * 1e3 / max(ms, 1e-3))))
 
 
 def measured_peaks():
@@ -233,69 +206,126 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0}, "fallback"
 
 
-def run_ours(args) -> None:
+def load_traffic():
+    """DRAM bytes read + written by one benchmark launch of the tile kernel:
+    ncu's own CSV of that launch (profiles/tile_kernel_reset_traffic.csv,
+    written by the command in the summary beside it), or None when absent."""
+    if not os.path.exists(TRAFFIC_CSV):
+        return None
+    got = {}
+    with open(TRAFFIC_CSV) as f:
+        rows = [r for r in csv.reader(f) if r]
+    hdr = next((r for r in rows if "Metric Name" in r), None)
+    if hdr is None:
+        return None
+    i_name, i_val, i_kernel = hdr.index("Metric Name"), hdr.index("Metric Value"), hdr.index("Kernel Name")
+    i_unit = hdr.index("Metric Unit") if "Metric Unit" in hdr else None
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    for r in rows:
+        if r is hdr or len(r) <= i_val or "tile_kernel" not in r[i_kernel]:
+            continue
+        unit = r[i_unit] if i_unit is not None else "byte"
+        if r[i_name] in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            got[r[i_name]] = float(r[i_val].replace(",", "")) * scale.get(unit, 1)
+    if len(got) != 2:
+        return None
+    return int(sum(got.values()))
+
+
+# ---------------------------------------------------- reference samples --
+def fbm_world(seed, W, H, D, torches, amplitude=50.0):
+    """The benchmark's world of one env (fBm terrain + surface torches at the
+    library's torch columns) as a reference-layout block volume (D, H, W),
+    built by the oracle restatement (input construction, not timed)."""
+    import numpy as np
+
+    import blocklab_b200 as B
+    from oracle.oracle import Oracle, WorldSpec
+
+    O = Oracle()
+    spec = WorldSpec(seed, W, H, D, amplitude=amplitude)
+    t = O.place_torches(spec, torches, B.torch_key(seed))
+    blocks, _ = O.build_blocks(spec, t, np.full(len(t), 4, np.uint8))
+    return blocks, len(t)
+
+
+def reference_cpu_times(n_generations):
+    """Wall times (s) of n consecutive generations of the reference's own CPU
+    build on the bounded sample: the 128^3 corner of the reset benchmark's env
+    0 (fBm world, its torches), given as a dense override list; the first
+    generation converges the reference's light-source capacity and is not
+    returned. Also returns (voxels, cores, description)."""
+    from oracle.oracle import Reference
+
+    blocks, n_t = fbm_world(BASE_SEED, RESET["W"], RESET["H"], RESET["D"], RESET["torches"])
+    sub = blocks[:SAMPLE["D"], :SAMPLE["H"], :SAMPLE["W"]].copy()
+    n_sub = int((sub == 4).sum())
+    R = Reference("cpu")
+    timing = []
+    R.light_blocks(sub, runs=n_generations + 1, timing=timing)
+    desc = (f"reference WorldGenerator::generate (its CUDA CPU-fallback build) on the {SAMPLE['W']}x{SAMPLE['H']}x"
+            f"{SAMPLE['D']} corner of the reset benchmark's env 0 (fBm terrain, {n_sub} of its torches), the world "
+            f"given as a dense override list (its generator has no fBm terrain: the sort of 2.1 M overrides and a "
+            f"binary search per voxel are part of its time); converged generations timed by wall clock (block "
+            f"cache + light + render list + cache readback)")
+    return [t / 1e3 for t in timing[1:]], sub.size, os.cpu_count() or 1, desc
+
+
+def reference_gpu_record(W, H, D, torches, unit, per_unit, amplitude=50.0, what="the reset benchmark's env 0"):
+    """The reference's own CUDA kernels (its WorldGenerator.cu built for
+    sm_100a under oracle/_ref) on one env of the configuration's world (dense
+    override list): device time of its kernels per generation by CUDA events
+    (one captured generation's kernels, without its host work and its 12 B per
+    voxel block-cache readback), and the wall time of an ordinary generation."""
+    from oracle.oracle import Reference, ref_available
+
+    if not ref_available("cuda"):
+        return None
+    blocks, n_t = fbm_world(BASE_SEED, W, H, D, torches, amplitude)
+    k_ms, w_ms = Reference("cuda").kernel_time(blocks, runs=2, reps=5)
+    return {"value": per_unit / (k_ms / 1e3), "unit": unit, "kernel_ms": k_ms, "wall_ms": w_ms,
+            "wall_value": per_unit / (w_ms / 1e3),
+            "sample": f"reference WorldGenerator::generate, its CUDA kernels built for sm_100a, on this GPU: {what} "
+                      f"({W}x{H}x{D}, fBm, {n_t} torches) given as a dense override list; value = its kernels' "
+                      f"device time per generation (CUDA events around a graph of one converged generation's kernels, "
+                      f"without its override sort and copies); wall_value = an ordinary generation by wall clock, "
+                      f"including its block-cache readback"}
+
+
+# ------------------------------------------------------------- records --
+def reset_record(args, rank, world, local, dev, pg, peaks, peak_kind):
     import numpy as np
     import torch
 
-    global ENVS_PER_GPU
-    ENVS_PER_GPU = args.envs or ENVS_PER_GPU
-
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        pg = dist
-
     import blocklab_b200 as B
 
-    cfg = B.WorldConfig(num_envs=ENVS_PER_GPU, width=W, height=H, depth=D, max_overrides=ENVS_PER_GPU * TORCHES)
+    E = args.envs or RESET["envs"]
+    W, H, D, T = RESET["W"], RESET["H"], RESET["D"], RESET["torches"]
+    FH, FW = RESET["frame"]
+    cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, max_overrides=E * T)
     wb = B.WorldBatch(cfg, device=local)
     stream = torch.cuda.current_stream(dev)
-    seeds_host = (BASE_SEED + rank * ENVS_PER_GPU + np.arange(ENVS_PER_GPU)).astype(np.uint32)
+    seeds_host = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
     seeds = torch.from_numpy(seeds_host.view(np.int32)).to(dev)
     gen = torch.Generator().manual_seed(1234 + rank)
-    frames_host = torch.randint(0, 256, (ENVS_PER_GPU, FRAME_H, FRAME_W, 4), dtype=torch.uint8,
-                                generator=gen).pin_memory()
+    frames_host = torch.randint(0, 256, (E, FH, FW, 4), dtype=torch.uint8, generator=gen).pin_memory()
     frames = frames_host.to(dev)
-    obs = torch.empty((ENVS_PER_GPU, 3, FRAME_H, FRAME_W), dtype=torch.float32, device=dev)
+    obs = torch.empty((E, 3, FH, FW), dtype=torch.float32, device=dev)
 
-    def step():
-        torches = wb.place_torches(seeds, TORCHES)
+    def step(_k):
+        torches = wb.place_torches(seeds, T)
         wb.generate(seeds, torches)
         B.convert_rgba8_to_float_nchw(frames, out=obs)
 
-    def barrier():
-        if pg is not None:
-            pg.barrier()
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
-        step()
-    wb.sync()
-    barrier()
-
-    clocks = ClockSampler(local)
-    clocks.start()
     wb.profile(True)
-    barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step()
-    ev1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    clock_info = clocks.stop()
-    wb.profile(False)
+    ms, clocks = time_steps(step, args.steps, args.warmup, dev, pg, local)
     prof = wb.profile_read()
+    wb.profile(False)
     wb.sync()
-    ms = ev0.elapsed_time(ev1)
     tile_ms = prof["generate_tiles_ms"] / max(prof["generate_calls"], 1)
+    prep_ms = prof["generate_prep_ms"] / max(prof["generate_calls"], 1)
+    n_sus = sustained_steps(ms / args.steps, args.steps, dev, pg)
+    sus_ms, sus_clocks = time_steps(step, n_sus, 1, dev, pg, local)
 
     # End to end through the public API with host buffers: every step copies
     # its seeds and frames from pinned host memory and reads its height maps
@@ -304,8 +334,8 @@ def run_ours(args) -> None:
     # every step's own transfers lie inside the timed region.
     seeds_pinned = torch.from_numpy(seeds_host.view(np.int32)).pin_memory()
     copy_stream = torch.cuda.Stream(dev)
-    hm_host = [torch.empty((ENVS_PER_GPU, D, W), dtype=torch.int16, pin_memory=True) for _ in range(2)]
-    hm_dev = [torch.empty((ENVS_PER_GPU, D, W), dtype=torch.int16, device=dev) for _ in range(2)]
+    hm_host = [torch.empty((E, D, W), dtype=torch.int16, pin_memory=True) for _ in range(2)]
+    hm_dev = [torch.empty((E, D, W), dtype=torch.int16, device=dev) for _ in range(2)]
     seeds_dev = [torch.empty_like(seeds) for _ in range(2)]
     frames_dev = [torch.empty_like(frames) for _ in range(2)]
     ev = {name: [torch.cuda.Event() for _ in range(2)] for name in ("in_ready", "used", "hm_ready", "hm_read")}
@@ -325,7 +355,7 @@ def run_ours(args) -> None:
         for k in range(n):
             b = k % 2
             stream.wait_event(ev["in_ready"][b])
-            torches = wb.place_torches(seeds_dev[b], TORCHES)
+            torches = wb.place_torches(seeds_dev[b], T)
             wb.generate(seeds_dev[b], torches)
             B.convert_rgba8_to_float_nchw(frames_dev[b], out=obs)
             stream.wait_event(ev["hm_read"][b])
@@ -342,117 +372,48 @@ def run_ours(args) -> None:
             stream.wait_event(ev["hm_read"][b])
 
     e2e_run(args.warmup)
-    barrier()
+    barrier(dev, pg)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     copy_stream.wait_event(e0)
     e2e_run(args.steps)
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
+    barrier(dev, pg)
+    (e2e_ms,) = max_over_ranks([e0.elapsed_time(e1)], dev, pg)
+    tile_ms, prep_ms = max_over_ranks([tile_ms, prep_ms], dev, pg)
+    wb.close()
 
-    times = torch.tensor([ms, e2e_ms, tile_ms], dtype=torch.float64, device=dev)
-    if pg is not None:
-        pg.all_reduce(times, op=pg.ReduceOp.MAX)
-    ms, e2e_ms, tile_ms = (float(v) for v in times.tolist())
-
-    vox_step = ENVS_PER_GPU * W * H * D
+    vox_step = E * W * H * D
     total_vox = vox_step * world * args.steps
-    value = total_vox / (ms / 1e3)
-    e2e_value = total_vox / (e2e_ms / 1e3)
-    peaks, peak_kind = measured_peaks()
     algo_bytes = 2 * vox_step
     achieved = algo_bytes / (tile_ms / 1e3) / 1e9
-    traffic = load_traffic()
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": workload_config(world),
-        "env_resets_per_s": ENVS_PER_GPU * world * args.steps / (ms / 1e3),
-        "roofline": {"bound": "hbm", "kernel": "tile_kernel", "achieved": achieved, "peak": peaks["hbm_gbs"],
+    traffic = load_traffic() if E == RESET["envs"] else None
+    return {
+        "metric": "voxels lit+generated/s", "value": total_vox / (ms / 1e3), "unit": "voxels/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic: fBm terrain 40+round(50*fbm) of the library's own specification (the benchmark names "
+                "fBm without its constants), seeds base+env, uniform random RGBA8 frames",
+        "config": {"workload": "world reset: generation + full sky/block light + RGBA8->NCHW conversion",
+                   "envs_per_gpu": E, "world": [W, H, D], "torches_per_env": T, "frames": [E, 3, FH, FW],
+                   "l2": f"outputs {2 * vox_step / 1e9:.2f} GB per step per GPU rewritten every step (> 126 MB L2)",
+                   "parallelism": f"env shards x{world}"},
+        "env_resets_per_s": E * world * args.steps / (ms / 1e3),
+        "roofline": {"bound": "hbm", "kernel": "tile_kernel<4, 0>", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                     "algorithmic_bytes_per_launch": algo_bytes, "kernel_ms": tile_ms,
-                     "traffic": traffic if ENVS_PER_GPU == 128 else None},
-        "e2e": {"value": e2e_value, "unit": UNIT,
+                     "algorithmic_bytes_per_launch": algo_bytes, "kernel_ms": tile_ms, "traffic": traffic,
+                     "traffic_source": "profiles/tile_kernel_reset_traffic.csv (ncu, one full-size launch)"
+                     if traffic is not None else None},
+        "e2e": {"value": total_vox / (e2e_ms / 1e3), "unit": "voxels/s",
                 "h2d_bytes_per_step": seeds.numel() * 4 + frames.numel(),
                 "d2h_bytes_per_step": hm_host[0].numel() * 2},
-        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
-        "clocks": clock_info,
-        "profile": {"generate_prep_ms": prof["generate_prep_ms"] / max(prof["generate_calls"], 1),
-                    "generate_tiles_ms": tile_ms},
+        "gpu_launches": LAUNCHES["reset"] * args.steps,
+        "clocks": clocks,
+        "sustained": {"steps": n_sus, "ms_per_step": sus_ms / n_sus,
+                      "value": vox_step * world * n_sus / (sus_ms / 1e3), "clocks": sus_clocks},
+        "profile": {"generate_prep_ms": prep_ms, "generate_tiles_ms": tile_ms},
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        dt, vox, kind, cores, desc = cpu_sample("reference")
-        line["cpu_baseline"] = {"value": vox / dt, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc}
-        ref_gpu = gpu_reference_sample()
-        if ref_gpu is not None:
-            dt, vox, desc = ref_gpu
-            line["reference_gpu"] = {"value": vox / dt, "unit": UNIT, "sample": desc}
-    wb.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if pg is not None:
-        pg.barrier()
-        pg.destroy_process_group()
-
-
-# --------------------------------------------------- secondary workloads --
-# The relight, day/night and scale-out configurations. Each prints its own
-# JSON line; the default invocation (reset) is the headline.
-RELIGHT = dict(envs=1024, W=128, H=128, D=128, torches=200, edits=10000)
-DAYNIGHT = dict(envs=4096, W=128, H=96, D=128, torches=300, frame=84, steps_per_sweep=256)
-SCALEOUT = dict(envs=1024, W=256, H=256, D=256, torches=2000, amplitude=120.0, edits_total=5000, envs_total=8192)
-
-
-def init_dist():
-    import datetime
-
-    import torch
-
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        pg = dist
-    return rank, world, local, dev, pg
-
-
-def time_steps(fn, steps, warmup, dev, pg, clock_gpu):
-    """Runs warmup untimed steps, then times `steps` calls of fn(k) with CUDA
-    events on the current stream between barriers; returns (ms, clocks)."""
-    import torch
-
-    def barrier():
-        if pg is not None:
-            pg.barrier()
-        torch.cuda.synchronize(dev)
-
-    for k in range(warmup):
-        fn(k)
-    barrier()
-    clocks = ClockSampler(clock_gpu)
-    clocks.start()
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for k in range(steps):
-        fn(warmup + k)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    info = clocks.stop()
-    ms = e0.elapsed_time(e1)
-    if pg is not None:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms = float(t.item())
-    return ms, info
 
 
 def surface_edits(rng, hm, envs, n, W, D, torch_xyz):
@@ -478,15 +439,16 @@ def surface_edits(rng, hm, envs, n, W, D, torch_xyz):
     return B.make_overrides(np.stack([x, y, z], 1), blk, env=env, kind=kind)
 
 
-def dirty_voxels(before, after, W, H, D):
-    """Voxels within L-inf distance 14 (clipped to the world) of a cell whose
-    light class changed (opaque / open / torch), summed over envs: the cells
-    whose light an exact relight must revisit. An opaque block replaced by
-    another opaque block changes no light, and neither does an air <-> opaque
-    change of a cell that ends the step enclosed (below its column's top before
-    and after the step, six opaque neighbours, no torch before or after). Also returns the number of
-    cells whose block id changed and the number of light-class changes."""
-    import numpy as np
+def dirty_voxels(before, after, hm_before, hm_after, origin_y=0):
+    """Voxels an exact relight must revisit, summed over envs: the union of the
+    L-inf radius-14 cubes (clipped to the world) around every cell whose light
+    class changed (opaque / open / torch) and around the column span its top
+    moved over. An opaque block replaced by another opaque block changes no
+    light, and neither does an air <-> opaque change of a cell that lay below
+    its column's top before and after the step and ends it enclosed (six
+    opaque neighbours, no torch before or after). Also returns the number of
+    cells whose block id changed and the number of light-class changes.
+    ids are (envs, D, W, H) tensors, height maps (envs, D, W) in world y."""
     import torch
     import torch.nn.functional as F
 
@@ -494,253 +456,355 @@ def dirty_voxels(before, after, W, H, D):
         return (ids == 0).to(torch.uint8) + 2 * (ids == 4).to(torch.uint8)
 
     n_changed = int((before != after).sum().item())
-    rows = []
     n_light = 0
-    for e0 in range(0, before.shape[0], 64):  # ids [env][z][x][y], 64 envs at a time
-        b, a = before[e0:e0 + 64], after[e0:e0 + 64]
+    total = 0
+    H = before.shape[3]
+    y = torch.arange(H, device=after.device, dtype=torch.int32)
+    for e0 in range(0, before.shape[0], 32):
+        b, a = before[e0:e0 + 32], after[e0:e0 + 32]
+        tb = (hm_before[e0:e0 + 32].to(torch.int32) - origin_y).unsqueeze(3)
+        ta = (hm_after[e0:e0 + 32].to(torch.int32) - origin_y).unsqueeze(3)
         moved = light_class(b) != light_class(a)
         n_light += int(moved.sum().item())
         opaque = ((a != 0) & (a != 4)).to(torch.uint8)
-        y = torch.arange(H, device=a.device, dtype=torch.int32)
-        top = torch.where(opaque.bool(), y, torch.full_like(y, -1)).amax(dim=3, keepdim=True)
-        top_before = torch.where((b != 0) & (b != 4), y, torch.full_like(y, -1)).amax(dim=3, keepdim=True)
         p = F.pad(opaque, (1, 1, 1, 1, 1, 1), value=1)
         nb = (p[:, :-2, 1:-1, 1:-1] & p[:, 2:, 1:-1, 1:-1] & p[:, 1:-1, :-2, 1:-1] & p[:, 1:-1, 2:, 1:-1]
               & p[:, 1:-1, 1:-1, :-2] & p[:, 1:-1, 1:-1, 2:]).bool()
-        enclosed = nb & (y < top) & (y < top_before) & (b != 4) & (a != 4)
-        idx = (moved & ~enclosed).nonzero()
-        idx[:, 0] += e0
-        rows.append(idx.cpu().numpy())
-    changed = np.concatenate(rows) if rows else np.zeros((0, 4), np.int64)  # (env, z, x, y)
-    total = 0
-    for e in np.unique(changed[:, 0]):
-        m = np.zeros((D, W, H), bool)
-        for _, z, x, y in changed[changed[:, 0] == e]:
-            m[max(z - 14, 0):z + 15, max(x - 14, 0):x + 15, max(y - 14, 0):y + 15] = True
-        total += int(m.sum())
-    return total, n_changed, n_light, len(changed)
+        enclosed = nb & (y < ta) & (y < tb) & (b != 4) & (a != 4)
+        seed = moved & ~enclosed
+        # the span of every moved top, in its column
+        span = (y > torch.minimum(ta, tb)) & (y <= torch.maximum(ta, tb))
+        seed = seed | span
+        # L-inf dilation by 14 of the seeds: a 29-wide max pool along each axis
+        dil = seed.to(torch.float16)
+        for k in ((29, 1, 1), (1, 29, 1), (1, 1, 29)):
+            dil = F.max_pool3d(dil, kernel_size=k, stride=1, padding=tuple(v // 2 for v in k))
+        total += int((dil > 0).sum().item())
+    return total, n_changed, n_light
 
 
-def run_workload(args) -> None:
+def relight_record(args, rank, world, local, dev, pg, peaks, peak_kind, standalone):
     import numpy as np
     import torch
 
-    if args.impl == "reference":
-        run_workload_reference(args)
-        return
     import blocklab_b200 as B
 
-    rank, world, local, dev, pg = init_dist()
-    peaks, peak_kind = measured_peaks()
-    line = {"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+    c = dict(RELIGHT)
+    E = (args.envs if standalone and args.envs else c["envs"])
+    Wd, Hd, Dd = c["W"], c["H"], c["D"]
+    n_edits = c["edits"] * E // RELIGHT["envs"]
+    cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, max_overrides=E * c["torches"],
+                        max_edits=n_edits)
+    wb = B.WorldBatch(cfg, device=local)
     rng = np.random.default_rng(4242 + rank)
+    seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+    torches = wb.place_torches(seeds, c["torches"])
+    wb.generate(seeds, torches)
+    wb.sync()
+    hm = wb.height_map.cpu().numpy()
+    tl = torches.cpu().numpy().view(B.OVERRIDE_DTYPE).reshape(E, c["torches"])
+    txyz = np.stack([tl["x"], tl["y"], tl["z"]], 2)
 
-    if args.workload == "relight":
-        c = dict(RELIGHT)
-        c["envs"] = args.envs or c["envs"]
-        E, Wd, Hd, Dd = c["envs"], c["W"], c["H"], c["D"]
-        n_edits = c["edits"] * E // RELIGHT["envs"]
-        cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, max_overrides=E * c["torches"],
-                            max_edits=n_edits)
-        wb = B.WorldBatch(cfg, device=local)
-        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
-        torches = wb.place_torches(seeds, c["torches"])
-        wb.generate(seeds, torches)
-        wb.sync()
-        hm = wb.height_map.cpu().numpy()
-        tl = torches.cpu().numpy().view(B.OVERRIDE_DTYPE).reshape(E, c["torches"])
-        txyz = np.stack([tl["x"], tl["y"], tl["z"]], 2)
-        batches = [surface_edits(rng, hm, E, n_edits, Wd, Dd, txyz) for _ in range(args.warmup + args.steps)]
-        dev_batches = [torch.from_numpy(b.view(np.uint8).copy()).to(dev) for b in batches]
-        # Dirty volume of the first timed step, measured outside the timed region.
-        for k in range(args.warmup):
-            wb.apply_edits(dev_batches[k])
-        before = wb.ids.clone()
-        wb.apply_edits(dev_batches[args.warmup])
-        dirty, n_changed, n_light, n_relit = dirty_voxels(before, wb.ids, Wd, Hd, Dd)
-        del before
-        # Timed run on a fresh copy of the same worlds and edit sequence.
-        wb.generate(seeds, torches)
-        wb.profile(True)
-        ms, clocks = time_steps(lambda k: wb.apply_edits(dev_batches[k]), args.steps, args.warmup, dev, pg, local)
-        prof = wb.profile_read()
-        wb.profile(False)
-        relight_ms = prof["relight_ms"] / max(prof["edit_calls"], 1)
-        pinned = [torch.from_numpy(b.view(np.uint8).copy()).pin_memory() for b in batches]
-        stage = torch.empty_like(dev_batches[0])
-        wb.generate(seeds, torches)
+    def batches(n):
+        return [torch.from_numpy(surface_edits(rng, hm, E, n_edits, Wd, Dd, txyz).view(np.uint8).copy()).to(dev)
+                for _ in range(n)]
 
-        def e2e(k):
-            stage.copy_(pinned[k], non_blocking=True)
-            wb.apply_edits(stage)
+    # Step time from a short run, then as many steps as fill SUSTAINED_S.
+    probe = batches(args.warmup + 3)
+    ms_probe, _ = time_steps(lambda k: wb.apply_edits(probe[k]), 3, args.warmup, dev, pg, local)
+    n = sustained_steps(ms_probe / 3, args.steps, dev, pg)
+    dev_batches = batches(args.warmup + n)
+    # Dirty volume per step, counted outside the timed region on the same edit
+    # sequence: at the first timed step and at the last.
+    wb.generate(seeds, torches)
+    for k in range(args.warmup):
+        wb.apply_edits(dev_batches[k])
+    counts = []
+    for k in (args.warmup, args.warmup + n - 1):
+        if k != args.warmup:
+            for j in range(args.warmup + 1, k):
+                wb.apply_edits(dev_batches[j])
+        before, hb = wb.ids.clone(), wb.height_map.clone()
+        wb.apply_edits(dev_batches[k])
+        counts.append(dirty_voxels(before, wb.ids, hb, wb.height_map))
+        del before, hb
+    dirty = sum(cn[0] for cn in counts) / len(counts)
+    # Timed run on a fresh copy of the same worlds and edit sequence.
+    wb.generate(seeds, torches)
+    wb.profile(True)
+    ms, clocks = time_steps(lambda k: wb.apply_edits(dev_batches[k]), n, args.warmup, dev, pg, local)
+    prof = wb.profile_read()
+    wb.profile(False)
+    wb.sync()
+    relight_ms = prof["relight_ms"] / max(prof["edit_calls"], 1)
+    # End to end: each step's edits copied from pinned host memory.
+    pinned = [b.cpu().pin_memory() for b in dev_batches]
+    stage = torch.empty_like(dev_batches[0])
+    wb.generate(seeds, torches)
 
-        e2e_ms, _ = time_steps(e2e, args.steps, args.warmup, dev, pg, local)
-        env_steps = E * world * args.steps
-        algo = 3 * dirty
-        line.update({
-            "metric": "env-steps/s (incremental relight)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
-            "ms_per_step": ms / args.steps, "dtype": "u8",
-            "config": {"workload": "relight: edits with World::setBlock semantics + exact incremental relight",
-                       "envs_per_gpu": E, "world": [Wd, Hd, Dd], "torches_per_env": c["torches"],
-                       "edits_per_step_per_gpu": n_edits, "mix": "45% dig, 45% stone, 5% torch, 5% remove torch",
-                       "l2": "edits touch scattered tiles of a 4.3 GB world; no flush needed (L2 126 MB)",
-                       "parallelism": f"env shards x{world}"},
-            "roofline": {"bound": "hbm", "kernel": "tile_kernel (relight) + apply_edits",
-                         "achieved": algo / (relight_ms / 1e3) / 1e9 if relight_ms > 0 else None,
-                         "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": (algo / (relight_ms / 1e3) / 1e9) / peaks["hbm_gbs"] if relight_ms > 0 else None,
-                         "algorithmic_bytes_per_step": algo, "dirty_voxels_per_step": dirty,
-                         "changed_cells_per_step": n_changed, "light_class_changes_per_step": n_light,
-                         "relit_changes_per_step": n_relit,
-                         "relight_ms": relight_ms, "traffic": None},
-            "e2e": {"value": env_steps / (e2e_ms / 1e3), "unit": "env-steps/s",
-                    "h2d_bytes_per_step": int(dev_batches[0].numel()), "d2h_bytes_per_step": 0},
-            "gpu_launches": None, "clocks": clocks})
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            # The reference regenerates and relights a region for every edit
-            # (src/graphics/Renderer.cpp:1121-1141): its own CUDA kernels on
-            # this GPU, one region per env-step.
-            from oracle.oracle import TERRAIN_REFERENCE, Oracle, Reference, WorldSpec, ref_available
+    def e2e(k):
+        stage.copy_(pinned[k], non_blocking=True)
+        wb.apply_edits(stage)
 
-            if ref_available("cuda"):
-                R = Reference("cuda")
-                rspec = WorldSpec(BASE_SEED, Wd, Hd, Dd, terrain=TERRAIN_REFERENCE)
-                rt = Oracle().place_torches(rspec, c["torches"], 0x5EED)
-                times = []
-                for _ in range(5):
-                    timing = []
-                    R.generate(BASE_SEED, (0, 0, 0), (Wd, Hd, Dd), rt, np.full(len(rt), 4, np.uint8), runs=2,
-                               timing=timing)
-                    times.append(timing[-1] / 1e3)
-                line["reference_gpu"] = {
-                    "value": len(times) / sum(times), "unit": "env-steps/s",
-                    "sample": f"reference WorldGenerator::generate, its CUDA kernels built for sm_100a, on this GPU: "
-                              f"one {Wd}x{Hd}x{Dd} region with {len(rt)} torches regenerated per env-step (reference "
-                              f"terrain; converged generation by wall clock, including its block-cache readback)"}
-        wb.close()
-    elif args.workload == "daynight":
-        c = dict(DAYNIGHT)
-        c["envs"] = args.envs or c["envs"]
-        E, Wd, Hd, Dd, F = c["envs"], c["W"], c["H"], c["D"], c["frame"]
-        cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, max_overrides=E * c["torches"])
-        wb = B.WorldBatch(cfg, device=local)
-        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
-        wb.generate(seeds, wb.place_torches(seeds, c["torches"]))
-        gen = torch.Generator().manual_seed(99 + rank)
-        frames = torch.randint(0, 256, (E, F, F, 4), dtype=torch.uint8, generator=gen).to(dev)
-        obs = torch.empty((E, 3, F, F), dtype=torch.float32, device=dev)
-        eff = torch.empty_like(wb.light) if args.materialize else None
-        half = c["steps_per_sweep"] // 2
-        # Tick of sweep step k: across the sunset ramp, then the sunrise ramp.
-        ticks = [12000 + (13702 - 12000) * k // (half - 1) for k in range(half)] + \
-                [22300 + (23961 - 22300) * k // (half - 1) for k in range(half)]
-        dims = torch.tensor([[B.sky_light_dimming(t)] * E for t in ticks], dtype=torch.uint8).pin_memory()
-        dim_dev = torch.empty(E, dtype=torch.uint8, device=dev)
+    e2e_ms, _ = time_steps(e2e, n, args.warmup, dev, pg, local)
+    (relight_ms,) = max_over_ranks([relight_ms], dev, pg)
+    env_steps = E * world * n
+    algo = 3 * dirty
+    achieved = algo / (relight_ms / 1e3) / 1e9
+    rec = {
+        "metric": "env-steps/s (incremental relight)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
+        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": ms / n, "higher_is_better": True,
+        "scaling": "weak", "dtype": "u8",
+        "config": {"workload": "relight: edits with World::setBlock semantics + exact incremental relight",
+                   "envs_per_gpu": E, "world": [Wd, Hd, Dd], "torches_per_env": c["torches"],
+                   "edits_per_step_per_gpu": n_edits, "mix": "45% dig, 45% stone, 5% torch, 5% remove torch, "
+                   "within 8 of the surface", "l2": "edits touch scattered regions of a 4.3 GB world",
+                   "parallelism": f"env shards x{world}"},
+        "roofline": {"bound": "hbm", "kernel": "relight (region kernels + tile path)", "achieved": achieved,
+                     "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_step": algo,
+                     "dirty_voxels_per_step": dirty, "dirty_voxels_first_last": [cn[0] for cn in counts],
+                     "changed_cells_per_step": counts[0][1], "light_class_changes_per_step": counts[0][2],
+                     "relight_ms": relight_ms, "edits_prep_ms": prof["edits_prep_ms"] / max(prof["edit_calls"], 1),
+                     "traffic": None},
+        "e2e": {"value": env_steps / (e2e_ms / 1e3), "unit": "env-steps/s",
+                "h2d_bytes_per_step": int(dev_batches[0].numel()), "d2h_bytes_per_step": 0},
+        "gpu_launches": LAUNCHES["relight"] * n, "clocks": clocks,
+    }
+    wb.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # The reference regenerates and relights the region for every edit
+        # (src/graphics/Renderer.cpp:1121-1141): one generation per env-step.
+        ref = reference_gpu_record(Wd, Hd, Dd, c["torches"], "env-steps/s", 1,
+                                   what="one env of this configuration, regenerated per env-step")
+        if ref is not None:
+            rec["reference_gpu"] = ref
+    return rec
 
-        def step(k):
-            dim_dev.copy_(dims[k % len(ticks)], non_blocking=True)
-            B.convert_rgba8_to_float_nchw(frames, out=obs)
-            if eff is not None:
-                wb.effective_light(dim_dev, out=eff)
 
-        ms, clocks = time_steps(step, args.steps, args.warmup, dev, pg, local)
-        env_steps = E * world * args.steps
-        conv_bytes = 16 * E * F * F + (2 * wb.light.numel() if eff is not None else 0)
-        achieved = conv_bytes * args.steps / (ms / 1e3) / 1e9
-        line.update({
-            "metric": "env-steps/s (day/night sweep)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
-            "ms_per_step": ms / args.steps, "dtype": "u8 -> f32",
-            "config": {"workload": "daynight: sky level by tick (sunset then sunrise ramps), dimming upload, "
-                                   "RGBA8 84x84 -> float32 NCHW" + (", effective light of every cell"
-                                                                     if eff is not None else ""),
-                       "envs_per_gpu": E, "world": [Wd, Hd, Dd], "torches_per_env": c["torches"],
-                       "frames": [E, 3, F, F], "l2": f"{conv_bytes / 1e9:.2f} GB moved per step (> 126 MB L2)",
-                       "parallelism": f"env shards x{world}"},
-            "roofline": {"bound": "hbm", "kernel": "rgba_to_nchw_vec_kernel" + (
-                " + effective_light_kernel" if eff is not None else ""), "achieved": achieved,
-                "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_step": conv_bytes, "traffic": None},
-            "gpu_launches": (2 if eff is not None else 1) * args.steps, "clocks": clocks})
-        wb.close()
-    elif args.workload == "render":
-        E = args.envs or ENVS_PER_GPU
-        cfg = B.WorldConfig(num_envs=E, width=W, height=H, depth=D, max_overrides=E * TORCHES)
-        wb = B.WorldBatch(cfg, device=local)
-        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
-        wb.generate(seeds, wb.place_torches(seeds, TORCHES))
-        hm = wb.height_map.cpu().numpy()
-        # Agents at the world centre on the surface, looking around, at several day times.
-        params = np.array([B.render_params_at((W / 2, hm[e, D // 2, W // 2] + 1, D / 2), 0.7 * e, -0.25,
-                                              (6000 + 997 * e) % 24000) for e in range(E)], B.RENDER_PARAMS_DTYPE)
-        params_dev = torch.from_numpy(params.view(np.uint8).copy()).to(dev)
-        frames = torch.empty((E, FRAME_H, FRAME_W, 4), dtype=torch.uint8, device=dev)
-        obs = torch.empty((E, 3, FRAME_H, FRAME_W), dtype=torch.float32, device=dev)
-        from blocklab_b200 import _native as N
+def daynight_record(args, rank, world, local, dev, pg, peaks, peak_kind, standalone):
+    import numpy as np
+    import torch
 
-        def step(k):
-            # Frames rendered straight into the observation tensor (RGBA8 kept too).
-            N.check(N.lib.blk_render_observations(wb._ctx, params_dev.data_ptr(), FRAME_W, FRAME_H, obs.data_ptr(),
-                                                  frames.data_ptr(), torch.cuda.current_stream(dev).cuda_stream))
+    import blocklab_b200 as B
 
-        ms, clocks = time_steps(step, args.steps, args.warmup, dev, pg, local)
-        line.update({
-            "metric": "frames/s (render to observations)", "value": E * world * args.steps / (ms / 1e3),
-            "unit": "frames/s", "ms_per_step": ms / args.steps, "dtype": "u8 -> f32",
-            "config": {"workload": "render: ray-cast 160x90 frames of the reset worlds into RGBA8 and float NCHW",
-                       "envs_per_gpu": E, "world": [W, H, D], "frames": [E, 3, FRAME_H, FRAME_W],
-                       "parallelism": f"env shards x{world}"},
-            "gpu_launches": args.steps, "clocks": clocks})
-        wb.close()
-    else:  # scaleout
-        c = dict(SCALEOUT)
-        c["envs"] = args.envs or c["envs"]
-        E, Wd, Hd, Dd = c["envs"], c["W"], c["H"], c["D"]
-        n_edits = c["edits_total"] * E // c["envs_total"]
-        cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, amplitude=c["amplitude"],
-                            max_overrides=E * c["torches"], max_edits=max(n_edits, 1))
-        wb = B.WorldBatch(cfg, device=local)
-        seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
-        seeds_dev = torch.from_numpy(seeds.view(np.int32)).to(dev)
-        reset_torches = {}
+    c = dict(DAYNIGHT)
+    E = (args.envs if standalone and args.envs else c["envs"])
+    Wd, Hd, Dd, Fr = c["W"], c["H"], c["D"], c["frame"]
+    cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, max_overrides=E * c["torches"])
+    wb = B.WorldBatch(cfg, device=local)
+    seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+    wb.generate(seeds, wb.place_torches(seeds, c["torches"]))
+    gen = torch.Generator().manual_seed(99 + rank)
+    frames_host = torch.randint(0, 256, (E, Fr, Fr, 4), dtype=torch.uint8, generator=gen).pin_memory()
+    frames = frames_host.to(dev)
+    obs = torch.empty((E, 3, Fr, Fr), dtype=torch.float32, device=dev)
+    eff = torch.empty_like(wb.light) if args.materialize else None
+    half = c["steps_per_sweep"] // 2
+    # Tick of sweep step k: across the sunset ramp, then the sunrise ramp.
+    ticks = [12000 + (13702 - 12000) * k // (half - 1) for k in range(half)] + \
+            [22300 + (23961 - 22300) * k // (half - 1) for k in range(half)]
+    dims = torch.tensor([[B.sky_light_dimming(t)] * E for t in ticks], dtype=torch.uint8).pin_memory()
+    dim_dev = torch.empty(E, dtype=torch.uint8, device=dev)
 
-        def reset(k):
-            reset_torches["t"] = wb.place_torches(seeds_dev, c["torches"])
-            wb.generate(seeds_dev, reset_torches["t"])
+    def step(k, src=frames):
+        dim_dev.copy_(dims[k % len(ticks)], non_blocking=True)
+        B.convert_rgba8_to_float_nchw(src, out=obs)
+        if eff is not None:
+            wb.effective_light(dim_dev, out=eff)
 
-        reset_ms, reset_clocks = time_steps(reset, 1, 1, dev, pg, local)
-        hm = wb.height_map.cpu().numpy()
-        tl = reset_torches["t"].cpu().numpy().view(B.OVERRIDE_DTYPE).reshape(E, c["torches"])
-        txyz = np.stack([tl["x"], tl["y"], tl["z"]], 2)
-        batches = [torch.from_numpy(surface_edits(rng, hm, E, n_edits, Wd, Dd, txyz).view(np.uint8).copy()).to(dev)
-                   for _ in range(args.warmup + args.steps)]
-        gen = torch.Generator().manual_seed(7 + rank)
-        frames = torch.randint(0, 256, (E, FRAME_H, FRAME_W, 4), dtype=torch.uint8, generator=gen).to(dev)
-        obs = torch.empty((E, 3, FRAME_H, FRAME_W), dtype=torch.float32, device=dev)
-        gathered = None
-        if args.gather and pg is not None and rank == 0:
-            gathered = [torch.empty_like(obs) for _ in range(world)]
+    ms_probe, _ = time_steps(step, 3, args.warmup, dev, pg, local)
+    n = sustained_steps(ms_probe / 3, args.steps, dev, pg)
+    ms, clocks = time_steps(step, n, args.warmup, dev, pg, local)
+    stage = torch.empty_like(frames)
 
+    def e2e(k):
+        stage.copy_(frames_host, non_blocking=True)
+        step(k, stage)
+
+    ms_probe, _ = time_steps(e2e, 2, 1, dev, pg, local)
+    n_e2e = sustained_steps(ms_probe / 2, args.steps, dev, pg)
+    e2e_ms, _ = time_steps(e2e, n_e2e, 1, dev, pg, local)
+    env_steps = E * world * n
+    conv_bytes = 16 * E * Fr * Fr + (2 * wb.light.numel() if eff is not None else 0)
+    achieved = conv_bytes * n / (ms / 1e3) / 1e9
+    rec = {
+        "metric": "env-steps/s (day/night sweep)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
+        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": ms / n, "higher_is_better": True,
+        "scaling": "weak", "dtype": "u8 -> f32",
+        "config": {"workload": "daynight: sky level by tick (sunset then sunrise ramps), dimming upload, RGBA8 "
+                               "84x84 -> float32 NCHW" + (", effective light of every cell" if eff is not None else ""),
+                   "envs_per_gpu": E, "world": [Wd, Hd, Dd], "torches_per_env": c["torches"],
+                   "frames": [E, 3, Fr, Fr], "l2": f"{conv_bytes / 1e9:.2f} GB moved per step (> 126 MB L2)",
+                   "parallelism": f"env shards x{world}"},
+        "roofline": {"bound": "hbm", "kernel": "rgba_to_nchw_vec_kernel" + (
+            " + effective_light_kernel" if eff is not None else ""), "achieved": achieved,
+            "peak": peaks["hbm_gbs"], "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_step": conv_bytes, "traffic": None},
+        "e2e": {"value": E * world * n_e2e / (e2e_ms / 1e3), "unit": "env-steps/s", "steps": n_e2e,
+                "h2d_bytes_per_step": frames.numel() + E, "d2h_bytes_per_step": 0},
+        "gpu_launches": (2 if eff is not None else 1) * n, "clocks": clocks,
+    }
+    wb.close()
+    return rec
+
+
+def scaleout_record(args, rank, world, local, dev, pg, peaks, peak_kind, standalone):
+    import numpy as np
+    import torch
+
+    import blocklab_b200 as B
+
+    c = dict(SCALEOUT)
+    E = (args.envs if standalone and args.envs else c["envs"])
+    Wd, Hd, Dd = c["W"], c["H"], c["D"]
+    n_edits = max(c["edits_total"] * E // c["envs_total"], 1)
+    FH, FW = RESET["frame"]
+    cfg = B.WorldConfig(num_envs=E, width=Wd, height=Hd, depth=Dd, amplitude=c["amplitude"],
+                        max_overrides=E * c["torches"], max_edits=n_edits)
+    wb = B.WorldBatch(cfg, device=local)
+    seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+    seeds_dev = torch.from_numpy(seeds.view(np.int32)).to(dev)
+    reset_torches = {}
+
+    def reset(_k):
+        reset_torches["t"] = wb.place_torches(seeds_dev, c["torches"])
+        wb.generate(seeds_dev, reset_torches["t"])
+
+    ms_probe, _ = time_steps(reset, 1, 1, dev, pg, local)
+    n_reset = sustained_steps(ms_probe, 1, dev, pg)
+    reset_ms, reset_clocks = time_steps(reset, n_reset, 1, dev, pg, local)
+    hm = wb.height_map.cpu().numpy()
+    tl = reset_torches["t"].cpu().numpy().view(B.OVERRIDE_DTYPE).reshape(E, c["torches"])
+    txyz = np.stack([tl["x"], tl["y"], tl["z"]], 2)
+    rng = np.random.default_rng(7 + rank)
+    gen = torch.Generator().manual_seed(7 + rank)
+    frames_host = torch.randint(0, 256, (E, FH, FW, 4), dtype=torch.uint8, generator=gen).pin_memory()
+    frames = frames_host.to(dev)
+    obs = torch.empty((E, 3, FH, FW), dtype=torch.float32, device=dev)
+    gathered = [torch.empty_like(obs) for _ in range(world)] if args.gather and pg is not None and rank == 0 else None
+
+    def make(n):
+        return [torch.from_numpy(surface_edits(rng, hm, E, n_edits, Wd, Dd, txyz).view(np.uint8).copy()).to(dev)
+                for _ in range(n)]
+
+    probe = make(args.warmup + 3)
+
+    def step_with(batches, src=frames):
         def step(k):
             wb.apply_edits(batches[k])
-            B.convert_rgba8_to_float_nchw(frames, out=obs)
+            B.convert_rgba8_to_float_nchw(src, out=obs)
             if args.gather and pg is not None:
                 pg.gather(obs, gathered if rank == 0 else None, dst=0)
+        return step
 
-        ms, clocks = time_steps(step, args.steps, args.warmup, dev, pg, local)
-        env_steps = E * world * args.steps
-        line.update({
-            "metric": "env-steps/s (scale-out)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
-            "ms_per_step": ms / args.steps, "dtype": "u8",
-            "config": {"workload": "scaleout: per step edits + exact relight + 90x160 frame conversion"
-                                   + (" + NCCL gather of observations to rank 0" if args.gather else ""),
-                       "envs_per_gpu": E, "world": [Wd, Hd, Dd], "terrain": "fBm 40+round(120*fbm)",
-                       "torches_per_env": c["torches"], "edits_per_step_per_gpu": n_edits,
-                       "l2": "34 GB of world per GPU", "parallelism": f"env shards x{world}"},
-            "reset": {"ms": reset_ms, "voxels_per_s": E * world * Wd * Hd * Dd / (reset_ms / 1e3),
-                      "clocks": reset_clocks},
-            "gpu_launches": None, "clocks": clocks})
-        wb.close()
+    ms_probe, _ = time_steps(step_with(probe), 3, args.warmup, dev, pg, local)
+    n = sustained_steps(ms_probe / 3, args.steps, dev, pg)
+    batches = make(args.warmup + n)
+    ms, clocks = time_steps(step_with(batches), n, args.warmup, dev, pg, local)
+    # End to end: edits and frames copied from pinned host memory every step.
+    pinned = [b.cpu().pin_memory() for b in batches]
+    stage_e, stage_f = torch.empty_like(batches[0]), torch.empty_like(frames)
+
+    def e2e(k):
+        stage_e.copy_(pinned[k], non_blocking=True)
+        stage_f.copy_(frames_host, non_blocking=True)
+        wb.apply_edits(stage_e)
+        B.convert_rgba8_to_float_nchw(stage_f, out=obs)
+
+    ms_probe, _ = time_steps(e2e, 2, 1, dev, pg, local)
+    n_e2e = min(sustained_steps(ms_probe / 2, args.steps, dev, pg), n)
+    e2e_ms, _ = time_steps(e2e, n_e2e, args.warmup, dev, pg, local)
+    env_steps = E * world * n
+    vox = E * Wd * Hd * Dd
+    reset_step_ms = reset_ms / n_reset
+    rec = {
+        "metric": "env-steps/s (scale-out)", "value": env_steps / (ms / 1e3), "unit": "env-steps/s",
+        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": ms / n, "higher_is_better": True,
+        "scaling": "weak", "dtype": "u8",
+        "config": {"workload": "scaleout: per step edits + exact relight + 90x160 frame conversion"
+                               + (" + NCCL gather of observations to rank 0" if args.gather else ""),
+                   "envs_per_gpu": E, "world": [Wd, Hd, Dd], "terrain": "fBm 40+round(120*fbm)",
+                   "torches_per_env": c["torches"], "edits_per_step_per_gpu": n_edits,
+                   "edits_reading": "5,000 edits per step over the whole 8192-env batch (not 5,000 per env)",
+                   "l2": f"{2 * vox / 1e9:.1f} GB of world per GPU", "parallelism": f"env shards x{world}"},
+        "reset": {"steps": n_reset, "ms": reset_step_ms, "voxels_per_s": vox * world / (reset_step_ms / 1e3),
+                  "clocks": reset_clocks},
+        "roofline": {"bound": "hbm", "kernel": "reset step (2 B per voxel written)",
+                     "achieved": 2 * vox / (reset_step_ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
+                     "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": 2 * vox / (reset_step_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                     "algorithmic_bytes_per_reset": 2 * vox, "traffic": None},
+        "e2e": {"value": E * world * n_e2e / (e2e_ms / 1e3), "unit": "env-steps/s", "steps": n_e2e,
+                "h2d_bytes_per_step": int(batches[0].numel() + frames.numel()), "d2h_bytes_per_step": 0},
+        "gpu_launches": LAUNCHES["scaleout"] * n, "clocks": clocks,
+    }
+    wb.close()
+    return rec
+
+
+def render_record(args, rank, world, local, dev, pg, peaks, peak_kind, standalone):
+    import numpy as np
+    import torch
+
+    import blocklab_b200 as B
+    from blocklab_b200 import _native as N
+
+    E = args.envs or RESET["envs"]
+    W, H, D, T = RESET["W"], RESET["H"], RESET["D"], RESET["torches"]
+    FH, FW = RESET["frame"]
+    wb = B.WorldBatch(B.WorldConfig(num_envs=E, width=W, height=H, depth=D, max_overrides=E * T), device=local)
+    seeds = (BASE_SEED + rank * E + np.arange(E)).astype(np.uint32)
+    wb.generate(seeds, wb.place_torches(seeds, T))
+    hm = wb.height_map.cpu().numpy()
+    # Agents at the world centre on the surface, looking around, at several day times.
+    params = np.array([B.render_params_at((W / 2, hm[e, D // 2, W // 2] + 1, D / 2), 0.7 * e, -0.25,
+                                          (6000 + 997 * e) % 24000) for e in range(E)], B.RENDER_PARAMS_DTYPE)
+    params_dev = torch.from_numpy(params.view(np.uint8).copy()).to(dev)
+    frames = torch.empty((E, FH, FW, 4), dtype=torch.uint8, device=dev)
+    obs = torch.empty((E, 3, FH, FW), dtype=torch.float32, device=dev)
+
+    def step(_k):
+        # Frames rendered straight into the observation tensor (RGBA8 kept too).
+        N.check(N.lib.blk_render_observations(wb._ctx, params_dev.data_ptr(), FW, FH, obs.data_ptr(),
+                                              frames.data_ptr(), torch.cuda.current_stream(dev).cuda_stream))
+
+    ms_probe, _ = time_steps(step, 3, args.warmup, dev, pg, local)
+    n = sustained_steps(ms_probe / 3, args.steps, dev, pg)
+    ms, clocks = time_steps(step, n, args.warmup, dev, pg, local)
+    wb.close()
+    return {"metric": "frames/s (render to observations)", "value": E * world * n / (ms / 1e3), "unit": "frames/s",
+            "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": ms / n, "higher_is_better": True,
+            "scaling": "weak", "dtype": "u8 -> f32",
+            "config": {"workload": "render: ray-cast 160x90 frames of the reset worlds into RGBA8 and float NCHW",
+                       "envs_per_gpu": E, "world": [W, H, D], "frames": [E, 3, FH, FW],
+                       "parallelism": f"env shards x{world}"},
+            "gpu_launches": LAUNCHES["render"] * n, "clocks": clocks}
+
+
+RECORDS = {"relight": relight_record, "daynight": daynight_record, "scaleout": scaleout_record,
+           "render": render_record}
+
+
+def run_ours(args) -> None:
+    rank, world, local, dev, pg = init_dist()
+    peaks, peak_kind = measured_peaks()
+    common = (args, rank, world, local, dev, pg, peaks, peak_kind)
+    if args.workload == "reset":
+        line = reset_record(*common)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            times, vox, cores, desc = reference_cpu_times(1)
+            line["cpu_baseline"] = {"value": vox / times[-1], "unit": "voxels/s", "cores": cores,
+                                    "kind": "reference", "sample": desc}
+            ref = reference_gpu_record(RESET["W"], RESET["H"], RESET["D"], RESET["torches"], "voxels/s",
+                                       RESET["W"] * RESET["H"] * RESET["D"])
+            if ref is not None:
+                line["reference_gpu"] = ref
+        if not args.no_configs:
+            line["configs"] = {name: RECORDS[name](*common, False) for name in ("relight", "daynight", "scaleout")}
+    else:
+        line = {"n_gpus": world, "vs_baseline": None, "data": "synthetic"}
+        line.update(RECORDS[args.workload](*common, True))
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -748,51 +812,46 @@ def run_workload(args) -> None:
         pg.destroy_process_group()
 
 
-def run_workload_reference(args) -> None:
-    """The reference regenerates a region for every edit
-    (src/graphics/Renderer.cpp:1121-1141): one env-step of relight costs one
-    WorldGenerator::generate of the region, timed on the host cores."""
+# ------------------------------------------------------------ reference --
+def run_reference(args) -> None:
+    """The reference's own CPU implementation of the path on the box's host
+    cores: `--warmup` + `--steps` consecutive generations of the bounded
+    sample of the reset world (one generator, converged first). Rank 0 only."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    if args.workload != "relight":
+    if args.workload != "reset":
         print(json.dumps({"impl": "reference", "workload": args.workload,
-                          "unavailable": "the reference has no batched CPU path for this workload"}), flush=True)
+                          "unavailable": "the reference arm is timed on the reset workload, the metric's "
+                                         "configuration; per-configuration reference figures are the "
+                                         "reference_gpu records of the default line"}), flush=True)
         return
-    import numpy as np
-
-    from oracle.oracle import TERRAIN_REFERENCE, Oracle, Reference, WorldSpec, ref_available
+    from oracle.oracle import ref_available
 
     if not ref_available("cpu"):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_cpu.so not built"}), flush=True)
         return
-    O, R = Oracle(), Reference("cpu")
-    c = RELIGHT
-    spec = WorldSpec(BASE_SEED, c["W"], c["H"], c["D"], terrain=TERRAIN_REFERENCE)
-    torches = O.place_torches(spec, c["torches"], 0x5EED)
-    times = []
-    for i in range(args.warmup + args.steps):
-        timing = []
-        R.generate(BASE_SEED, (0, 0, 0), (c["W"], c["H"], c["D"]), torches, np.full(len(torches), 4, np.uint8),
-                   runs=1, timing=timing)
-        if i >= args.warmup:
-            times.append(timing[-1] / 1e3)
-    value = len(times) / sum(times)
-    print(json.dumps({"impl": "reference", "metric": "env-steps/s (incremental relight)", "value": value,
-                      "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                      "higher_is_better": True,
-                      "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": os.cpu_count() or 1,
-                                       "kind": "reference",
-                                       "sample": f"one WorldGenerator::generate of a {c['W']}x{c['H']}x{c['D']} region "
-                                                 f"with {len(torches)} torches per env-step (reference terrain)"}}),
-          flush=True)
+    times, vox, cores, desc = reference_cpu_times(args.warmup + args.steps)
+    timed = times[args.warmup:]
+    total = sum(timed)
+    value = vox * len(timed) / total
+    cfg = {"workload": "world reset: generation + full sky/block light (bounded sample of the reset world)",
+           "world": [SAMPLE["W"], SAMPLE["H"], SAMPLE["D"]], "sample_of": [RESET["W"], RESET["H"], RESET["D"]],
+           "envs_per_step": 1, "terrain": "fBm 40+round(50*fbm) as a dense override list",
+           "parallelism": "host threads"}
+    print(json.dumps({
+        "impl": "reference", "metric": "voxels lit+generated/s", "value": value, "unit": "voxels/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(timed),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": "voxels/s", "cores": cores, "kind": "reference", "sample": desc},
+        "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+        flush=True)
 
 
 def main() -> None:
     args = parse_args()
-    if args.workload != "reset":
-        run_workload(args)
-    elif args.impl == "reference":
+    if args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -244,22 +244,49 @@ class Reference:
         vox = np.zeros(max(max_voxels, 1) * 3, np.uint32)
         cnt = np.zeros(1, np.uint32)
         hdr = np.zeros(3, np.int32)
-        last_ms = ctypes.c_double(0.0)
+        run_ms = np.zeros(max(runs, 1), np.float64)
         rc = self.lib.ref_generate(ctypes.c_uint32(seed & 0xFFFFFFFF), ctypes.c_int32(origin[0]),
                                    ctypes.c_int32(origin[1]), ctypes.c_int32(origin[2]), ctypes.c_uint32(W),
                                    ctypes.c_uint32(H), ctypes.c_uint32(D), _ptr(xyz), _ptr(blk),
                                    ctypes.c_uint32(len(blk)), ctypes.c_int32(runs), _ptr(b), _ptr(bl), _ptr(sl),
                                    _ptr(hm), _ptr(vox), ctypes.c_uint32(max_voxels), _ptr(cnt), _ptr(hdr),
-                                   ctypes.byref(last_ms))
+                                   _ptr(run_ms))
         if rc != 0:
             raise RuntimeError(f"reference generate failed: {rc}")
-        if timing is not None:
-            timing.append(last_ms.value)
+        if timing is not None:  # wall time of every generation, ms
+            timing.extend(float(v) for v in run_ms)
         sh = (D, H, W)
         n = int(min(cnt[0], max_voxels))
         return dict(blocks=b.reshape(sh), block_light=bl.reshape(sh), sky_light=sl.reshape(sh),
                     height_map=hm.reshape(D, W).astype(np.int16), voxel_count=int(cnt[0]),
                     voxels=vox.reshape(-1, 3)[:n].copy(), header=tuple(int(v) for v in hdr))
+
+    @staticmethod
+    def dense_overrides(blocks: np.ndarray, origin=(0, 0, 0)):
+        """Every cell of a block volume (D, H, W) as override records (xyz, ids)."""
+        D, H, W = blocks.shape
+        z, y, x = np.meshgrid(np.arange(D, dtype=np.int32), np.arange(H, dtype=np.int32),
+                              np.arange(W, dtype=np.int32), indexing="ij")
+        xyz = np.stack([x.ravel() + origin[0], y.ravel() + origin[1], z.ravel() + origin[2]], 1)
+        return xyz, np.ascontiguousarray(blocks.ravel(), np.uint8)
+
+    def kernel_time(self, blocks: np.ndarray, origin=(0, 0, 0), runs: int = 2, reps: int = 5):
+        """(kernel ms, wall ms) of the reference's generator on a block volume
+        given as dense overrides: device time of its own kernels per generation
+        (CUDA events around a graph of the kernels of one captured generation,
+        without its host work and copies), and the wall time of one ordinary
+        generation. CUDA build only."""
+        D, H, W = blocks.shape
+        xyz, blk = self.dense_overrides(blocks, origin)
+        k_ms, w_ms = ctypes.c_double(0.0), ctypes.c_double(0.0)
+        rc = self.lib.ref_kernel_time(ctypes.c_uint32(0), ctypes.c_int32(origin[0]), ctypes.c_int32(origin[1]),
+                                      ctypes.c_int32(origin[2]), ctypes.c_uint32(W), ctypes.c_uint32(H),
+                                      ctypes.c_uint32(D), _ptr(xyz), _ptr(blk), ctypes.c_uint32(len(blk)),
+                                      ctypes.c_int32(runs), ctypes.c_int32(reps), ctypes.byref(k_ms),
+                                      ctypes.byref(w_ms))
+        if rc != 0:
+            raise RuntimeError(f"reference kernel timing failed: {rc}")
+        return k_ms.value, w_ms.value
 
     def light_blocks(self, blocks: np.ndarray, origin=(0, 0, 0), runs: int = 2, timing: Optional[list] = None):
         """The reference's generator run over a given block volume (D, H, W):
@@ -269,11 +296,8 @@ class Reference:
         H <= 128 (uchar3 light-source coordinates, int8 height map); the render
         voxel list is skipped (its packing needs W, D <= 64)."""
         D, H, W = blocks.shape
-        z, y, x = np.meshgrid(np.arange(D, dtype=np.int32), np.arange(H, dtype=np.int32),
-                              np.arange(W, dtype=np.int32), indexing="ij")
-        xyz = np.stack([x.ravel() + origin[0], y.ravel() + origin[1], z.ravel() + origin[2]], 1)
-        return self.generate(0, origin, (W, H, D), xyz, np.ascontiguousarray(blocks.ravel(), np.uint8), runs=runs,
-                             max_voxels=0, timing=timing)
+        xyz, blk = self.dense_overrides(blocks, origin)
+        return self.generate(0, origin, (W, H, D), xyz, blk, runs=runs, max_voxels=0, timing=timing)
 
     def convert_rgba8(self, rgba: np.ndarray) -> np.ndarray:
         n, h, w, _ = rgba.shape
