@@ -1637,8 +1637,12 @@ int blk_build_render_voxels_static(const uint8_t* ids, const uint8_t* light, uin
                   "height <= 512, depth * height <= 32768 rows)");
         return BLK_ERR_CAPACITY;
     }
-    // Set-up, once per device, with that device current: the scratch array's
-    // device address. Later calls only read the cached pointer.
+    // The scratch array's device address on the current device. Outside a
+    // stream capture it is looked up on every call (a cheap query that
+    // allocates nothing), so a cudaDeviceReset or a reloaded module never
+    // leaves a stale address behind; inside a capture the address of the
+    // device's last uncaptured call is used, so the first call on a device
+    // must come before any capture.
     constexpr int kMaxDevices = 64;
     static std::mutex setup_mutex;
     static uint32_t* scratch_of[kMaxDevices] = {};
@@ -1648,13 +1652,36 @@ int blk_build_render_voxels_static(const uint8_t* ids, const uint8_t* light, uin
         set_error("blk_build_render_voxels_static: device ordinal out of range");
         return BLK_ERR_INVALID_ARGUMENT;
     }
+    {
+        // The world must live on the current device: the scratch is per device.
+        cudaPointerAttributes attr {};
+        if (cudaPointerGetAttributes(&attr, ids) != cudaSuccess) {
+            cudaGetLastError();
+            attr.type = cudaMemoryTypeUnregistered;
+        }
+        if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+            set_error("blk_build_render_voxels_static: ids must be device memory");
+            return BLK_ERR_INVALID_ARGUMENT;
+        }
+        if (attr.type == cudaMemoryTypeDevice && attr.device != dev) {
+            set_error("blk_build_render_voxels_static: ids live on device " + std::to_string(attr.device)
+                + ", not on the current device " + std::to_string(dev));
+            return BLK_ERR_INVALID_ARGUMENT;
+        }
+    }
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    BLK_CUDA(cudaStreamIsCapturing(as_stream(stream_handle), &capture), "cudaStreamIsCapturing");
     uint32_t* scratch;
     {
         std::lock_guard<std::mutex> lock(setup_mutex);
-        if (!scratch_of[dev]) {
+        if (capture == cudaStreamCaptureStatusNone) {
             void* addr = nullptr;
             BLK_CUDA(cudaGetSymbolAddress(&addr, g_voxel_rows), "cudaGetSymbolAddress (render voxel scratch)");
             scratch_of[dev] = static_cast<uint32_t*>(addr);
+        } else if (!scratch_of[dev]) {
+            set_error("blk_build_render_voxels_static: the first call on a device must come before any stream "
+                      "capture");
+            return BLK_ERR_INVALID_ARGUMENT;
         }
         scratch = scratch_of[dev];
     }

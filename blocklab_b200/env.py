@@ -7,8 +7,10 @@ from the library's own ray-cast frames of the worlds.
 
 Observations are double-buffered device tensors, valid until the next call
 after the following one (the reference's renderer double-buffers them the
-same way, src/graphics/Renderer.cpp:605-613); they export through DLPack
-(`torch.utils.dlpack.to_dlpack` or the tensor's `__dlpack__`).
+same way, src/graphics/Renderer.cpp:605-613). reset / step / render return a
+WorldObservation: a DLPack producer whose consumer stream waits for the
+observation's write, as the reference's BlockLabObservation does
+(python/blocklab/env.py:29-62, src/python/Bindings.cpp:138-183).
 """
 from __future__ import annotations
 
@@ -20,6 +22,46 @@ import torch
 from .observation import convert_rgba8_to_float_nchw
 from .sharding import env_seeds, shard_envs
 from .world import WorldBatch, WorldConfig
+
+
+class WorldObservation:
+    """One observation: the float32 (envs, 3, height, width) tensor written on
+    the env's stream and a CUDA event recorded after that write. Importing it
+    through DLPack (torch.from_dlpack(obs), or obs.to_tensor()) makes the
+    consumer's stream wait for the event first, so a consumer on any stream
+    sees the finished observation; the data stays valid until the env's next
+    call after the following one."""
+
+    def __init__(self, tensor: torch.Tensor, event: torch.cuda.Event, version: int) -> None:
+        self._tensor = tensor
+        self._event = event
+        self.version = version
+        self.shape = tuple(tensor.shape)
+        self.dtype = tensor.dtype
+        self.device = tensor.device
+
+    def __dlpack_device__(self) -> tuple[int, int]:
+        return (2, self.device.index if self.device.index is not None else 0)  # kDLCUDA
+
+    def __dlpack__(self, stream: Optional[int] = None, **_kwargs):
+        """DLPack capsule of the tensor after making `stream` wait for the
+        observation: None waits on the current stream, 1 is the legacy default
+        stream, 2 the per-thread default stream, any other value a stream
+        handle (the DLPack stream convention for CUDA)."""
+        if stream is None:
+            consumer = torch.cuda.current_stream(self.device)
+        else:
+            handle = 0 if stream == 1 else stream  # 0 addresses the legacy default stream
+            consumer = torch.cuda.ExternalStream(handle, device=self.device)
+        consumer.wait_event(self._event)
+        return torch.utils.dlpack.to_dlpack(self._tensor)
+
+    def to_tensor(self) -> torch.Tensor:
+        return torch.from_dlpack(self)
+
+    def wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Makes `stream` (default: the current one) wait for the observation."""
+        (stream or torch.cuda.current_stream(self.device)).wait_event(self._event)
 
 
 class WorldEnv:
@@ -47,15 +89,21 @@ class WorldEnv:
         self._version = 0
         self._reset_done = False
 
-    def _next_obs(self, frames: Optional[torch.Tensor]) -> torch.Tensor:
+    def _published(self, out: torch.Tensor) -> WorldObservation:
+        """Records the observation's ready event on the current stream."""
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._version += 1
+        return WorldObservation(out, ev, self._version)
+
+    def _next_obs(self, frames: Optional[torch.Tensor]) -> WorldObservation:
         out = self._obs[self._flip]
         self._flip ^= 1
         if frames is not None:
             if frames.shape != (self.config.num_envs, self.height, self.width, 4):
                 raise ValueError(f"frames must be ({self.config.num_envs}, {self.height}, {self.width}, 4) uint8")
             convert_rgba8_to_float_nchw(frames, out=out)
-        self._version += 1
-        return out
+        return self._published(out)
 
     def reset(self, *, seed: int = 1, overrides=None, frames: Optional[torch.Tensor] = None, origins=None):
         """Regenerates and fully relights every owned world. World i (global
@@ -76,15 +124,14 @@ class WorldEnv:
         seeds = np.array([env_seeds(seed, self.env_begin + int(i), 1, self.seed_policy)[0] for i in ids], np.uint32)
         self.world.generate_envs(ids.astype(np.uint32), seeds, overrides, origins=origins)
 
-    def render(self, params) -> torch.Tensor:
+    def render(self, params) -> WorldObservation:
         """Observation rendered by the library itself: ray-cast RGBA8 frames of
         every owned world from per-env render parameters (render_params_at),
         converted to float32 NCHW."""
         out = self._obs[self._flip]
         self._flip ^= 1
         self.world.render_observations(params, self.width, self.height, out=out)
-        self._version += 1
-        return out
+        return self._published(out)
 
     def step(self, edits=None, frames: Optional[torch.Tensor] = None):
         """Applies edits (World::setBlock semantics, exact relight) and converts

@@ -177,11 +177,16 @@ int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t m
  * device memory at call time, e.g. a renderer recording its frame work.
  * Limits: width, depth <= 64 and height <= 512 (the reference packing) and
  * depth * height <= 32768 rows; larger regions return BLK_ERR_CAPACITY.
- * The first call on a device does the set-up (looks up the scratch array's
- * device address with that device current) and should come before any
- * stream capture. Nothing has to start at zero. All calls on a device share
- * the scratch: calls that overlap in time (other streams or host threads)
- * race, so order them. `voxels`, `count` and `header` are device memory. */
+ * The world must live on the current device (its scratch is used; another
+ * device's world returns BLK_ERR_INVALID_ARGUMENT). Each call outside a stream
+ * capture looks up the scratch array's device address with that device
+ * current (a query that allocates nothing, so it stays right across a
+ * cudaDeviceReset); a call inside a capture reuses the address of the
+ * device's last call outside one, so the first call on a device must come
+ * before any stream capture. Nothing has to start at zero. All calls on a
+ * device share the scratch: calls that overlap in time (other streams or host
+ * threads) race, so order them. `voxels`, `count` and `header` are device
+ * memory. */
 int blk_build_render_voxels_static(const uint8_t* ids, const uint8_t* light, uint32_t width, uint32_t height,
     uint32_t depth, int32_t origin_x, int32_t origin_y, int32_t origin_z, void* voxels, uint32_t max_voxels,
     uint32_t* count, int32_t* header, uintptr_t stream);

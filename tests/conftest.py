@@ -7,7 +7,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-REFERENCE = "/root/reference"
+# The reference checkout, when present (BLOCKLAB_REFERENCE_DIR, else its usual location here).
+REFERENCE = os.environ.get("BLOCKLAB_REFERENCE_DIR", "/root/reference")
 
 
 def pytest_configure(config):

@@ -1,6 +1,6 @@
 """Generates tests/golden/lighting_scenarios.npz from the reference itself.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference DIR]   (default: $BLOCKLAB_REFERENCE_DIR or /root/reference)
 
 For every generation of the lighting-test scenarios (tests/golden/scenarios.py)
 this runs the reference's own generator (its CUDA CPU-fallback build,
@@ -29,7 +29,7 @@ from oracle.oracle import Reference  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("BLOCKLAB_REFERENCE_DIR", "/root/reference"))
     args = ap.parse_args()
     masks = S.parse_masks(os.path.join(args.reference, "tests", "WorldLighting.cpp"))
     R = Reference("cpu")

@@ -59,7 +59,7 @@ def test_reset_and_step_match_oracle(B, oracle):
         assert np.array_equal(got[1], bl) and np.array_equal(got[2], sl)
         state.append((blocks, hm))
     want_obs = oracle.convert_rgba8(frames.cpu().numpy())
-    assert np.array_equal(obs.cpu().numpy().view(np.uint32), want_obs.view(np.uint32))
+    assert np.array_equal(obs.to_tensor().cpu().numpy().view(np.uint32), want_obs.view(np.uint32))
     for step in range(3):
         lists, local = [], []
         for e in range(3):
@@ -108,13 +108,15 @@ def test_observation_buffers_and_dlpack(B):
     f1 = torch.randint(0, 256, (3, 24, 32, 4), dtype=torch.uint8, device="cuda")
     f2 = torch.randint(0, 256, (3, 24, 32, 4), dtype=torch.uint8, device="cuda")
     o1, _ = env.reset(seed=1, frames=f1)
-    keep = o1.clone()
+    t1 = o1.to_tensor()
+    keep = t1.clone()
     o2, _ = env.step(frames=f2)
-    assert o1.data_ptr() != o2.data_ptr()
-    assert torch.equal(o1, keep)  # the previous observation stays valid for one more call
-    cap = torch.utils.dlpack.to_dlpack(o2)
-    back = torch.utils.dlpack.from_dlpack(cap)
-    assert back.data_ptr() == o2.data_ptr() and back.shape == (3, 3, 24, 32)
+    t2 = torch.from_dlpack(o2)
+    assert t1.data_ptr() != t2.data_ptr() and o2.version == o1.version + 1
+    assert torch.equal(t1, keep)  # the previous observation stays valid for one more call
+    assert o2.__dlpack_device__() == (2, 0) and o2.shape == (3, 3, 24, 32)
+    back = torch.utils.dlpack.from_dlpack(o2.__dlpack__(stream=1))  # legacy default stream
+    assert back.data_ptr() == t2.data_ptr() and back.shape == (3, 3, 24, 32)
     with pytest.raises(ValueError):
         env.step(frames=torch.zeros((3, 24, 31, 4), dtype=torch.uint8, device="cuda"))
     env.close()
@@ -177,7 +179,7 @@ def test_env_renders_its_observations(B):
     env.reset(seed=4)
     params = np.array([B.render_params_at((-10 + 3 * e, 45, -5), 0.5 * e, -0.4, 3000) for e in range(3)],
                       B.RENDER_PARAMS_DTYPE)
-    obs = env.render(params)
+    obs = env.render(params).to_tensor()
     frames = env.world.render(params, 32, 24)
     torch.cuda.synchronize()
     assert obs.shape == (3, 3, 24, 32)
@@ -237,3 +239,31 @@ def test_partial_reset_matches_oracle_with_new_origins(B, oracle):
     got = _batch_world(wb, 1)
     assert np.array_equal(got[0], blocks) and np.array_equal(got[1], bl) and np.array_equal(got[2], sl)
     wb.close()
+
+
+def test_observation_consumed_on_another_stream(B, oracle):
+    """The consumer of an observation runs on its own stream while the
+    producer's stream is still busy (a ~25 ms spin queued before the
+    conversion): importing it through DLPack makes the consumer stream wait
+    for the write, as the reference's observation_dlpack does with
+    enqueueReadyWait (src/python/Bindings.cpp:150-151)."""
+    env = _env(B)
+    env.reset(seed=2)
+    rng = np.random.default_rng(12)
+    frames_np = rng.integers(0, 256, (3, 24, 32, 4), dtype=np.uint8)
+    frames = torch.from_numpy(frames_np).cuda()
+    want = torch.from_numpy(oracle.convert_rgba8(frames_np)).cuda()
+    consumer = torch.cuda.Stream()
+    for trial in range(3):
+        torch.cuda.synchronize()
+        torch.cuda._sleep(50_000_000)  # the producer stream stays busy before the conversion
+        obs, _ = env.step(frames=frames)
+        with torch.cuda.stream(consumer):
+            t = torch.from_dlpack(obs)  # the consumer stream waits for the observation's event
+            total = (t == want).all()
+        consumer.synchronize()
+        assert bool(total.item()), f"trial {trial}: the consumer read the observation before it was written"
+        frames = torch.flip(frames, dims=[0]).contiguous()
+        frames_np = frames_np[::-1].copy()
+        want = torch.from_numpy(oracle.convert_rgba8(frames_np)).cuda()
+    env.close()

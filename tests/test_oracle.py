@@ -20,7 +20,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "golden"))
 import scenarios as S  # noqa: E402
 
-REFERENCE = "/root/reference"
+# The reference checkout (its test files are parsed when present).
+REFERENCE = os.environ.get("BLOCKLAB_REFERENCE_DIR", "/root/reference")
 GOLDEN = os.path.join(HERE, "golden", "lighting_scenarios.npz")
 
 

@@ -75,4 +75,10 @@ def test_static_voxels_match_context_entry_on_consecutive_calls():
     torch.cuda.synchronize(dev)
     assert int(cnt.item()) == n_want
     assert torch.equal(vox, want[:small])
+    # A world in host memory is refused before any device work (the scratch
+    # belongs to the current device).
+    host_ids = wb.ids[1].cpu().numpy()
+    assert _call(host_ids.ctypes.data, host_ids.ctypes.data, W, H, D, origin, vox.data_ptr(), small, cnt.data_ptr(),
+                 hdr.data_ptr(), stream) == BLK_ERR_INVALID_ARGUMENT
+    assert "device memory" in N.last_error()
     wb.close()
