@@ -441,9 +441,11 @@ def surface_edits(rng, hm, envs, n, W, D, torch_xyz):
 
 def dirty_voxels(before, after, hm_before, hm_after, origin_y=0):
     """Voxels an exact relight must revisit, summed over envs: the union of the
-    L-inf radius-14 cubes (clipped to the world) around every cell whose light
-    class changed (opaque / open / torch) and around the column span its top
-    moved over. An opaque block replaced by another opaque block changes no
+    prisms (clipped to the world) of every cell whose light class changed
+    (opaque / open / torch) and of every cell of the column span its top moved
+    over; the prism of a cell is the columns within L1 distance 14 of its
+    column times the rows within 14 of it (light falls by one per step, so a
+    change reaches no farther). An opaque block replaced by another opaque block changes no
     light, and neither does an air <-> opaque change of a cell that lay below
     its column's top before and after the step and ends it enclosed (six
     opaque neighbours, no torch before or after). Also returns the number of
@@ -475,10 +477,12 @@ def dirty_voxels(before, after, hm_before, hm_after, origin_y=0):
         # the span of every moved top, in its column
         span = (y > torch.minimum(ta, tb)) & (y <= torch.maximum(ta, tb))
         seed = seed | span
-        # L-inf dilation by 14 of the seeds: a 29-wide max pool along each axis
-        dil = seed.to(torch.float16)
-        for k in ((29, 1, 1), (1, 29, 1), (1, 1, 29)):
-            dil = F.max_pool3d(dil, kernel_size=k, stride=1, padding=tuple(v // 2 for v in k))
+        # rows within 14 (a 29-wide max pool along y), then columns within L1
+        # distance 14 (14 steps of a cross-shaped dilation over z and x)
+        dil = F.max_pool3d(seed.to(torch.float16), kernel_size=(1, 1, 29), stride=1, padding=(0, 0, 14))
+        for _ in range(14):
+            dil = torch.maximum(F.max_pool3d(dil, kernel_size=(3, 1, 1), stride=1, padding=(1, 0, 0)),
+                                F.max_pool3d(dil, kernel_size=(1, 3, 1), stride=1, padding=(0, 1, 0)))
         total += int((dil > 0).sum().item())
     return total, n_changed, n_light
 

@@ -328,81 +328,123 @@ struct EditArgs {
     uint64_t env_stride;
 };
 
-// One thread per env: sort the env's edit indices (insertion sort restores
-// input order after the atomic scatter), then apply them sequentially with
-// World::setBlock semantics (src/world/World.cpp:239-287).
-__global__ void apply_edits_kernel(EditArgs a)
+constexpr int kEditWarps = 4; // envs per CTA of apply_edits_kernel (one warp each)
+
+// One warp per env: put the env's edit indices back in input order (the
+// scatter filed them in any order), then apply them with World::setBlock
+// semantics (src/world/World.cpp:239-287). An edit changes its own column
+// only (the cell, the torch it may knock off above it, the column's top), so
+// edits of different columns run side by side, 32 at a time; an edit waits
+// for the earlier edits of its column.
+__global__ void __launch_bounds__(32 * kEditWarps) apply_edits_kernel(EditArgs a)
 {
-    const uint32_t env = blockIdx.x * blockDim.x + threadIdx.x;
+    constexpr unsigned kFull = 0xFFFFFFFFu;
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    const uint32_t env = blockIdx.x * kEditWarps + (threadIdx.x >> 5);
     if (env >= a.r.num_envs)
-        return;
+        return; // the whole warp
     const uint32_t beg = a.env_offset[env], end = a.env_offset[env + 1];
-    for (uint32_t k = beg + 1; k < end; ++k) {
-        const uint32_t v = a.order[k];
-        uint32_t m = k;
-        while (m > beg && a.order[m - 1] > v) {
-            a.order[m] = a.order[m - 1];
-            --m;
+    if (end - beg <= 32) {
+        // Rank of each index among the env's (all distinct).
+        const uint32_t v = beg + lane < end ? a.order[beg + lane] : 0xFFFFFFFFu;
+        uint32_t rank = 0u;
+        for (uint32_t j = 0; j < end - beg; ++j)
+            rank += __shfl_sync(kFull, v, static_cast<int>(j)) < v ? 1u : 0u;
+        __syncwarp();
+        if (beg + lane < end)
+            a.order[beg + rank] = v;
+    } else if (lane == 0) {
+        for (uint32_t k = beg + 1; k < end; ++k) { // insertion sort (the scatter keeps most of the order)
+            const uint32_t v = a.order[k];
+            uint32_t m = k;
+            while (m > beg && a.order[m - 1] > v) {
+                a.order[m] = a.order[m - 1];
+                --m;
+            }
+            a.order[m] = v;
         }
-        a.order[m] = v;
     }
+    __syncwarp();
     uint8_t* ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
     int16_t* hm = a.hmap + static_cast<uint64_t>(env) * a.r.W * a.r.D;
     const int32_t H = a.r.H;
     const int4 org = a.r.origin[env];
-    for (uint32_t k = beg; k < end; ++k) {
-        a.changes[2 * static_cast<uint64_t>(k)].w = 0u;
-        a.changes[2 * static_cast<uint64_t>(k) + 1].w = 0u;
-        const blk_override e = a.edits[a.order[k]];
-        int32_t x = e.x - org.x, y = e.y - org.y, z = e.z - org.z;
-        uint8_t block = e.kind == 1 ? Air : e.block;
-        if (x < 0 || z < 0 || y < 0 || x >= a.r.W || z >= a.r.D || y >= H || block > Torch)
-            continue;
-        const uint64_t col = static_cast<uint64_t>(z) * a.r.W + x;
-        if (e.kind == 1 && ids[col * H + y] != Torch)
-            continue;
-        // setBlock, with the torch-support rule unrolled (the torch removal
-        // cannot cascade: Air is not solid).
-        for (int pass = 0; pass < 2; ++pass) {
-            uint8_t& cell = ids[col * H + y];
-            const uint8_t old = cell;
-            if (old == block)
-                break;
-            cell = block;
-            const int32_t old_top = hm[col] - org.y;
-            int32_t top = old_top;
-            if (is_opaque(block) && y > top)
-                top = y;
-            else if (!is_opaque(block) && is_opaque(old) && y == top) {
-                top = -1;
-                for (int32_t yy = y - 1; yy >= 0; --yy)
-                    if (is_opaque(ids[col * H + yy])) {
-                        top = yy;
+    for (uint32_t k0 = beg; k0 < end; k0 += 32) {
+        const uint32_t k = k0 + lane;
+        bool valid = false;
+        blk_override e {};
+        int32_t x = 0, y = 0, z = 0;
+        uint8_t block = Air;
+        uint64_t col = 0;
+        if (k < end) {
+            a.changes[2 * static_cast<uint64_t>(k)].w = 0u;
+            a.changes[2 * static_cast<uint64_t>(k) + 1].w = 0u;
+            e = a.edits[a.order[k]];
+            x = e.x - org.x;
+            y = e.y - org.y;
+            z = e.z - org.z;
+            block = e.kind == 1 ? Air : e.block;
+            valid = !(x < 0 || z < 0 || y < 0 || x >= a.r.W || z >= a.r.D || y >= H || block > Torch);
+            col = valid ? static_cast<uint64_t>(z) * a.r.W + x : 0;
+        }
+        // Lanes of one column go in lane order (= input order); distinct
+        // keys for lanes without an edit.
+        const uint64_t key = valid ? col : (0xFFFFFFFF00000000ull | static_cast<uint32_t>(lane));
+        const unsigned same = __match_any_sync(kFull, key);
+        unsigned pending = __ballot_sync(kFull, valid);
+        while (pending) { // warp-uniform
+            const bool ready = ((pending >> lane) & 1u) != 0u && (same & pending & lt) == 0u;
+            if (ready && !(e.kind == 1 && ids[col * H + y] != Torch)) {
+                // setBlock, with the torch-support rule unrolled (the torch
+                // removal cannot cascade: Air is not solid).
+                int32_t yc = y;
+                uint8_t bc = block;
+                for (int pass = 0; pass < 2; ++pass) {
+                    uint8_t& cell = ids[col * H + yc];
+                    const uint8_t old = cell;
+                    if (old == bc)
                         break;
+                    cell = bc;
+                    const int32_t old_top = hm[col] - org.y;
+                    int32_t top = old_top;
+                    if (is_opaque(bc) && yc > top)
+                        top = yc;
+                    else if (!is_opaque(bc) && is_opaque(old) && yc == top) {
+                        top = -1;
+                        for (int32_t yy = yc - 1; yy >= 0; --yy)
+                            if (is_opaque(ids[col * H + yy])) {
+                                top = yy;
+                                break;
+                            }
                     }
+                    hm[col] = static_cast<int16_t>(top + org.y);
+                    int32_t ylo = yc, yhi = yc;
+                    if (top != old_top) {
+                        ylo = min(ylo, min(top, old_top) + 1);
+                        yhi = max(yhi, max(top, old_top));
+                    }
+                    // Light depends on which cells are opaque and which are
+                    // torches only (the height map follows the opaque cells):
+                    // an opaque cell replaced by another opaque block changes no
+                    // light anywhere. Other changes are recorded, with the
+                    // column's top just before the change (w = 1 | (old_top + 2)
+                    // << 8), and marked for relight by mark_changes_kernel once
+                    // every env's last edit is in.
+                    if (!(is_opaque(old) && is_opaque(bc)))
+                        a.changes[2 * static_cast<uint64_t>(k) + pass] = make_uint4(
+                            static_cast<uint32_t>(x) | (static_cast<uint32_t>(z) << 16),
+                            static_cast<uint32_t>(yc) | (static_cast<uint32_t>(old) << 16) | (static_cast<uint32_t>(bc) << 24),
+                            static_cast<uint32_t>(max(ylo, 0)) | (static_cast<uint32_t>(min(yhi, H - 1)) << 16),
+                            1u | (static_cast<uint32_t>(old_top + 2) << 8));
+                    if (!(is_opaque(old) && !is_opaque(bc) && yc + 1 < H && ids[col * H + yc + 1] == Torch))
+                        break;
+                    yc = yc + 1;
+                    bc = Air;
+                }
             }
-            hm[col] = static_cast<int16_t>(top + org.y);
-            int32_t ylo = y, yhi = y;
-            if (top != old_top) {
-                ylo = min(ylo, min(top, old_top) + 1);
-                yhi = max(yhi, max(top, old_top));
-            }
-            // Light depends on which cells are opaque and which are torches
-            // only (the height map follows the opaque cells): an opaque cell
-            // replaced by another opaque block changes no light anywhere.
-            // Other changes are recorded, with the column's top just before
-            // the change (w = 1 | (old_top + 2) << 8), and marked for relight
-            // by mark_changes_kernel once every env's last edit is in.
-            if (!(is_opaque(old) && is_opaque(block)))
-                a.changes[2 * static_cast<uint64_t>(k) + pass] = make_uint4(
-                    static_cast<uint32_t>(x) | (static_cast<uint32_t>(z) << 16),
-                    static_cast<uint32_t>(y) | (static_cast<uint32_t>(old) << 16) | (static_cast<uint32_t>(block) << 24),
-                    static_cast<uint32_t>(max(ylo, 0)) | (static_cast<uint32_t>(min(yhi, H - 1)) << 16),
-                    1u | (static_cast<uint32_t>(old_top + 2) << 8));
-            if (!(is_opaque(old) && !is_opaque(block) && y + 1 < H && ids[col * H + y + 1] == Torch))
-                break;
-            y = y + 1;
-            block = Air;
+            __syncwarp(); // this round's column writes are seen by the next round
+            pending &= ~__ballot_sync(kFull, ready);
         }
     }
 }
@@ -929,9 +971,10 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
     ctx->box_capacity = 2 * std::max<uint32_t>(c.max_edits, 1);
-    ctx->region_capacity = ctx->box_capacity + static_cast<uint32_t>(std::min<uint64_t>(n_tiles, 1u << 24));
-    A(dalloc(&ctx->region_lists, 8ull * ctx->region_capacity, "relight region lists"));
-    A(dalloc(&ctx->region_counts, 4, "relight region counts"));
+    ctx->region_capacity = ctx->box_capacity; // every item holds a marked change
+    A(dalloc(&ctx->region_lists, 2ull * kRegionLists * ctx->region_capacity, "relight region lists"));
+    A(dalloc(&ctx->region_centres, ctx->region_capacity, "relight region centres"));
+    A(dalloc(&ctx->region_counts, kRegionLists + 1, "relight region counts"));
     A(dalloc(&ctx->render_params, envs, "render parameters"));
     A(dalloc(&ctx->col_summary, envs * ctx->columns_per_env, "column summaries"));
     A(dalloc(&ctx->env_mask, envs, "partial reset env mask"));
@@ -946,11 +989,11 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
         }
         ctx->park_ctas = static_cast<uint32_t>(sms);
         A(dalloc(&ctx->park, static_cast<size_t>(sms) * 16 * 1024, "tile scratch"));
-        A(dalloc(&ctx->region_park, 4ull * sms * region_park_words_per_sm(), "region relight scratch"));
+        A(dalloc(&ctx->region_park, static_cast<uint64_t>(kRegionLists) * sms * region_park_words_per_sm(), "region relight scratch"));
     }
     if (rc == BLK_OK) {
         bool ok = cudaEventCreateWithFlags(&ctx->relight_fork, cudaEventDisableTiming) == cudaSuccess;
-        for (int k = 0; k < 4 && ok; ++k)
+        for (int k = 0; k < kRegionLists && ok; ++k)
             ok = cudaStreamCreateWithFlags(&ctx->relight_streams[k], cudaStreamNonBlocking) == cudaSuccess
                 && cudaEventCreateWithFlags(&ctx->relight_join[k], cudaEventDisableTiming) == cudaSuccess;
         if (!ok) {
@@ -1005,7 +1048,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
     for (auto& m : ctx->marks)
         for (cudaEvent_t ev : m.e)
             cudaEventDestroy(ev);
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < kRegionLists; ++k) {
         if (ctx->relight_streams[k])
             cudaStreamDestroy(ctx->relight_streams[k]);
         if (ctx->relight_join[k])
@@ -1015,7 +1058,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
         cudaEventDestroy(ctx->relight_fork);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->origins, ctx->origin_stage, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order, ctx->edit_changes,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->region_lists, ctx->region_counts, ctx->region_park, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->region_lists, ctx->region_centres, ctx->region_counts, ctx->region_park, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -1220,7 +1263,7 @@ int blk_apply_edits(blk_ctx* ctx, const blk_override* edits, uint32_t n_edits, u
     a.hmap = ctx->hmap;
     a.r = region(ctx);
     a.env_stride = ctx->env_stride;
-    apply_edits_kernel<<<(envs + 127) / 128, 128, 0, st>>>(a);
+    apply_edits_kernel<<<(envs + kEditWarps - 1) / kEditWarps, 32 * kEditWarps, 0, st>>>(a);
     mark_changes_kernel<<<grid_for(2ull * n_edits, 256), 256, 0, st>>>(a);
     BLK_CUDA(cudaGetLastError(), "apply edits launch");
     prof_mark(ctx, mark, 1, st);
@@ -1542,6 +1585,8 @@ int blk_sync(blk_ctx* ctx, uintptr_t stream_handle)
             msg += " permutation guard hit";
         if (f & kFlagEnvIndex)
             msg += " partial reset env index out of range";
+        if (f & kFlagRelightRegion)
+            msg += " relight region larger than its size class";
         set_error(msg);
         return BLK_ERR_DEVICE_FLAG;
     }

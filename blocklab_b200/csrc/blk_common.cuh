@@ -22,6 +22,7 @@ enum : uint32_t {
     kFlagEditOverflow = 1u << 2,   // changed-cell list of an edit batch overflowed
     kFlagPermuteGuard = 1u << 3,   // permutation walk hit its iteration bound
     kFlagEnvIndex = 1u << 4,       // an env index of a partial reset is out of range
+    kFlagRelightRegion = 1u << 5,  // a relight region held more columns than its size class
 };
 
 // src/utility/Hash.h:10-24

@@ -11,6 +11,10 @@
 #include <string>
 #include <vector>
 
+// Size classes of the region relight kernels (blk_relight.cu): one item list,
+// side stream and scratch area each.
+constexpr int kRegionLists = 6;
+
 struct blk_ctx {
     int device = 0;
     blk_world_config cfg {};
@@ -51,13 +55,14 @@ struct blk_ctx {
     uint32_t* dirty_window = nullptr;     // [num_envs * tiles] packed ylo | yhi<<16, 0xFFFFFFFF = clean
     uint32_t* dirty_list = nullptr;       // [num_envs * tiles] dirty tile ids
     uint32_t* dirty_count = nullptr;      // [1]
-    uint4* region_lists = nullptr;        // [4][region_capacity][2] relight items by size class (see blk_relight.cu)
-    uint32_t region_capacity = 0;         // items per list
-    uint32_t* region_counts = nullptr;    // [4]
+    uint4* region_lists = nullptr;        // [kRegionLists][region_capacity][2] relight items by size class (see blk_relight.cu)
+    uint32_t region_capacity = 0;         // items per list, and footprint centres of all items
+    uint32_t* region_centres = nullptr;   // [region_capacity] footprint centres of the items (x | z << 16)
+    uint32_t* region_counts = nullptr;    // [kRegionLists + 1]: items per list, then centres used
     uint32_t* region_park = nullptr;      // region kernels' scratch: parked block counters per CTA, one area per list
-    cudaStream_t relight_streams[4] = {}; // side streams of the region kernels (forked from the caller's stream)
+    cudaStream_t relight_streams[kRegionLists] = {}; // side streams of the region kernels (forked from the caller's stream)
     cudaEvent_t relight_fork = nullptr;
-    cudaEvent_t relight_join[4] = {};
+    cudaEvent_t relight_join[kRegionLists] = {};
     uint32_t box_capacity = 0;            // 2 * max_edits (an edit changes at most two cells)
     uint32_t* h_dirty_count = nullptr;    // pinned [1]
 
@@ -85,9 +90,10 @@ struct RegionBuildArgs {
     const uint32_t* env_offset; // [num_envs + 1] edit positions per env
     uint32_t num_envs;
     int32_t W, H, D;
-    uint4* lists[4];            // relight item lists by size class, two uint4 per item
-    uint32_t* counts;           // [4]
-    uint32_t capacity;          // entries per list
+    uint4* lists[kRegionLists]; // relight item lists by size class, two uint4 per item
+    uint32_t* counts;           // [kRegionLists + 1]: items per list, then centres used
+    uint32_t capacity;          // entries per list, and of the centre array
+    uint32_t* centres;          // footprint centres of the items (x | z << 16)
     uint32_t* win_lo;           // tile path: per env tile dirty rows (atomicMin / atomicMax)
     uint32_t* win_hi;
     int32_t tiles_x, tiles_z;
@@ -105,12 +111,14 @@ struct RegionRelightArgs {
     const uint4* regions;       // this kernel's item list (two uint4 per item) and its count
     const uint32_t* count;
     uint32_t capacity;
+    const uint32_t* centres;    // footprint centres (x | z << 16) the items point into
     uint32_t* park;
+    uint32_t* flags;
 };
 
 uint64_t region_park_words_per_sm();
 int launch_region_build(blk_ctx* ctx, const RegionBuildArgs& a, cudaStream_t stream);
-int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[4]);
+int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[kRegionLists]);
 
 void set_error(const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);

@@ -1,54 +1,62 @@
 // Exact incremental relight after edits: the changed cells of an env are
-// grouped into regions (boxes of columns x rows) whose one-cell boundary ring
-// no edit of the step can have relit, and each region's light is recomputed
-// from its resident boundary.
+// grouped into regions whose one-cell boundary ring no edit of the step can
+// have relit, and each region's light is recomputed from its resident ring.
 //
 // Why a region with a clean ring is exact. Light is the unique solution of
 //     L(v) = opaque(v) ? 0 : max(src(v), max_{n in N6(v)} L(n) - 1, 0)
 // (src = 15 at torches for block light, at open cells above the column's top
-// for sky light; cells outside the world are opaque). Restricted to a box R,
-// the same equation with the values of the cells just outside R held fixed has
-// exactly one solution: a positive level needs a neighbour one higher, so it is
-// carried by a chain that ends at a source in R or at a fixed cell. The light
-// of the whole world restricted to R is such a solution, so solving the box
-// problem with the CORRECT boundary values gives the new light of R.
+// for sky light; cells outside the world are opaque). Restricted to a set R of
+// cells, the same equation with the values of the cells just outside R held
+// fixed has exactly one solution: a positive level needs a neighbour one
+// higher, so it is carried by a chain that ends at a source in R or at a fixed
+// cell. The light of the whole world restricted to R is such a solution, so
+// solving the region problem with the CORRECT ring values gives the new light
+// of R.
 //
-// A change can move light only within L-inf distance 14 of its cell or of the
-// column span its top moved over (the dirty cube of the change). Outside the
-// union of the step's dirty cubes the old light is the new light. So the
-// resident light of a cell outside every cube is its correct new value: a box
-// whose boundary ring avoids every cube can be solved from the resident ring.
-// The regions are built per env by merging dirty cubes: two regions whose
-// bounding boxes come within one cell of each other (one region's ring meets
-// the other region) are replaced by their common bounding box, until no two
-// regions touch. Every region's ring then lies outside every cube.
+// The dirty prism of a change. Light falls by one per step along 6-connected
+// paths, so a changed cell c (or a changed source: every cell of the span a
+// column's top moved over) can move the light of v only if |v - c|_1 <= 14.
+// That L1 ball lies inside the prism of the change: the columns within L1
+// distance 14 of its column (a diamond of at most 421 columns) times the rows
+// within 14 of its cell and moved span. Outside the union of the step's
+// prisms the old light is the new light.
+//
+// Regions. Per env the prisms are grouped: two groups join while some pair of
+// their columns lies within L1 distance 29 (their diamonds overlap or touch)
+// and their row hulls overlap or touch. A region is the union of its group's
+// diamonds times the group's row hull. Its ring: the columns at L1 distance
+// exactly 15 from the nearest centre (over the hull's rows; each is a
+// 4-neighbour of a diamond column), and the rows just below and above the
+// hull in the region's columns. The ring avoids every prism: its columns lie
+// beyond reach of the group's own centres; a prism of another group reaching a
+// ring column would have a centre within 29 of this group's and rows inside
+// this hull, and one reaching a ring row would have its rows touching this
+// hull, and either would have joined the groups.
 //
 // Solving a region: with S_k = {v : L(v) >= k}, a fixed cell of level l joins
 // the level sets at S_l and stays, a source joins at S_15, and
 //     S_k = S_{k+1} | fixed_k | (open & dilate6(S_{k+1}))       k = 14 .. 1,
-// one bit per cell, 32 rows of a column per word (as in the tile kernel).
-// Fixed cells are the region's ring: the ring columns around it (every row of
-// the region) and the rows just below and above the region in each of its
-// columns. A region needs only its own columns and no halo: about 29 x 29
-// columns and one word for a single change, instead of a 60 x 60-column tile
-// with a 14-column halo.
-//
-// A region of more than 4096 columns or 64 a side is split into sub-boxes of
-// 32 x 32 columns, each solved over itself and the region's columns within 14
-// of it
-// (light from farther away cannot reach it). Regions of more than 62 rows are
-// relit by the tile kernel's halo path over the tiles they cover. Every path
-// writes only correct new values, and a region's ring cells are never changed
-// by any, so they may run side by side.
+// one bit per cell, 32 rows of a column per word (as in the tile kernel). The
+// region's columns and ring columns are compacted into slots (a column's four
+// horizontal neighbours are slot indices), so a CTA works on the diamonds'
+// columns only: 421 for a single change instead of a 29 x 29 box (841).
+// Regions of more than 62 rows, or beyond the largest size class, are relit by
+// the tile kernel's halo path over the tiles they cover (it reads no resident
+// light). Every path writes only correct new values, and a region's ring cells
+// are never changed by any, so they may run side by side.
 #include "blk_bits.cuh"
 #include "blk_internal.h"
+
+#include <climits>
 
 namespace blk {
 namespace {
 
-constexpr int kMaxRegionsPerEnv = 32; // more disjoint regions in one env: its bounding box goes to the tile path
-constexpr int kRegionLists = 4;       // size classes, see launch_region_relight
-constexpr int kMaxSide = 64;          // region columns along x or z in one item
+constexpr int kMaxPrisms = 64;                // separate prisms of one env; more: the env's hull goes to the tile path
+constexpr int kMaxCentres = 32;               // diamond centres of one region; more: the tile path
+constexpr int kBuildWarps = 4;                // envs per CTA of region_build_kernel (one warp each)
+constexpr int kReach = 2 * kMaxDistance + 1;  // centres this close (L1) have overlapping or touching diamonds
+constexpr int kBuildGuard = 4 * kMaxPrisms;   // grouping passes before an env falls back to the tile path
 
 // Low bit of each byte -> 4 packed bits.
 __device__ inline uint32_t pack4_lo(uint32_t m) { return ((m & 0x01010101u) * 0x10204080u) >> 28; }
@@ -57,123 +65,313 @@ struct Box {
     int32_t x0, x1, z0, z1, y0, y1; // inclusive
 };
 
-__device__ inline bool touches(const Box& a, const Box& b)
-{
-    return a.x0 - 1 <= b.x1 && b.x0 <= a.x1 + 1 && a.z0 - 1 <= b.z1 && b.z0 <= a.z1 + 1 && a.y0 - 1 <= b.y1
-        && b.y0 <= a.y1 + 1;
-}
-
 __device__ inline Box hull(const Box& a, const Box& b)
 {
     return Box { min(a.x0, b.x0), max(a.x1, b.x1), min(a.z0, b.z0), max(a.z1, b.z1), min(a.y0, b.y0),
         max(a.y1, b.y1) };
 }
 
-// One thread per env: merges the env's dirty cubes (the change records that
-// mark_changes_kernel marked) into regions and files each region by size
-// (region lists), or, when it exceeds the region kernels' limits, widens the
-// dirty row windows of the tiles it covers (tile path).
-__global__ void region_build_kernel(RegionBuildArgs a)
+// Per-class limits of the region kernels. A CTA of THREADS threads owns two
+// solved columns per thread (slot d = tid + k * THREADS) and one ring column
+// (slot kMaxCols + r); NB words of 32 rows per column.
+template <int THREADS, int NB>
+struct RegionClass {
+    static constexpr int kCpt = 2;
+    static constexpr int kMaxCols = THREADS * kCpt;        // solved columns
+    static constexpr int kRing = THREADS;                  // ring columns
+    static constexpr int kZero = kMaxCols + kRing;         // slot that stays empty: neighbours outside the world
+    static constexpr int kExt = (kZero + 1 + 3) & ~3;      // slots per plane
+    static constexpr int kMapCells = 6 * NB * kExt;        // grid cells the setup map can hold (16 bits each)
+    static constexpr int kCtasPerSm = THREADS <= 256 ? 4 : (THREADS <= 512 ? 2 : 1);
+    static constexpr int kParkWords = kMaxCols * NB * 4;   // parked block counters per CTA
+};
+
+template <int THREADS, int NB>
+struct RegionSmem {
+    using K = RegionClass<THREADS, NB>;
+    uint32_t planes[3][NB][K::kExt];  // open cells (0) and level set S ping-pong (1, 2; 2 holds torch bits
+                                      // before a block flood); during setup the grid map (slot per grid cell)
+    uint32_t ring[8][NB][K::kRing];   // level planes of the ring columns: block 0..3, sky 4..7
+    uint2 nbr[K::kMaxCols];           // slots of each solved column's neighbours: x-1 | x+1 << 16, z-1 | z+1 << 16
+    uint16_t pos[K::kMaxCols + K::kRing]; // grid cell of each solved and ring slot
+    int16_t top[K::kMaxCols];         // local y of each solved column's highest opaque cell
+    uint32_t cen[kMaxCentres];        // the region's diamond centres, x | z << 16
+    uint32_t n_act, n_ring;
+};
+
+template <int THREADS, int NB>
+__host__ __device__ constexpr bool class_fits(uint32_t cols, uint32_t ring, int64_t cells)
 {
-    const uint32_t env = blockIdx.x * blockDim.x + threadIdx.x;
-    if (env >= a.num_envs)
-        return;
-    Box reg[kMaxRegionsPerEnv];
-    int n = 0;
-    bool overflow = false;
-    const uint64_t beg = 2ull * a.env_offset[env], end = 2ull * a.env_offset[env + 1];
-    for (uint64_t i = beg; i < end; ++i) {
-        const uint4 c = a.changes[i];
-        if ((c.w & 3u) != 3u) // recorded and marked for relight
-            continue;
-        const int32_t x = static_cast<int32_t>(c.x & 0xFFFFu), z = static_cast<int32_t>(c.x >> 16);
-        const int32_t ylo = static_cast<int32_t>(c.z & 0xFFFFu), yhi = static_cast<int32_t>(c.z >> 16);
-        Box b { max(x - kMaxDistance, 0), min(x + kMaxDistance, a.W - 1), max(z - kMaxDistance, 0),
-            min(z + kMaxDistance, a.D - 1), max(ylo - kMaxDistance, 0), min(yhi + kMaxDistance, a.H - 1) };
-        if (overflow) {
-            reg[0] = hull(reg[0], b);
-            continue;
-        }
-        // Absorb every region the growing box touches; the others are
-        // pairwise apart already.
-        for (bool merged = true; merged;) {
-            merged = false;
-            for (int j = 0; j < n; ++j)
-                if (touches(b, reg[j])) {
-                    b = hull(b, reg[j]);
-                    reg[j] = reg[--n];
-                    merged = true;
-                    break;
-                }
-        }
-        if (n == kMaxRegionsPerEnv) {
-            for (int j = 1; j < n; ++j)
-                b = hull(b, reg[j]);
-            reg[0] = hull(b, reg[0]);
-            n = 1;
-            overflow = true;
-        } else {
-            reg[n++] = b;
-        }
+    using K = RegionClass<THREADS, NB>;
+    return cols <= static_cast<uint32_t>(K::kMaxCols) && ring <= static_cast<uint32_t>(K::kRing)
+        && cells <= K::kMapCells;
+}
+
+// Item list of a region with the given words, solved and ring columns and
+// grid cells: 2 s + nb - 1 for the size class of 256 << s threads; -1 when
+// none fits (tile path).
+__device__ inline int region_list_for(int nb, uint32_t cols, uint32_t ring, int64_t cells)
+{
+    if (nb == 1) {
+        if (class_fits<256, 1>(cols, ring, cells))
+            return 0;
+        if (class_fits<512, 1>(cols, ring, cells))
+            return 2;
+        if (class_fits<1024, 1>(cols, ring, cells))
+            return 4;
+    } else {
+        if (class_fits<256, 2>(cols, ring, cells))
+            return 1;
+        if (class_fits<512, 2>(cols, ring, cells))
+            return 3;
+        if (class_fits<1024, 2>(cols, ring, cells))
+            return 5;
     }
-    // Files one item: solve the columns of box e (sides fixed by the resident
-    // ring where `sides` says so), write those of box w; into the tile path
-    // when the lists are full.
-    auto emit = [&](int list, const Box& e, const Box& w, uint32_t sides) {
-        const uint32_t k = atomicAdd(a.counts + list, 1u);
-        if (k < a.capacity) {
-            uint4* it = a.lists[list] + 2ull * k;
-            it[0] = make_uint4(env, static_cast<uint32_t>(e.x0) | (static_cast<uint32_t>(e.z0) << 16),
-                static_cast<uint32_t>(e.x1 - e.x0 + 1) | (static_cast<uint32_t>(e.z1 - e.z0 + 1) << 16),
-                static_cast<uint32_t>(e.y0) | (static_cast<uint32_t>(e.y1 - e.y0 + 1) << 16));
-            it[1] = make_uint4(static_cast<uint32_t>(w.x0) | (static_cast<uint32_t>(w.z0) << 16),
-                static_cast<uint32_t>(w.x1 - w.x0 + 1) | (static_cast<uint32_t>(w.z1 - w.z0 + 1) << 16), sides, 0u);
-            return;
+    return -1;
+}
+
+// Columns q .. q + 31 of world row z that lie within L1 distance r of one of
+// the centres, as bits.
+__device__ inline uint32_t diamond_row_bits(const uint32_t* cen, int nc, int32_t r, int32_t z, int32_t q)
+{
+    uint32_t m = 0u;
+    for (int i = 0; i < nc; ++i) {
+        const int32_t cx = static_cast<int32_t>(cen[i] & 0xFFFFu), cz = static_cast<int32_t>(cen[i] >> 16);
+        const int32_t h = r - abs(z - cz);
+        if (h < 0)
+            continue;
+        const int32_t lo = max(cx - h, q) - q, hi = min(cx + h, q + 31) - q;
+        if (lo > hi)
+            continue;
+        m |= (hi == 31 ? 0xFFFFFFFFu : ((2u << hi) - 1u)) & ~((1u << lo) - 1u);
+    }
+    return m;
+}
+
+// Tile path: widens the dirty row windows of the tiles box b covers.
+__device__ inline void stamp_tiles(const RegionBuildArgs& a, uint32_t env, const Box& b)
+{
+    for (int32_t tz = b.z0 / 32; tz <= b.z1 / 32; ++tz)
+        for (int32_t tx = b.x0 / 32; tx <= b.x1 / 32; ++tx) {
+            const uint64_t t = static_cast<uint64_t>(env) * a.tiles_x * a.tiles_z
+                + static_cast<uint64_t>(tz) * a.tiles_x + tx;
+            atomicMin(a.win_lo + t, static_cast<uint32_t>(b.y0));
+            atomicMax(a.win_hi + t, static_cast<uint32_t>(b.y1));
         }
-        for (int32_t tz = w.z0 / 32; tz <= w.z1 / 32; ++tz)
-            for (int32_t tx = w.x0 / 32; tx <= w.x1 / 32; ++tx) {
-                const uint64_t t = static_cast<uint64_t>(env) * a.tiles_x * a.tiles_z
-                    + static_cast<uint64_t>(tz) * a.tiles_x + tx;
-                atomicMin(a.win_lo + t, static_cast<uint32_t>(w.y0));
-                atomicMax(a.win_hi + t, static_cast<uint32_t>(w.y1));
+}
+
+struct BuildWarp {
+    uint32_t xz[kMaxPrisms];          // prism column x | z << 16
+    int32_t y0[kMaxPrisms], y1[kMaxPrisms]; // prism rows (inclusive)
+    int32_t lab[kMaxPrisms];          // group label: the smallest prism index of the group
+    int32_t hy0[kMaxPrisms], hy1[kMaxPrisms]; // row hull per label
+    uint32_t cen[kMaxCentres];        // centres of the group being filed
+};
+
+// One warp per env: the env's marked change records become prisms, the
+// prisms are grouped into regions (label propagation until no two groups
+// touch), and each region is filed by size (region lists) with its diamond
+// centres, or, beyond the region kernels' limits, widens the dirty row windows
+// of the tiles it covers (tile path).
+__global__ void __launch_bounds__(32 * kBuildWarps) region_build_kernel(RegionBuildArgs a)
+{
+    __shared__ BuildWarp sw[kBuildWarps];
+    const int lane = threadIdx.x & 31;
+    BuildWarp& w = sw[threadIdx.x >> 5];
+    const uint32_t env = blockIdx.x * kBuildWarps + (threadIdx.x >> 5);
+    if (env >= a.num_envs)
+        return; // the whole warp
+    constexpr unsigned kFull = 0xFFFFFFFFu;
+    const unsigned lt = (1u << lane) - 1u;
+    const uint64_t beg = 2ull * a.env_offset[env], end = 2ull * a.env_offset[env + 1];
+
+    // ---- prisms: one per changed column and row span --------------------------
+    int n = 0; // prisms filed (warp-uniform; may exceed kMaxPrisms)
+    Box hb { INT_MAX, INT_MIN, INT_MAX, INT_MIN, INT_MAX, INT_MIN }; // this lane's prisms' cubes (tile path)
+    for (uint64_t base = beg; base < end; base += 32) {
+        const uint64_t i = base + lane;
+        bool mk = false;
+        uint32_t xz = 0u;
+        int32_t y0 = 0, y1 = 0;
+        if (i < end) {
+            const uint4 c = a.changes[i];
+            if ((c.w & 3u) == 3u) { // recorded and marked for relight
+                mk = true;
+                xz = c.x;
+                const int32_t x = static_cast<int32_t>(xz & 0xFFFFu), z = static_cast<int32_t>(xz >> 16);
+                y0 = max(static_cast<int32_t>(c.z & 0xFFFFu) - kMaxDistance, 0);
+                y1 = min(static_cast<int32_t>(c.z >> 16) + kMaxDistance, a.H - 1);
+                hb = hull(hb, Box { max(x - kMaxDistance, 0), min(x + kMaxDistance, a.W - 1),
+                                   max(z - kMaxDistance, 0), min(z + kMaxDistance, a.D - 1), y0, y1 });
+                // A filed prism of the same column whose rows touch: widen it.
+                for (int j = 0; j < min(n, kMaxPrisms) && mk; ++j)
+                    if (w.xz[j] == xz && w.y0[j] - 1 <= y1 && y0 <= w.y1[j] + 1) {
+                        atomicMin(&w.y0[j], y0);
+                        atomicMax(&w.y1[j], y1);
+                        mk = false;
+                    }
             }
-    };
-    for (int j = 0; j < n; ++j) {
-        const Box& b = reg[j];
-        const int32_t nx = b.x1 - b.x0 + 1, nz = b.z1 - b.z0 + 1, ny = b.y1 - b.y0 + 1;
-        const int32_t span = ny + 2;                // the region's rows and its two ring rows
-        const int nb = span <= 32 ? 1 : (span <= 64 ? 2 : 0);
-        if (nb == 0) {                              // taller than the region kernels' words: tile path
-            for (int32_t tz = b.z0 / 32; tz <= b.z1 / 32; ++tz)
-                for (int32_t tx = b.x0 / 32; tx <= b.x1 / 32; ++tx) {
-                    const uint64_t t = static_cast<uint64_t>(env) * a.tiles_x * a.tiles_z
-                        + static_cast<uint64_t>(tz) * a.tiles_x + tx;
-                    atomicMin(a.win_lo + t, static_cast<uint32_t>(b.y0));
-                    atomicMax(a.win_hi + t, static_cast<uint32_t>(b.y1));
+        }
+        const unsigned m = __ballot_sync(kFull, mk);
+        if (mk) {
+            const int k = n + __popc(m & lt);
+            if (k < kMaxPrisms) {
+                w.xz[k] = xz;
+                w.y0[k] = y0;
+                w.y1[k] = y1;
+            }
+        }
+        n += __popc(m);
+        __syncwarp();
+    }
+    bool overflow = n > kMaxPrisms;
+
+    // ---- groups: label propagation over touching prisms ------------------------
+    if (!overflow) {
+        for (int i = lane; i < n; i += 32)
+            w.lab[i] = i;
+        __syncwarp();
+        bool converged = n == 0;
+        for (int it = 0; it < kBuildGuard && !converged; ++it) {
+            for (int i = lane; i < n; i += 32) {
+                w.hy0[i] = INT_MAX;
+                w.hy1[i] = INT_MIN;
+            }
+            __syncwarp();
+            for (int i = lane; i < n; i += 32) {
+                atomicMin(&w.hy0[w.lab[i]], w.y0[i]);
+                atomicMax(&w.hy1[w.lab[i]], w.y1[i]);
+            }
+            __syncwarp();
+            int nl[2];
+            bool changed = false;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int i = lane + 32 * t;
+                nl[t] = -1;
+                if (i >= n)
+                    continue;
+                const int li = w.lab[i];
+                int best = li;
+                const int32_t xi = static_cast<int32_t>(w.xz[i] & 0xFFFFu), zi = static_cast<int32_t>(w.xz[i] >> 16);
+                const int32_t g0 = w.hy0[li], g1 = w.hy1[li];
+                for (int j = 0; j < n; ++j) {
+                    const int lj = w.lab[j];
+                    if (lj >= best)
+                        continue;
+                    const int32_t d = abs(static_cast<int32_t>(w.xz[j] & 0xFFFFu) - xi)
+                        + abs(static_cast<int32_t>(w.xz[j] >> 16) - zi);
+                    if (d <= kReach && g0 - 1 <= w.hy1[lj] && w.hy0[lj] <= g1 + 1)
+                        best = lj;
                 }
-            continue;
-        }
-        const int64_t cols = static_cast<int64_t>(nx) * nz;
-        const int64_t big = 4096;                   // columns of the larger classes
-        if (nx <= kMaxSide && nz <= kMaxSide && cols <= big) {
-            emit((cols <= 1024 ? 0 : 2) + nb - 1, b, b, 0xFu);
-            continue;
-        }
-        // Larger: sub-boxes of 32 x 32 columns, each solved over itself and the
-        // region's columns within 14 of it. A side of that box inside the
-        // region lies 15 columns from the sub-box, beyond the reach of light,
-        // so it holds nothing; a side on the region's ring is held at the
-        // resident light.
-        const int32_t sub_x = 32;
-        for (int32_t sz = b.z0; sz <= b.z1; sz += 32)
-            for (int32_t sx = b.x0; sx <= b.x1; sx += sub_x) {
-                const Box w { sx, min(sx + sub_x - 1, b.x1), sz, min(sz + 31, b.z1), b.y0, b.y1 };
-                const Box e { max(w.x0 - kMaxDistance, b.x0), min(w.x1 + kMaxDistance, b.x1),
-                    max(w.z0 - kMaxDistance, b.z0), min(w.z1 + kMaxDistance, b.z1), b.y0, b.y1 };
-                const uint32_t sides = (e.x0 == b.x0 ? 1u : 0u) | (e.x1 == b.x1 ? 2u : 0u)
-                    | (e.z0 == b.z0 ? 4u : 0u) | (e.z1 == b.z1 ? 8u : 0u);
-                emit(2 + nb - 1, e, w, sides);
+                nl[t] = best;
+                changed |= best != li;
             }
+            __syncwarp();
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+                if (nl[t] >= 0)
+                    w.lab[lane + 32 * t] = nl[t];
+            __syncwarp();
+            converged = !__any_sync(kFull, changed);
+        }
+        overflow = !converged;
+    }
+    if (overflow) {
+        // The env's hull goes to the tile path.
+        const Box b { __reduce_min_sync(kFull, hb.x0), __reduce_max_sync(kFull, hb.x1),
+            __reduce_min_sync(kFull, hb.z0), __reduce_max_sync(kFull, hb.z1), __reduce_min_sync(kFull, hb.y0),
+            __reduce_max_sync(kFull, hb.y1) };
+        if (lane == 0 && b.x0 <= b.x1)
+            stamp_tiles(a, env, b);
+        return;
+    }
+
+    // ---- file each group: the warp together, one group at a time -------------
+    for (int r = 0; r < n; ++r) {
+        if (w.lab[r] != r) // warp-uniform
+            continue;
+        // Distinct centres (in prism order) and the footprint's bounding box.
+        int nc = 0;
+        int32_t cx0 = INT_MAX, cx1 = INT_MIN, cz0 = INT_MAX, cz1 = INT_MIN;
+        for (int j0 = 0; j0 < n; j0 += 32) {
+            const int j = j0 + lane;
+            bool keep = false;
+            if (j < n && w.lab[j] == r) {
+                const uint32_t xz = w.xz[j];
+                const int32_t x = static_cast<int32_t>(xz & 0xFFFFu), z = static_cast<int32_t>(xz >> 16);
+                cx0 = min(cx0, x);
+                cx1 = max(cx1, x);
+                cz0 = min(cz0, z);
+                cz1 = max(cz1, z);
+                keep = true;
+                for (int q = 0; q < j && keep; ++q)
+                    keep = !(w.lab[q] == r && w.xz[q] == xz);
+            }
+            const unsigned m = __ballot_sync(kFull, keep);
+            if (keep) {
+                const int k = nc + __popc(m & lt);
+                if (k < kMaxCentres)
+                    w.cen[k] = w.xz[j];
+            }
+            nc += __popc(m);
+        }
+        const bool many = nc > kMaxCentres;
+        nc = min(nc, kMaxCentres);
+        cx0 = __reduce_min_sync(kFull, cx0);
+        cx1 = __reduce_max_sync(kFull, cx1);
+        cz0 = __reduce_min_sync(kFull, cz0);
+        cz1 = __reduce_max_sync(kFull, cz1);
+        __syncwarp();
+        const Box b { max(cx0 - kMaxDistance, 0), min(cx1 + kMaxDistance, a.W - 1), max(cz0 - kMaxDistance, 0),
+            min(cz1 + kMaxDistance, a.D - 1), w.hy0[r], w.hy1[r] };
+        const int32_t span = b.y1 - b.y0 + 3; // the region's rows and its two ring rows
+        const int nb = span <= 32 ? 1 : (span <= 64 ? 2 : 0);
+        int list = -1;
+        if (nb != 0 && !many) {
+            // Solved and ring columns over the box and its one-column margin,
+            // exactly as the region kernel classifies them; a lane per row.
+            const int32_t gx0 = max(b.x0 - 1, 0), gx1 = min(b.x1 + 1, a.W - 1);
+            uint32_t n_act = 0u, n_ring = 0u;
+            for (int32_t z = max(b.z0 - 1, 0) + lane; z <= min(b.z1 + 1, a.D - 1); z += 32)
+                for (int32_t q = gx0; q <= gx1; q += 32) {
+                    const int32_t qe = min(q + 31, gx1);
+                    const uint32_t valid = qe - q == 31 ? 0xFFFFFFFFu : ((2u << (qe - q)) - 1u);
+                    const uint32_t m14 = diamond_row_bits(w.cen, nc, kMaxDistance, z, q) & valid;
+                    const uint32_t m15 = diamond_row_bits(w.cen, nc, kMaxDistance + 1, z, q) & valid;
+                    n_act += __popc(m14);
+                    n_ring += __popc(m15 & ~m14);
+                }
+            n_act = __reduce_add_sync(kFull, n_act);
+            n_ring = __reduce_add_sync(kFull, n_ring);
+            const int64_t cells = static_cast<int64_t>(b.x1 - b.x0 + 3) * (b.z1 - b.z0 + 3);
+            list = region_list_for(nb, n_act, n_ring, cells);
+            if (list >= 0) {
+                uint32_t k = 0u, co = 0u;
+                if (lane == 0) {
+                    k = atomicAdd(a.counts + list, 1u);
+                    co = atomicAdd(a.counts + kRegionLists, static_cast<uint32_t>(nc));
+                }
+                k = __shfl_sync(kFull, k, 0);
+                co = __shfl_sync(kFull, co, 0);
+                if (k < a.capacity && co <= a.capacity && static_cast<uint32_t>(nc) <= a.capacity - co) {
+                    if (lane < nc)
+                        a.centres[co + lane] = w.cen[lane];
+                    if (lane == 0) {
+                        uint4* it = a.lists[list] + 2ull * k;
+                        it[0] = make_uint4(env, static_cast<uint32_t>(b.x0) | (static_cast<uint32_t>(b.z0) << 16),
+                            static_cast<uint32_t>(b.x1 - b.x0 + 1) | (static_cast<uint32_t>(b.z1 - b.z0 + 1) << 16),
+                            static_cast<uint32_t>(b.y0) | (static_cast<uint32_t>(b.y1 - b.y0 + 1) << 16));
+                        it[1] = make_uint4(co, static_cast<uint32_t>(nc), n_act | (n_ring << 16), 0u);
+                    }
+                } else {
+                    list = -1;
+                }
+            }
+        }
+        if (list < 0 && lane == 0)
+            stamp_tiles(a, env, b);
+        __syncwarp(); // the centre array is reused by the next group
     }
 }
 
@@ -198,27 +396,6 @@ __device__ inline uint32_t window32(uint32_t m0, uint32_t m1, uint32_t m2, int o
     return static_cast<uint32_t>(v >> off);
 }
 
-// Per-class limits of the region kernels. A CTA of THREADS threads owns CPT
-// columns of the solved box per thread (column d = tid + k * THREADS); NB
-// words of 32 rows per column.
-template <int THREADS, int CPT, int NB>
-struct RegionClass {
-    static constexpr int kMaxCols = THREADS * CPT;           // columns of the solved box
-    static constexpr int kRing = 4 * kMaxSide;               // ring columns (corners neighbour no solved cell)
-    static constexpr int kMaxExt = kMaxCols + kRing + 4;     // with the ring
-    static constexpr int kCtasPerSm = CPT == 1 ? 2048 / THREADS : (THREADS <= 256 ? 4 : (THREADS <= 512 ? 2 : 1));
-    static constexpr int kParkWords = THREADS * CPT * NB * 4; // parked block counters per CTA
-};
-
-template <int THREADS, int CPT, int NB>
-struct RegionSmem {
-    using K = RegionClass<THREADS, CPT, NB>;
-    uint32_t open[NB][K::kMaxExt];  // open cells of the solved rows (solved columns)
-    uint32_t set[2][NB][K::kMaxExt];// level set S, ping-pong (set[1] holds torch bits before a block flood)
-    uint32_t ring[8][NB][K::kRing]; // level planes of the ring columns: block 0..3, sky 4..7
-    int16_t top[K::kMaxExt];        // local y of each solved column's highest opaque cell
-};
-
 // Cells of level >= L among 32 rows given as level bit planes p[0..3].
 __device__ inline uint32_t at_least(int L, const uint32_t (&p)[4])
 {
@@ -232,37 +409,45 @@ __device__ inline uint32_t at_least(int L, const uint32_t (&p)[4])
     return ge | eq;
 }
 
-// The region kernels: a CTA solves one region at a time (persistent over its
-// list). NB words of 32 rows from row wb = y0 - 1 hold the region's rows
-// (bits 1 .. ny) and its two ring rows (bits 0 and ny + 1). Threads below the
-// ring length also own one ring column. The ext column pitch is nx + 2.
-template <int THREADS, int CPT, int NB>
-__global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasPerSm)
+// The region kernels: a CTA solves one region at a time, persistent over its
+// list. NB words of 32 rows from row wb = y0 - 1 hold the region's rows (bits
+// 1 .. ny) and its two ring rows (bits 0 and ny + 1). Setup classifies the
+// cells of the region's bounding box and its one-column margin (the grid,
+// pitch nx + 2) by L1 distance to the nearest centre, compacts the solved
+// (<= 14) and ring (== 15) columns into slots and records each solved column's
+// neighbour slots.
+template <int THREADS, int NB>
+__global__ void __launch_bounds__(THREADS, RegionClass<THREADS, NB>::kCtasPerSm)
     relight_region_kernel(RegionRelightArgs a)
 {
-    using K = RegionClass<THREADS, CPT, NB>;
-    using Sm = RegionSmem<THREADS, CPT, NB>;
+    using K = RegionClass<THREADS, NB>;
+    using Sm = RegionSmem<THREADS, NB>;
+    constexpr int CPT = K::kCpt;
     static_assert(K::kRing <= THREADS, "one ring column per thread");
+    static_assert(K::kZero < 0xFFFF, "slots fit 16 bits");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Sm& s = *reinterpret_cast<Sm*>(smem_raw);
-    const int tid = threadIdx.x;
+    uint16_t* map = reinterpret_cast<uint16_t*>(&s.planes[0][0][0]);
+    const int tid = threadIdx.x, lane = tid & 31;
     const uint32_t count = min(*a.count, a.capacity);
     uint32_t* park = a.park + static_cast<uint64_t>(blockIdx.x) * K::kParkWords;
 
     for (uint32_t item = blockIdx.x; item < count; item += gridDim.x) {
         const uint4 rec = a.regions[2ull * item];
-        const uint4 wrt = a.regions[2ull * item + 1];
+        const uint4 inf = a.regions[2ull * item + 1];
         const uint32_t env = rec.x;
-        // Columns written (a sub-box of the solved box for a split region),
-        // and which sides of the solved box are held at the resident ring.
-        const int32_t wx0 = static_cast<int32_t>(wrt.x & 0xFFFFu), wz0 = static_cast<int32_t>(wrt.x >> 16);
-        const int32_t wnx = static_cast<int32_t>(wrt.y & 0xFFFFu), wnz = static_cast<int32_t>(wrt.y >> 16);
-        const uint32_t sides = wrt.z;
         const int32_t x0 = static_cast<int32_t>(rec.y & 0xFFFFu), z0 = static_cast<int32_t>(rec.y >> 16);
         const int32_t nx = static_cast<int32_t>(rec.z & 0xFFFFu), nz = static_cast<int32_t>(rec.z >> 16);
         const int32_t y0 = static_cast<int32_t>(rec.w & 0xFFFFu), ny = static_cast<int32_t>(rec.w >> 16);
+        const int nc = min(static_cast<int>(inf.y), kMaxCentres);
         const int32_t H = a.H;
-        const int P = nx + 2;                 // ext pitch
+        const int P = nx + 2;                 // grid pitch
+        const int G = P * (nz + 2);           // grid cells
+        if (G > K::kMapCells || nx < 1 || nz < 1) { // the build files no such region
+            if (tid == 0)
+                atomicOr(a.flags, kFlagRelightRegion);
+            continue;
+        }
         const int32_t wb = y0 - 1;            // row of bit 0 of word 0 (the lower ring row)
         const int32_t cs = wb & ~15;          // first 16-row chunk of the words' rows
         const int off = wb - cs;              // 0 .. 15
@@ -279,21 +464,90 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
             dom[w] = lo > hi ? 0u : ((hi == 31 ? 0xFFFFFFFFu : ((1u << (hi + 1)) - 1u)) & ~((1u << lo) - 1u));
         }
 
-        // ---- own region columns: open and torch bits, top, ring-row levels ----
-        // Per own column: ext index (low 16 bits, 0xFFFF = none) and the levels
-        // of its ring rows (high 16 bits: block lo | block hi << 4 | sky lo << 8
-        // | sky hi << 12).
+        // ---- grid: solved and ring columns, compacted into slots ---------------
+        if (tid < nc)
+            s.cen[tid] = __ldg(a.centres + inf.x + tid);
+        if (tid == 0) {
+            s.n_act = 0u;
+            s.n_ring = 0u;
+        }
+        __syncthreads();
+        for (int g0 = 0; g0 < G; g0 += THREADS) { // warp-uniform trip count (ballots)
+            const int g = g0 + tid;
+            int kind = 0; // 1 solved, 2 ring
+            if (g < G) {
+                const int32_t x = x0 - 1 + g % P, z = z0 - 1 + g / P;
+                if (x >= 0 && z >= 0 && x < a.W && z < a.D) {
+                    int32_t m = INT_MAX;
+                    for (int i = 0; i < nc; ++i) {
+                        const uint32_t c = s.cen[i];
+                        m = min(m, abs(x - static_cast<int32_t>(c & 0xFFFFu)) + abs(z - static_cast<int32_t>(c >> 16)));
+                    }
+                    kind = m <= kMaxDistance ? 1 : (m == kMaxDistance + 1 ? 2 : 0);
+                }
+            }
+            const unsigned ma = __ballot_sync(0xFFFFFFFFu, kind == 1), mr = __ballot_sync(0xFFFFFFFFu, kind == 2);
+            uint32_t base_a = 0u, base_r = 0u;
+            if (lane == 0) {
+                if (ma)
+                    base_a = atomicAdd(&s.n_act, static_cast<uint32_t>(__popc(ma)));
+                if (mr)
+                    base_r = atomicAdd(&s.n_ring, static_cast<uint32_t>(__popc(mr)));
+            }
+            base_a = __shfl_sync(0xFFFFFFFFu, base_a, 0);
+            base_r = __shfl_sync(0xFFFFFFFFu, base_r, 0);
+            const unsigned lt = (1u << lane) - 1u;
+            if (g < G) {
+                uint16_t v = static_cast<uint16_t>(K::kZero);
+                if (kind == 1) {
+                    const uint32_t d = base_a + __popc(ma & lt);
+                    if (d < static_cast<uint32_t>(K::kMaxCols)) {
+                        v = static_cast<uint16_t>(d);
+                        s.pos[d] = static_cast<uint16_t>(g);
+                    }
+                } else if (kind == 2) {
+                    const uint32_t d = base_r + __popc(mr & lt);
+                    if (d < static_cast<uint32_t>(K::kRing)) {
+                        v = static_cast<uint16_t>(K::kMaxCols + d);
+                        s.pos[K::kMaxCols + d] = static_cast<uint16_t>(g);
+                    }
+                }
+                map[g] = v;
+            }
+        }
+        __syncthreads();
+        const int n_act = min(static_cast<int>(s.n_act), K::kMaxCols);
+        const int n_ring = min(static_cast<int>(s.n_ring), K::kRing);
+        if (tid == 0 && (s.n_act > static_cast<uint32_t>(K::kMaxCols) || s.n_ring > static_cast<uint32_t>(K::kRing)))
+            atomicOr(a.flags, kFlagRelightRegion); // columns past the class stay unsolved
+        // Neighbour slots (solved columns lie inside the grid's margin).
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+            const int d = tid + k * THREADS;
+            if (d < n_act) {
+                const int g = s.pos[d];
+                s.nbr[d] = make_uint2(static_cast<uint32_t>(map[g - 1]) | (static_cast<uint32_t>(map[g + 1]) << 16),
+                    static_cast<uint32_t>(map[g - P]) | (static_cast<uint32_t>(map[g + P]) << 16));
+            }
+        }
+        __syncthreads(); // the map is read: the planes take the columns
+        if (tid < 2 * NB)
+            s.planes[1 + tid / NB][tid % NB][K::kZero] = 0u;
+
+        // ---- own columns: open and torch bits, top, ring-row levels ------------
+        // Per own column: slot (low 16 bits, 0xFFFF = none) and the levels of
+        // its ring rows (high 16 bits: block lo | block hi << 4 | sky lo << 8 |
+        // sky hi << 12).
         uint32_t cl[CPT];
         bool any_torch = false, any_dark = false, any_ring_block = false;
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
             const int d = tid + k * THREADS;
             cl[k] = 0xFFFFu;
-            if (d >= nx * nz)
+            if (d >= n_act)
                 continue;
-            const int dx = d % nx, dz = d / nx;
-            const int c = (dz + 1) * P + dx + 1;
-            const uint64_t gcol = static_cast<uint64_t>(z0 + dz) * a.W + (x0 + dx);
+            const int g = s.pos[d];
+            const uint64_t gcol = static_cast<uint64_t>(z0 - 1 + g / P) * a.W + (x0 - 1 + g % P);
             const uint8_t* idc = ids + gcol * H;
             const uint8_t* lc = light + gcol * H;
             uint4 chunk[2 * NB + 1];
@@ -310,53 +564,34 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
 #pragma unroll
             for (int q = 0; q < 2 * NB + 1; ++q)
                 id_chunk_bits(chunk[q], mo[q], mt[q]); // rows outside the world read as stone
-            s.top[c] = static_cast<int16_t>(t);
+            s.top[d] = static_cast<int16_t>(t);
 #pragma unroll
             for (int w = 0; w < NB; ++w) {
                 const uint32_t o = window32(mo[2 * w], mo[2 * w + 1], mo[2 * w + 2], off) & dom[w];
                 const uint32_t tb = window32(mt[2 * w], mt[2 * w + 1], mt[2 * w + 2], off) & dom[w];
-                s.open[w][c] = o;
-                s.set[1][w][c] = tb;
+                s.planes[0][w][d] = o;
+                s.planes[2][w][d] = tb;
                 any_torch |= tb != 0u;
                 any_dark |= (o & ~above_mask(wb + 32 * w, t)) != 0u;
             }
-            cl[k] = static_cast<uint32_t>(c) | (((lo & 15u) | ((hi & 15u) << 4) | ((lo >> 4) << 8) | ((hi >> 4) << 12)) << 16);
+            cl[k] = static_cast<uint32_t>(d) | (((lo & 15u) | ((hi & 15u) << 4) | ((lo >> 4) << 8) | ((hi >> 4) << 12)) << 16);
             any_ring_block |= ((lo | hi) & 15u) != 0u;
         }
 
-        // ---- own ring column: its level planes over the region's rows -------
-        // Ring column r goes to thread (nx * nz + r) % THREADS: the slots past
-        // the solved box's last column first, so that ring work falls on
-        // threads with fewer own columns.
-        const int n_ring = 2 * nx + 2 * nz;
-        const int ri = (tid - (nx * nz) % THREADS + THREADS) % THREADS; // this thread's ring index
-        int rc = -1;
-        if (ri < n_ring) {
-            int ex, ez;
-            if (ri < nx) {
-                ex = ri + 1;
-                ez = 0;
-            } else if (ri < 2 * nx) {
-                ex = ri - nx + 1;
-                ez = nz + 1;
-            } else if (ri < 2 * nx + nz) {
-                ex = 0;
-                ez = ri - 2 * nx + 1;
-            } else {
-                ex = nx + 1;
-                ez = ri - 2 * nx - nz + 1;
-            }
-            rc = ez * P + ex;
-            const int32_t gx = x0 - 1 + ex, gz = z0 - 1 + ez;
-            const uint32_t side = ex == 0 ? 1u : (ex == nx + 1 ? 2u : (ez == 0 ? 4u : 8u));
-            const bool inside = (sides & side) != 0u && gx >= 0 && gz >= 0 && gx < a.W && gz < a.D;
-            const uint8_t* lc = light + (static_cast<uint64_t>(inside ? gz : 0) * a.W + (inside ? gx : 0)) * H;
+        // ---- own ring column: its level planes over the region's rows ---------
+        // Ring column r goes to thread (n_act + r) % THREADS: the slots past
+        // the last solved column first, so that ring work falls on threads
+        // with fewer own columns.
+        const int ri = (tid - n_act % THREADS + THREADS) % THREADS; // this thread's ring index
+        const int rc = ri < n_ring ? K::kMaxCols + ri : -1;
+        if (rc >= 0) {
+            const int g = s.pos[rc];
+            const uint8_t* lc = light + (static_cast<uint64_t>(z0 - 1 + g / P) * a.W + (x0 - 1 + g % P)) * H;
             uint4 v[2 * NB + 1];
 #pragma unroll
             for (int q = 0; q < 2 * NB + 1; ++q) {
                 const int32_t r = cs + 16 * q;
-                v[q] = inside && r >= 0 && r < H ? __ldg(reinterpret_cast<const uint4*>(lc + r))
-                                                 : make_uint4(0u, 0u, 0u, 0u);
+                v[q] = r >= 0 && r < H ? __ldg(reinterpret_cast<const uint4*>(lc + r)) : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -376,8 +611,9 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                 }
             }
         }
-        const bool need_block = __syncthreads_or(any_torch || any_ring_block) != 0;
-        const bool need_sky = __syncthreads_or(any_dark) != 0;
+        const uint32_t need = (__syncthreads_or(any_torch || any_ring_block) ? 1u : 0u)
+            | (__syncthreads_or(any_dark) ? 2u : 0u);
+        const bool need_block = (need & 1u) != 0u, need_sky = (need & 2u) != 0u;
 
         // ---- the floods: block (f = 0) and sky (f = 1) -------------------------
         // 14 level steps over the own columns; their level counters in cnt
@@ -400,7 +636,7 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                 for (int w = 0; w < NB; ++w) {
                     uint32_t v = 0u;
                     if (has) {
-                        v = sky ? (s.open[w][c] & above_mask(wb + 32 * w, t)) : s.set[1][w][c];
+                        v = sky ? (s.planes[0][w][c] & above_mask(wb + 32 * w, t)) : s.planes[2][w][c];
                         if (w == 0 && (lv & 15u) == 15u)
                             v |= 1u;
                         if (w == w_hi && ((lv >> 4) & 15u) == 15u)
@@ -411,19 +647,19 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                     cnt[k][w][1] = cnt[k][w][2] = cnt[k][w][3] = 0u;
                 }
             }
-            __syncthreads(); // the torch bits in set[1] are read
+            __syncthreads(); // the torch bits in plane 2 are read
 #pragma unroll
             for (int k = 0; k < CPT; ++k)
                 if ((cl[k] & 0xFFFFu) != 0xFFFFu)
 #pragma unroll
                     for (int w = 0; w < NB; ++w)
-                        s.set[0][w][cl[k] & 0xFFFFu] = own[k][w];
+                        s.planes[1][w][cl[k] & 0xFFFFu] = own[k][w];
             if (rc >= 0)
 #pragma unroll
                 for (int w = 0; w < NB; ++w) {
                     const uint32_t pl[4] = { s.ring[4 * f][w][ri], s.ring[4 * f + 1][w][ri],
                         s.ring[4 * f + 2][w][ri], s.ring[4 * f + 3][w][ri] };
-                    s.set[0][w][rc] = at_least(15, pl);
+                    s.planes[1][w][rc] = at_least(15, pl);
                 }
             __syncthreads();
             // Steps in groups of four (levels 14 - 4g .. 11 - 4g): the parity
@@ -435,8 +671,8 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                     if (step > kMaxDistance)
                         break;
                     const int level = 15 - step; // level & 3 == (2 - u) & 3
-                    const uint32_t* cur = s.set[(step - 1) & 1][0];
-                    uint32_t* nxt = s.set[step & 1][0];
+                    const uint32_t* cur = s.planes[1 + ((step - 1) & 1)][0];
+                    uint32_t* nxt = s.planes[1 + (step & 1)][0];
 #pragma unroll
                     for (int k = 0; k < CPT; ++k) {
                         if ((cl[k] & 0xFFFFu) == 0xFFFFu)
@@ -445,22 +681,25 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                         const uint32_t lv = cl[k] >> lv_shift;
                         const bool inj_lo = (lv & 15u) == static_cast<uint32_t>(level);
                         const bool inj_hi = ((lv >> 4) & 15u) == static_cast<uint32_t>(level);
+                        const uint2 nbr = s.nbr[c];
+                        const int n0 = static_cast<int>(nbr.x & 0xFFFFu), n1 = static_cast<int>(nbr.x >> 16);
+                        const int n2 = static_cast<int>(nbr.y & 0xFFFFu), n3 = static_cast<int>(nbr.y >> 16);
                         // One word: the own word stays in a register; two: it is
                         // read back from the set (fewer registers per column).
                         uint32_t ow[NB];
 #pragma unroll
                         for (int w = 0; w < NB; ++w)
-                            ow[w] = NB == 1 ? own[k][w] : cur[w * K::kMaxExt + c];
+                            ow[w] = NB == 1 ? own[k][w] : cur[w * K::kExt + c];
                         uint32_t v[NB];
 #pragma unroll
                         for (int w = 0; w < NB; ++w) {
-                            const uint32_t* Bw = cur + w * K::kMaxExt + c;
+                            const uint32_t* Cw = cur + w * K::kExt;
                             const uint32_t below = w > 0 ? ow[w > 0 ? w - 1 : 0] : 0u;
                             const uint32_t above = w + 1 < NB ? ow[w + 1 < NB ? w + 1 : w] : 0u;
                             const uint32_t up = __funnelshift_l(below, ow[w], 1); // cell y takes y-1
                             const uint32_t dn = __funnelshift_r(ow[w], above, 1); // cell y takes y+1
-                            const uint32_t nb = up | dn | Bw[-1] | Bw[1] | Bw[-P] | Bw[P];
-                            uint32_t x = ow[w] | (s.open[w][c] & nb);
+                            const uint32_t nb = up | dn | Cw[n0] | Cw[n1] | Cw[n2] | Cw[n3];
+                            uint32_t x = ow[w] | (s.planes[0][w][c] & nb);
                             if (w == 0 && inj_lo)
                                 x |= 1u;
                             if (w == w_hi && inj_hi)
@@ -471,7 +710,7 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                         for (int w = 0; w < NB; ++w) {
                             if (NB == 1)
                                 own[k][w] = v[w];
-                            nxt[w * K::kMaxExt + c] = v[w];
+                            nxt[w * K::kExt + c] = v[w];
                             cnt[k][w][0] ^= v[w];
                             if ((u & 1) == 0) // level even
                                 cnt[k][w][1] ^= v[w];
@@ -486,7 +725,7 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                         for (int w = 0; w < NB; ++w) {
                             const uint32_t pl[4] = { s.ring[4 * f][w][ri], s.ring[4 * f + 1][w][ri],
                                 s.ring[4 * f + 2][w][ri], s.ring[4 * f + 3][w][ri] };
-                            nxt[w * K::kMaxExt + rc] = at_least(level, pl);
+                            nxt[w * K::kExt + rc] = at_least(level, pl);
                         }
                     }
                     __syncthreads();
@@ -502,17 +741,15 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                             park[((k * NB + w) * 4 + i) * THREADS + tid] = cnt[k][w][i];
         }
 
-        // ---- new light of the region's rows -----------------------------------
+        // ---- new light of the region's rows ------------------------------------
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
             if ((cl[k] & 0xFFFFu) == 0xFFFFu)
                 continue;
-            const int d = tid + k * THREADS;
-            const int dx = d % nx, dz = d / nx;
-            if (x0 + dx < wx0 || x0 + dx >= wx0 + wnx || z0 + dz < wz0 || z0 + dz >= wz0 + wnz)
-                continue; // solved for the sub-box only
-            uint8_t* lc = light + (static_cast<uint64_t>(z0 + dz) * a.W + (x0 + dx)) * H;
-            const int32_t t = s.top[cl[k] & 0xFFFFu];
+            const int d = static_cast<int>(cl[k] & 0xFFFFu);
+            const int g = s.pos[d];
+            uint8_t* lc = light + (static_cast<uint64_t>(z0 - 1 + g / P) * a.W + (x0 - 1 + g % P)) * H;
+            const int32_t t = s.top[d];
             // Light bytes of the word stream (rows wb ..), 4 rows per 32-bit
             // word, stored as aligned 4-row words of the column from row
             // A = wb & ~3: memory word j takes stream bytes 4j - e .. 4j - e + 3
@@ -563,23 +800,24 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasP
                 }
             }
         }
-        __syncthreads(); // shared planes are reused by the next region
+        __syncthreads(); // shared planes and counters are reused by the next region
     }
 }
 
-template <int THREADS, int CPT, int NB>
+template <int THREADS, int NB>
 int launch_region_list(blk_ctx* ctx, const RegionRelightArgs& base, int list, cudaStream_t st)
 {
-    using K = RegionClass<THREADS, CPT, NB>;
+    using K = RegionClass<THREADS, NB>;
     static bool attr_set[64] = {};
     const int dev = ctx->device;
-    constexpr size_t kSmem = sizeof(RegionSmem<THREADS, CPT, NB>);
+    constexpr size_t kSmem = sizeof(RegionSmem<THREADS, NB>);
+    static_assert(K::kCtasPerSm * K::kParkWords <= 32768, "park slice per SM");
     if (dev < 0 || dev >= 64) {
         set_error("device index out of range");
         return BLK_ERR_INVALID_ARGUMENT;
     }
     if (!attr_set[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(relight_region_kernel<THREADS, CPT, NB>,
+        const cudaError_t e = cudaFuncSetAttribute(relight_region_kernel<THREADS, NB>,
             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
         if (e != cudaSuccess)
             return cuda_fail(e, "cudaFuncSetAttribute(relight_region_kernel)");
@@ -589,9 +827,8 @@ int launch_region_list(blk_ctx* ctx, const RegionRelightArgs& base, int list, cu
     a.regions = ctx->region_lists + 2ull * list * ctx->region_capacity;
     a.count = ctx->region_counts + list;
     a.park = ctx->region_park + static_cast<uint64_t>(list) * ctx->park_ctas * region_park_words_per_sm();
-    const uint32_t grid = ctx->park_ctas * K::kCtasPerSm;
-    static_assert(K::kCtasPerSm * K::kParkWords <= 32768, "park slice per SM");
-    relight_region_kernel<THREADS, CPT, NB><<<grid, THREADS, kSmem, st>>>(a);
+    const unsigned grid = ctx->park_ctas * K::kCtasPerSm;
+    relight_region_kernel<THREADS, NB><<<grid, THREADS, kSmem, st>>>(a);
     return cuda_fail(cudaGetLastError(), "relight_region_kernel launch");
 }
 
@@ -625,7 +862,7 @@ int launch_relight(blk_ctx* ctx, cudaStream_t st)
     uint32_t* win_hi = ctx->dirty_window + n_tiles;
     if (cudaMemsetAsync(win_lo, 0xFF, n_tiles * sizeof(uint32_t), st) != cudaSuccess
         || cudaMemsetAsync(win_hi, 0, n_tiles * sizeof(uint32_t), st) != cudaSuccess
-        || cudaMemsetAsync(ctx->region_counts, 0, 4 * sizeof(uint32_t), st) != cudaSuccess
+        || cudaMemsetAsync(ctx->region_counts, 0, (kRegionLists + 1) * sizeof(uint32_t), st) != cudaSuccess
         || cudaMemsetAsync(ctx->dirty_count, 0, sizeof(uint32_t), st) != cudaSuccess)
         return cuda_fail(cudaGetLastError(), "relight memsets");
     RegionBuildArgs b {};
@@ -639,12 +876,13 @@ int launch_relight(blk_ctx* ctx, cudaStream_t st)
         b.lists[k] = ctx->region_lists + 2ull * k * ctx->region_capacity;
     b.counts = ctx->region_counts;
     b.capacity = ctx->region_capacity;
+    b.centres = ctx->region_centres;
     b.win_lo = win_lo;
     b.win_hi = win_hi;
     b.tiles_x = static_cast<int32_t>(ctx->tiles_x);
     b.tiles_z = static_cast<int32_t>(ctx->tiles_z);
     b.flags = ctx->flags;
-    region_build_kernel<<<(b.num_envs + 127) / 128, 128, 0, st>>>(b);
+    region_build_kernel<<<(b.num_envs + kBuildWarps - 1) / kBuildWarps, 32 * kBuildWarps, 0, st>>>(b);
     // Pack windows in place into win_lo's slots: window[t] = lo | hi << 16.
     uint64_t blocks = (n_tiles + 255) / 256;
     if (blocks > 148ull * 16)
@@ -660,21 +898,21 @@ int launch_relight(blk_ctx* ctx, cudaStream_t st)
     // exit at once).
     if (cudaEventRecord(ctx->relight_fork, st) != cudaSuccess)
         return cuda_fail(cudaGetLastError(), "relight fork");
-    for (int k = 0; k < 4; ++k)
+    for (int k = 0; k < kRegionLists; ++k)
         if (cudaStreamWaitEvent(ctx->relight_streams[k], ctx->relight_fork, 0) != cudaSuccess)
             return cuda_fail(cudaGetLastError(), "relight fork wait");
     const int rr = launch_region_relight(ctx, ctx->relight_streams);
     if (rr != BLK_OK)
         return rr;
     const int rt = launch_tiles(ctx, 1, static_cast<uint32_t>(n_tiles), st);
-    for (int k = 0; k < 4; ++k)
+    for (int k = 0; k < kRegionLists; ++k)
         if (cudaEventRecord(ctx->relight_join[k], ctx->relight_streams[k]) != cudaSuccess
             || cudaStreamWaitEvent(st, ctx->relight_join[k], 0) != cudaSuccess)
             return cuda_fail(cudaGetLastError(), "relight join");
     return rt;
 }
 
-int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[4])
+int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[kRegionLists])
 {
     RegionRelightArgs a {};
     a.ids = ctx->ids;
@@ -687,20 +925,24 @@ int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[4])
     a.env_stride = ctx->env_stride;
     a.columns = ctx->columns_per_env;
     a.capacity = ctx->region_capacity;
+    a.centres = ctx->region_centres;
     a.park = ctx->region_park;
+    a.flags = ctx->flags;
     // Size classes (lists of region_build_kernel), each on its own stream so
-    // that their tails overlap, all at most 64 columns a side: 0: <= 1024
-    // columns, one word (1024 threads x 1 column, two CTAs per SM); 1: the
-    // same, two words (512 x 2); 2: <= 4096 columns (a region, or a sub-box of
-    // a larger one with its 14-column surround), one word (1024 x 4); 3: the
-    // same, two words.
-    int rc = launch_region_list<1024, 1, 1>(ctx, a, 0, side[0]);
+    // that their tails overlap: list 2 s + nb - 1 holds regions of nb words
+    // solved by CTAs of 256 << s threads (at most 512 << s solved and 256 << s
+    // ring columns); the largest first.
+    int rc = launch_region_list<1024, 2>(ctx, a, 5, side[5]);
     if (rc == BLK_OK)
-        rc = launch_region_list<512, 2, 2>(ctx, a, 1, side[1]);
+        rc = launch_region_list<1024, 1>(ctx, a, 4, side[4]);
     if (rc == BLK_OK)
-        rc = launch_region_list<1024, 4, 1>(ctx, a, 2, side[2]);
+        rc = launch_region_list<512, 2>(ctx, a, 3, side[3]);
     if (rc == BLK_OK)
-        rc = launch_region_list<1024, 4, 2>(ctx, a, 3, side[3]);
+        rc = launch_region_list<512, 1>(ctx, a, 2, side[2]);
+    if (rc == BLK_OK)
+        rc = launch_region_list<256, 2>(ctx, a, 1, side[1]);
+    if (rc == BLK_OK)
+        rc = launch_region_list<256, 1>(ctx, a, 0, side[0]);
     return rc;
 }
 
