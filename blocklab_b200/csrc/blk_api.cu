@@ -923,7 +923,7 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     if (c.num_envs == 0 || c.num_envs > 65536 || c.max_overrides > (1u << 26) || c.width == 0 || c.depth == 0 || c.width > 4096 || c.depth > 4096
         || c.height == 0 || c.height % 32 != 0 || c.height > 256 || c.terrain_mode < 0 || c.terrain_mode > 2) {
         set_error("blk_ctx_create: unsupported configuration (num_envs 1..65536, W/D 1..4096, H a multiple of 32 up "
-                  "to 128, terrain_mode 0..2)");
+                  "to 256, terrain_mode 0..2)");
         return BLK_ERR_INVALID_ARGUMENT;
     }
     BLK_CUDA(cudaSetDevice(device), "cudaSetDevice");
@@ -989,7 +989,6 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
         }
         ctx->park_ctas = static_cast<uint32_t>(sms);
         A(dalloc(&ctx->park, static_cast<size_t>(sms) * 16 * 1024, "tile scratch"));
-        A(dalloc(&ctx->region_park, static_cast<uint64_t>(kRegionLists) * sms * region_park_words_per_sm(), "region relight scratch"));
     }
     if (rc == BLK_OK) {
         bool ok = cudaEventCreateWithFlags(&ctx->relight_fork, cudaEventDisableTiming) == cudaSuccess;
@@ -1058,7 +1057,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
         cudaEventDestroy(ctx->relight_fork);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->origins, ctx->origin_stage, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order, ctx->edit_changes,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->region_lists, ctx->region_centres, ctx->region_counts, ctx->region_park, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->region_lists, ctx->region_centres, ctx->region_counts, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);

@@ -23,6 +23,49 @@ __device__ inline void level_nibbles(uint32_t p0, uint32_t p1, uint32_t p2, uint
     n3 = ((o01 >> 2) & 0x33333333u) | (o23 & 0xCCCCCCCCu);
 }
 
+// Light bytes of 32 rows from block level bit planes b and sky level bit
+// planes s: out[q] holds rows 4q .. 4q + 3, one byte each (sky << 4 | block).
+// The nibbles of both floods are interleaved into bytes (l: rows 8m + k, h:
+// rows 8m + 4 + k in byte m of l[k], h[k]), then each group of four words is
+// transposed bytewise.
+__device__ inline void planes_to_bytes(const uint32_t (&b)[4], const uint32_t (&s)[4], uint32_t (&out)[8])
+{
+    uint32_t n[4], m[4], l[4], h[4];
+    level_nibbles(b[0], b[1], b[2], b[3], n[0], n[1], n[2], n[3]);
+    level_nibbles(s[0], s[1], s[2], s[3], m[0], m[1], m[2], m[3]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        l[k] = (n[k] & 0x0F0F0F0Fu) | ((m[k] << 4) & 0xF0F0F0F0u);
+        h[k] = ((n[k] >> 4) & 0x0F0F0F0Fu) | (m[k] & 0xF0F0F0F0u);
+    }
+    const uint32_t la = __byte_perm(l[0], l[1], 0x5140), lb = __byte_perm(l[0], l[1], 0x7362);
+    const uint32_t lc = __byte_perm(l[2], l[3], 0x5140), ld = __byte_perm(l[2], l[3], 0x7362);
+    const uint32_t ha = __byte_perm(h[0], h[1], 0x5140), hb = __byte_perm(h[0], h[1], 0x7362);
+    const uint32_t hc = __byte_perm(h[2], h[3], 0x5140), hd = __byte_perm(h[2], h[3], 0x7362);
+    out[0] = __byte_perm(la, lc, 0x5410);
+    out[2] = __byte_perm(la, lc, 0x7632);
+    out[4] = __byte_perm(lb, ld, 0x5410);
+    out[6] = __byte_perm(lb, ld, 0x7632);
+    out[1] = __byte_perm(ha, hc, 0x5410);
+    out[3] = __byte_perm(ha, hc, 0x7632);
+    out[5] = __byte_perm(hb, hd, 0x5410);
+    out[7] = __byte_perm(hb, hd, 0x7632);
+}
+
+// Asynchronous global -> shared copies (cp.async): 4 and 16 bytes, and the
+// wait for all of this thread's copies.
+__device__ inline void cp_async4(void* smem, const void* gmem)
+{
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ inline void cp_async16(void* smem, const void* gmem)
+{
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ inline void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // Bits j of the word starting at row ybase where ybase + j > top.
 __device__ inline uint32_t above_mask(int32_t ybase, int32_t top)
 {

@@ -59,7 +59,6 @@ struct blk_ctx {
     uint32_t region_capacity = 0;         // items per list, and footprint centres of all items
     uint32_t* region_centres = nullptr;   // [region_capacity] footprint centres of the items (x | z << 16)
     uint32_t* region_counts = nullptr;    // [kRegionLists + 1]: items per list, then centres used
-    uint32_t* region_park = nullptr;      // region kernels' scratch: parked block counters per CTA, one area per list
     cudaStream_t relight_streams[kRegionLists] = {}; // side streams of the region kernels (forked from the caller's stream)
     cudaEvent_t relight_fork = nullptr;
     cudaEvent_t relight_join[kRegionLists] = {};
@@ -112,11 +111,9 @@ struct RegionRelightArgs {
     const uint32_t* count;
     uint32_t capacity;
     const uint32_t* centres;    // footprint centres (x | z << 16) the items point into
-    uint32_t* park;
     uint32_t* flags;
 };
 
-uint64_t region_park_words_per_sm();
 int launch_region_build(blk_ctx* ctx, const RegionBuildArgs& a, cudaStream_t stream);
 int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[kRegionLists]);
 

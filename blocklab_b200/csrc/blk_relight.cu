@@ -71,60 +71,62 @@ __device__ inline Box hull(const Box& a, const Box& b)
         max(a.y1, b.y1) };
 }
 
-// Per-class limits of the region kernels. A CTA of THREADS threads owns two
-// solved columns per thread (slot d = tid + k * THREADS) and one ring column
-// (slot kMaxCols + r); NB words of 32 rows per column.
-template <int THREADS, int NB>
+// Per-class limits of the region kernels. A CTA of THREADS threads owns CPT
+// solved columns per thread (slot d = tid + k * THREADS) and at most one ring
+// column (slot kMaxCols + r); NB words of 32 rows per column. The block and
+// sky floods run together, so both level counters of a column stay in
+// registers.
+template <int THREADS, int CPT, int NB>
 struct RegionClass {
-    static constexpr int kCpt = 2;
-    static constexpr int kMaxCols = THREADS * kCpt;        // solved columns
-    static constexpr int kRing = THREADS;                  // ring columns
+    static constexpr int kMaxCols = THREADS * CPT;         // solved columns
+    static constexpr int kRing = THREADS / 2;              // ring columns
     static constexpr int kZero = kMaxCols + kRing;         // slot that stays empty: neighbours outside the world
     static constexpr int kExt = (kZero + 1 + 3) & ~3;      // slots per plane
-    static constexpr int kMapCells = 6 * NB * kExt;        // grid cells the setup map can hold (16 bits each)
-    static constexpr int kCtasPerSm = THREADS <= 256 ? 4 : (THREADS <= 512 ? 2 : 1);
-    static constexpr int kParkWords = kMaxCols * NB * 4;   // parked block counters per CTA
+    static constexpr int kMapCells = 10 * NB * kExt;       // grid cells the setup map can hold (16 bits each)
+    static constexpr int kCtasPerSm = THREADS <= 512 ? 2 : 1;
 };
 
-template <int THREADS, int NB>
+template <int THREADS, int CPT, int NB>
 struct RegionSmem {
-    using K = RegionClass<THREADS, NB>;
-    uint32_t planes[3][NB][K::kExt];  // open cells (0) and level set S ping-pong (1, 2; 2 holds torch bits
-                                      // before a block flood); during setup the grid map (slot per grid cell)
+    using K = RegionClass<THREADS, CPT, NB>;
+    uint2 set[2][NB][K::kExt];        // level set S of the block (x) and sky (y) floods, ping-pong; during
+                                      // setup (with open) the grid map: slot per grid cell
+    uint32_t open[NB][K::kExt];       // open cells of the solved columns
     uint32_t ring[8][NB][K::kRing];   // level planes of the ring columns: block 0..3, sky 4..7
     uint2 nbr[K::kMaxCols];           // slots of each solved column's neighbours: x-1 | x+1 << 16, z-1 | z+1 << 16
     uint16_t pos[K::kMaxCols + K::kRing]; // grid cell of each solved and ring slot
     int16_t top[K::kMaxCols];         // local y of each solved column's highest opaque cell
-    uint32_t cen[kMaxCentres];        // the region's diamond centres, x | z << 16
-    uint32_t n_act, n_ring;
+    uint4 hdr[2][2];                  // item records: this region's and the next one's (prefetched)
+    uint32_t cen[2][kMaxCentres];     // their diamond centres, x | z << 16
+    uint32_t wcount[THREADS / 32];    // solved | ring << 16 grid cells per warp
 };
 
-template <int THREADS, int NB>
+template <int THREADS, int CPT, int NB>
 __host__ __device__ constexpr bool class_fits(uint32_t cols, uint32_t ring, int64_t cells)
 {
-    using K = RegionClass<THREADS, NB>;
+    using K = RegionClass<THREADS, CPT, NB>;
     return cols <= static_cast<uint32_t>(K::kMaxCols) && ring <= static_cast<uint32_t>(K::kRing)
         && cells <= K::kMapCells;
 }
 
 // Item list of a region with the given words, solved and ring columns and
-// grid cells: 2 s + nb - 1 for the size class of 256 << s threads; -1 when
-// none fits (tile path).
+// grid cells: 2 s + nb - 1 for size class s (512 x 1, 1024 x 1 and 1024 x 2
+// columns); -1 when none fits (tile path).
 __device__ inline int region_list_for(int nb, uint32_t cols, uint32_t ring, int64_t cells)
 {
     if (nb == 1) {
-        if (class_fits<256, 1>(cols, ring, cells))
+        if (class_fits<512, 1, 1>(cols, ring, cells))
             return 0;
-        if (class_fits<512, 1>(cols, ring, cells))
+        if (class_fits<1024, 1, 1>(cols, ring, cells))
             return 2;
-        if (class_fits<1024, 1>(cols, ring, cells))
+        if (class_fits<1024, 2, 1>(cols, ring, cells))
             return 4;
     } else {
-        if (class_fits<256, 2>(cols, ring, cells))
+        if (class_fits<512, 1, 2>(cols, ring, cells))
             return 1;
-        if (class_fits<512, 2>(cols, ring, cells))
+        if (class_fits<1024, 1, 2>(cols, ring, cells))
             return 3;
-        if (class_fits<1024, 2>(cols, ring, cells))
+        if (class_fits<1024, 2, 2>(cols, ring, cells))
             return 5;
     }
     return -1;
@@ -415,39 +417,56 @@ __device__ inline uint32_t at_least(int L, const uint32_t (&p)[4])
 // cells of the region's bounding box and its one-column margin (the grid,
 // pitch nx + 2) by L1 distance to the nearest centre, compacts the solved
 // (<= 14) and ring (== 15) columns into slots and records each solved column's
-// neighbour slots.
-template <int THREADS, int NB>
-__global__ void __launch_bounds__(THREADS, RegionClass<THREADS, NB>::kCtasPerSm)
+// neighbour slots. The block and sky floods then run together: 14 steps over
+// (block, sky) word pairs, one barrier per step.
+template <int THREADS, int CPT, int NB>
+__global__ void __launch_bounds__(THREADS, RegionClass<THREADS, CPT, NB>::kCtasPerSm)
     relight_region_kernel(RegionRelightArgs a)
 {
-    using K = RegionClass<THREADS, NB>;
-    using Sm = RegionSmem<THREADS, NB>;
-    constexpr int CPT = K::kCpt;
+    using K = RegionClass<THREADS, CPT, NB>;
+    using Sm = RegionSmem<THREADS, CPT, NB>;
     static_assert(K::kRing <= THREADS, "one ring column per thread");
     static_assert(K::kZero < 0xFFFF, "slots fit 16 bits");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Sm& s = *reinterpret_cast<Sm*>(smem_raw);
-    uint16_t* map = reinterpret_cast<uint16_t*>(&s.planes[0][0][0]);
+    uint16_t* map = reinterpret_cast<uint16_t*>(&s.set[0][0][0]);
     const int tid = threadIdx.x, lane = tid & 31;
     const uint32_t count = min(*a.count, a.capacity);
-    uint32_t* park = a.park + static_cast<uint64_t>(blockIdx.x) * K::kParkWords;
 
-    for (uint32_t item = blockIdx.x; item < count; item += gridDim.x) {
-        const uint4 rec = a.regions[2ull * item];
-        const uint4 inf = a.regions[2ull * item + 1];
+    // The item record and centres of the next region are copied into shared
+    // memory (cp.async) while this one is solved: the header at the start,
+    // the centres once the header is in.
+    uint32_t item = blockIdx.x;
+    int hb = 0; // buffer of this region's record and centres
+    if (item < count) {
+        if (tid < 2)
+            s.hdr[0][tid] = a.regions[2ull * item + tid];
+        __syncthreads();
+        const uint4 inf0 = s.hdr[0][1];
+        if (tid < min(static_cast<int>(inf0.y), kMaxCentres))
+            s.cen[0][tid] = __ldg(a.centres + inf0.x + tid);
+        __syncthreads();
+    }
+    for (; item < count; item += gridDim.x, hb ^= 1) {
+        const uint4 rec = s.hdr[hb][0];
+        const uint4 inf = s.hdr[hb][1];
+        const uint32_t next = item + gridDim.x;
+        if (tid < 2 && next < count)
+            cp_async16(&s.hdr[hb ^ 1][tid], a.regions + 2ull * next + tid);
         const uint32_t env = rec.x;
         const int32_t x0 = static_cast<int32_t>(rec.y & 0xFFFFu), z0 = static_cast<int32_t>(rec.y >> 16);
         const int32_t nx = static_cast<int32_t>(rec.z & 0xFFFFu), nz = static_cast<int32_t>(rec.z >> 16);
         const int32_t y0 = static_cast<int32_t>(rec.w & 0xFFFFu), ny = static_cast<int32_t>(rec.w >> 16);
-        const int nc = min(static_cast<int>(inf.y), kMaxCentres);
         const int32_t H = a.H;
         const int P = nx + 2;                 // grid pitch
-        const int G = P * (nz + 2);           // grid cells
-        if (G > K::kMapCells || nx < 1 || nz < 1) { // the build files no such region
-            if (tid == 0)
-                atomicOr(a.flags, kFlagRelightRegion);
-            continue;
-        }
+        // The build files no region past the map; one that were would be
+        // flagged and left unsolved (no centres, no grid).
+        const bool bad = P * (nz + 2) > K::kMapCells || nx < 1 || nz < 1;
+        if (bad && tid == 0)
+            atomicOr(a.flags, kFlagRelightRegion);
+        const int G = bad ? 0 : P * (nz + 2); // grid cells
+        const int nc = bad ? 0 : min(static_cast<int>(inf.y), kMaxCentres);
+        const uint32_t* cen = s.cen[hb];
         const int32_t wb = y0 - 1;            // row of bit 0 of word 0 (the lower ring row)
         const int32_t cs = wb & ~15;          // first 16-row chunk of the words' rows
         const int off = wb - cs;              // 0 .. 15
@@ -465,60 +484,88 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, NB>::kCtasPerSm)
         }
 
         // ---- grid: solved and ring columns, compacted into slots ---------------
-        if (tid < nc)
-            s.cen[tid] = __ldg(a.centres + inf.x + tid);
-        if (tid == 0) {
-            s.n_act = 0u;
-            s.n_ring = 0u;
-        }
-        __syncthreads();
-        for (int g0 = 0; g0 < G; g0 += THREADS) { // warp-uniform trip count (ballots)
-            const int g = g0 + tid;
-            int kind = 0; // 1 solved, 2 ring
-            if (g < G) {
-                const int32_t x = x0 - 1 + g % P, z = z0 - 1 + g / P;
-                if (x >= 0 && z >= 0 && x < a.W && z < a.D) {
+        // Kind of grid cell g: 1 solved (L1 distance to the nearest centre <=
+        // 14), 2 ring (== 15), 0 neither or outside the world. Two passes:
+        // the warps' ballots and counts (cell g = g0 + tid, its coordinates
+        // stepped without division), then slots from the prefix of the warp
+        // counts (warp w's cells g = 32 w + lane + i THREADS, in that order).
+        // The ballots wait in the ring planes, which setup fills later.
+        const int warp = tid >> 5;
+        const unsigned lt = (1u << lane) - 1u;
+        uint2* masks = reinterpret_cast<uint2*>(&s.ring[0][0][0]); // [iteration][warp]: solved, ring
+        static_assert((K::kMapCells / THREADS + 1) * (THREADS / 32) * sizeof(uint2) <= sizeof(s.ring),
+            "grid ballots fit the ring planes");
+        {
+            const int step_z = THREADS / P, step_x = THREADS - step_z * P;
+            int gx = tid % P, gz = tid / P;
+            uint32_t ca = 0u, cr = 0u;
+            for (int g0 = 0, it = 0; g0 < G; g0 += THREADS, ++it) { // warp-uniform trip count (ballots)
+                int kind = 0;
+                const int32_t x = x0 - 1 + gx, z = z0 - 1 + gz;
+                if (g0 + tid < G && x >= 0 && z >= 0 && x < a.W && z < a.D) {
                     int32_t m = INT_MAX;
                     for (int i = 0; i < nc; ++i) {
-                        const uint32_t c = s.cen[i];
+                        const uint32_t c = cen[i];
                         m = min(m, abs(x - static_cast<int32_t>(c & 0xFFFFu)) + abs(z - static_cast<int32_t>(c >> 16)));
                     }
                     kind = m <= kMaxDistance ? 1 : (m == kMaxDistance + 1 ? 2 : 0);
                 }
-            }
-            const unsigned ma = __ballot_sync(0xFFFFFFFFu, kind == 1), mr = __ballot_sync(0xFFFFFFFFu, kind == 2);
-            uint32_t base_a = 0u, base_r = 0u;
-            if (lane == 0) {
-                if (ma)
-                    base_a = atomicAdd(&s.n_act, static_cast<uint32_t>(__popc(ma)));
-                if (mr)
-                    base_r = atomicAdd(&s.n_ring, static_cast<uint32_t>(__popc(mr)));
-            }
-            base_a = __shfl_sync(0xFFFFFFFFu, base_a, 0);
-            base_r = __shfl_sync(0xFFFFFFFFu, base_r, 0);
-            const unsigned lt = (1u << lane) - 1u;
-            if (g < G) {
-                uint16_t v = static_cast<uint16_t>(K::kZero);
-                if (kind == 1) {
-                    const uint32_t d = base_a + __popc(ma & lt);
-                    if (d < static_cast<uint32_t>(K::kMaxCols)) {
-                        v = static_cast<uint16_t>(d);
-                        s.pos[d] = static_cast<uint16_t>(g);
-                    }
-                } else if (kind == 2) {
-                    const uint32_t d = base_r + __popc(mr & lt);
-                    if (d < static_cast<uint32_t>(K::kRing)) {
-                        v = static_cast<uint16_t>(K::kMaxCols + d);
-                        s.pos[K::kMaxCols + d] = static_cast<uint16_t>(g);
-                    }
+                const unsigned ma = __ballot_sync(0xFFFFFFFFu, kind == 1), mr = __ballot_sync(0xFFFFFFFFu, kind == 2);
+                if (lane == 0)
+                    masks[it * (THREADS / 32) + warp] = make_uint2(ma, mr);
+                ca += __popc(ma);
+                cr += __popc(mr);
+                gx += step_x;
+                gz += step_z;
+                if (gx >= P) {
+                    gx -= P;
+                    ++gz;
                 }
-                map[g] = v;
+            }
+            if (lane == 0)
+                s.wcount[warp] = ca | (cr << 16);
+        }
+        __syncthreads();
+        uint32_t tot_a = 0u, tot_r = 0u;
+        {
+            uint32_t base_a = 0u, base_r = 0u;
+            for (int w = 0; w < THREADS / 32; ++w) {
+                const uint32_t v = s.wcount[w];
+                if (w < warp) {
+                    base_a += v & 0xFFFFu;
+                    base_r += v >> 16;
+                }
+                tot_a += v & 0xFFFFu;
+                tot_r += v >> 16;
+            }
+            for (int g0 = 0, it = 0; g0 < G; g0 += THREADS, ++it) {
+                const int g = g0 + tid;
+                const uint2 mk = masks[it * (THREADS / 32) + warp];
+                if (g < G) {
+                    uint16_t v = static_cast<uint16_t>(K::kZero);
+                    if ((mk.x >> lane) & 1u) {
+                        const uint32_t d = base_a + __popc(mk.x & lt);
+                        if (d < static_cast<uint32_t>(K::kMaxCols)) {
+                            v = static_cast<uint16_t>(d);
+                            s.pos[d] = static_cast<uint16_t>(g);
+                        }
+                    } else if ((mk.y >> lane) & 1u) {
+                        const uint32_t d = base_r + __popc(mk.y & lt);
+                        if (d < static_cast<uint32_t>(K::kRing)) {
+                            v = static_cast<uint16_t>(K::kMaxCols + d);
+                            s.pos[K::kMaxCols + d] = static_cast<uint16_t>(g);
+                        }
+                    }
+                    map[g] = v;
+                }
+                base_a += __popc(mk.x);
+                base_r += __popc(mk.y);
             }
         }
         __syncthreads();
-        const int n_act = min(static_cast<int>(s.n_act), K::kMaxCols);
-        const int n_ring = min(static_cast<int>(s.n_ring), K::kRing);
-        if (tid == 0 && (s.n_act > static_cast<uint32_t>(K::kMaxCols) || s.n_ring > static_cast<uint32_t>(K::kRing)))
+        const int n_act = min(static_cast<int>(tot_a), K::kMaxCols);
+        const int n_ring = min(static_cast<int>(tot_r), K::kRing);
+        if (tid == 0 && (tot_a > static_cast<uint32_t>(K::kMaxCols) || tot_r > static_cast<uint32_t>(K::kRing)))
             atomicOr(a.flags, kFlagRelightRegion); // columns past the class stay unsolved
         // Neighbour slots (solved columns lie inside the grid's margin).
 #pragma unroll
@@ -532,18 +579,23 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, NB>::kCtasPerSm)
         }
         __syncthreads(); // the map is read: the planes take the columns
         if (tid < 2 * NB)
-            s.planes[1 + tid / NB][tid % NB][K::kZero] = 0u;
+            s.set[tid / NB][tid % NB][K::kZero] = make_uint2(0u, 0u);
 
-        // ---- own columns: open and torch bits, top, ring-row levels ------------
+        // ---- own columns: open bits, top, ring-row levels, level-15 sets -------
         // Per own column: slot (low 16 bits, 0xFFFF = none) and the levels of
         // its ring rows (high 16 bits: block lo | block hi << 4 | sky lo << 8 |
-        // sky hi << 12).
+        // sky hi << 12). The level-15 sets: torches and sky sources (open cells
+        // above the top), and ring rows of level 15.
         uint32_t cl[CPT];
-        bool any_torch = false, any_dark = false, any_ring_block = false;
+        uint2 own[CPT][NB];
+        bool any_block = false, any_dark = false;
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
             const int d = tid + k * THREADS;
             cl[k] = 0xFFFFu;
+#pragma unroll
+            for (int w = 0; w < NB; ++w)
+                own[k][w] = make_uint2(0u, 0u);
             if (d >= n_act)
                 continue;
             const int g = s.pos[d];
@@ -569,20 +621,34 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, NB>::kCtasPerSm)
             for (int w = 0; w < NB; ++w) {
                 const uint32_t o = window32(mo[2 * w], mo[2 * w + 1], mo[2 * w + 2], off) & dom[w];
                 const uint32_t tb = window32(mt[2 * w], mt[2 * w + 1], mt[2 * w + 2], off) & dom[w];
-                s.planes[0][w][d] = o;
-                s.planes[2][w][d] = tb;
-                any_torch |= tb != 0u;
-                any_dark |= (o & ~above_mask(wb + 32 * w, t)) != 0u;
+                const uint32_t above = above_mask(wb + 32 * w, t);
+                s.open[w][d] = o;
+                any_block |= tb != 0u;
+                any_dark |= (o & ~above) != 0u;
+                uint32_t vb = tb, vs = o & above;
+                if (w == 0) {
+                    vb |= (lo & 15u) == 15u ? 1u : 0u;
+                    vs |= (lo >> 4) == 15u ? 1u : 0u;
+                }
+                if (w == w_hi) {
+                    vb |= (hi & 15u) == 15u ? b_hi : 0u;
+                    vs |= (hi >> 4) == 15u ? b_hi : 0u;
+                }
+                own[k][w] = make_uint2(vb, vs);
+                s.set[0][w][d] = own[k][w];
             }
             cl[k] = static_cast<uint32_t>(d) | (((lo & 15u) | ((hi & 15u) << 4) | ((lo >> 4) << 8) | ((hi >> 4) << 12)) << 16);
-            any_ring_block |= ((lo | hi) & 15u) != 0u;
+            any_block |= ((lo | hi) & 15u) != 0u;
         }
 
         // ---- own ring column: its level planes over the region's rows ---------
-        // Ring column r goes to thread (n_act + r) % THREADS: the slots past
-        // the last solved column first, so that ring work falls on threads
-        // with fewer own columns.
-        const int ri = (tid - n_act % THREADS + THREADS) % THREADS; // this thread's ring index
+        // Ring column r goes to thread (base + r) % THREADS, base = the first
+        // warp past the last solved column when the ring fits there (no warp
+        // then runs both a solved and a ring column per step, the step's
+        // longest path), else the last n_ring threads.
+        const int last = (n_act - 1) % THREADS + 1;                 // threads with the most solved columns
+        const int ring_base = min((last + 31) & ~31, THREADS - n_ring);
+        const int ri = (tid - ring_base + THREADS) % THREADS;       // this thread's ring index
         const int rc = ri < n_ring ? K::kMaxCols + ri : -1;
         if (rc >= 0) {
             const int g = s.pos[rc];
@@ -607,190 +673,180 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, NB>::kCtasPerSm)
                     const uint32_t pl = window32(m[2 * w], m[2 * w + 1], m[2 * w + 2], off) & dom[w];
                     s.ring[i][w][ri] = pl;
                     if (i < 4)
-                        any_ring_block |= pl != 0u;
+                        any_block |= pl != 0u;
                 }
+            }
+#pragma unroll
+            for (int w = 0; w < NB; ++w) {
+                const uint32_t pb[4] = { s.ring[0][w][ri], s.ring[1][w][ri], s.ring[2][w][ri], s.ring[3][w][ri] };
+                const uint32_t ps[4] = { s.ring[4][w][ri], s.ring[5][w][ri], s.ring[6][w][ri], s.ring[7][w][ri] };
+                s.set[0][w][rc] = make_uint2(at_least(15, pb), at_least(15, ps));
             }
         }
-        const uint32_t need = (__syncthreads_or(any_torch || any_ring_block) ? 1u : 0u)
-            | (__syncthreads_or(any_dark) ? 2u : 0u);
-        const bool need_block = (need & 1u) != 0u, need_sky = (need & 2u) != 0u;
+        // Floods only where they can give more than the level-15 sets: block
+        // light needs a torch or block light on the ring, sky light a dark open
+        // cell (else sky = 15 above the top, 0 below).
+        if (tid < 2)
+            cp_async_wait_all(); // the next record is in (visible after the barrier)
+        const bool need_block = __syncthreads_or(any_block) != 0;
+        const bool floods = __syncthreads_or(any_dark) != 0 || need_block;
+        if (next < count) {
+            const uint4 ninf = s.hdr[hb ^ 1][1];
+            if (tid < min(static_cast<int>(ninf.y), kMaxCentres))
+                cp_async4(&s.cen[hb ^ 1][tid], a.centres + ninf.x + tid);
+        }
 
-        // ---- the floods: block (f = 0) and sky (f = 1) -------------------------
-        // 14 level steps over the own columns; their level counters in cnt
-        // (bit planes: parity of the level, bit 1, bit 2, bit 3). The block
-        // counters wait in this CTA's scratch slice during a sky flood.
-        uint32_t cnt[CPT][NB][4];
-        const bool parked = need_block && need_sky;
-        for (int f = need_block ? 0 : 1; f < (need_sky ? 2 : 1); ++f) {
-            const bool sky = f == 1;
-            const int lv_shift = sky ? 24 : 16;
-            uint32_t own[CPT][NB];
-            // Level-15 set: sources, and fixed cells of level 15.
+        // ---- the floods: 14 level steps of both sets ---------------------------
+        // Level counters of the own words, block (b = 0) and sky (b = 1), as bit
+        // planes: parity of the level, bit 1, bit 2, bit 3.
+        uint32_t cnt[CPT][NB][2][4];
 #pragma unroll
-            for (int k = 0; k < CPT; ++k) {
-                const bool has = (cl[k] & 0xFFFFu) != 0xFFFFu;
-                const int c = has ? static_cast<int>(cl[k] & 0xFFFFu) : 0;
-                const uint32_t lv = cl[k] >> lv_shift;
-                const int32_t t = s.top[c];
+        for (int k = 0; k < CPT; ++k)
 #pragma unroll
-                for (int w = 0; w < NB; ++w) {
-                    uint32_t v = 0u;
-                    if (has) {
-                        v = sky ? (s.planes[0][w][c] & above_mask(wb + 32 * w, t)) : s.planes[2][w][c];
-                        if (w == 0 && (lv & 15u) == 15u)
-                            v |= 1u;
-                        if (w == w_hi && ((lv >> 4) & 15u) == 15u)
-                            v |= b_hi;
-                    }
-                    own[k][w] = v;
-                    cnt[k][w][0] = v;
-                    cnt[k][w][1] = cnt[k][w][2] = cnt[k][w][3] = 0u;
-                }
+            for (int w = 0; w < NB; ++w) {
+                cnt[k][w][0][0] = own[k][w].x;
+                cnt[k][w][1][0] = own[k][w].y;
+#pragma unroll
+                for (int i = 1; i < 4; ++i)
+                    cnt[k][w][0][i] = cnt[k][w][1][i] = 0u;
             }
-            __syncthreads(); // the torch bits in plane 2 are read
+        if (floods) {
+#pragma unroll 1
+            for (int step = 1; step <= kMaxDistance; ++step) {
+                const int level = 15 - step;
+                const bool even = (level & 1) == 0, four = (level & 3) == 0, eight = level == 8;
+                const uint2* cur = s.set[(step - 1) & 1][0];
+                uint2* nxt = s.set[step & 1][0];
 #pragma unroll
-            for (int k = 0; k < CPT; ++k)
-                if ((cl[k] & 0xFFFFu) != 0xFFFFu)
+                for (int k = 0; k < CPT; ++k) {
+                    if ((cl[k] & 0xFFFFu) == 0xFFFFu)
+                        continue;
+                    const int c = static_cast<int>(cl[k] & 0xFFFFu);
+                    const uint32_t lv = cl[k] >> 16;
+                    const uint32_t L = static_cast<uint32_t>(level);
+                    const bool ib_lo = (lv & 15u) == L, ib_hi = ((lv >> 4) & 15u) == L;
+                    const bool is_lo = ((lv >> 8) & 15u) == L, is_hi = (lv >> 12) == L;
+                    const uint2 nbr = s.nbr[c];
+                    const int n0 = static_cast<int>(nbr.x & 0xFFFFu), n1 = static_cast<int>(nbr.x >> 16);
+                    const int n2 = static_cast<int>(nbr.y & 0xFFFFu), n3 = static_cast<int>(nbr.y >> 16);
+                    // One word: the own pair stays in registers; two: it is read
+                    // back from the set (fewer registers per column).
+                    uint2 ow[NB];
 #pragma unroll
                     for (int w = 0; w < NB; ++w)
-                        s.planes[1][w][cl[k] & 0xFFFFu] = own[k][w];
-            if (rc >= 0)
+                        ow[w] = NB == 1 ? own[k][w] : cur[w * K::kExt + c];
+                    uint2 v[NB];
 #pragma unroll
-                for (int w = 0; w < NB; ++w) {
-                    const uint32_t pl[4] = { s.ring[4 * f][w][ri], s.ring[4 * f + 1][w][ri],
-                        s.ring[4 * f + 2][w][ri], s.ring[4 * f + 3][w][ri] };
-                    s.planes[1][w][rc] = at_least(15, pl);
-                }
-            __syncthreads();
-            // Steps in groups of four (levels 14 - 4g .. 11 - 4g): the parity
-            // tests of the counters are compile-time within a group.
-            for (int g = 0; g < 4; ++g) {
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int step = 4 * g + u + 1;
-                    if (step > kMaxDistance)
-                        break;
-                    const int level = 15 - step; // level & 3 == (2 - u) & 3
-                    const uint32_t* cur = s.planes[1 + ((step - 1) & 1)][0];
-                    uint32_t* nxt = s.planes[1 + (step & 1)][0];
-#pragma unroll
-                    for (int k = 0; k < CPT; ++k) {
-                        if ((cl[k] & 0xFFFFu) == 0xFFFFu)
-                            continue;
-                        const int c = static_cast<int>(cl[k] & 0xFFFFu);
-                        const uint32_t lv = cl[k] >> lv_shift;
-                        const bool inj_lo = (lv & 15u) == static_cast<uint32_t>(level);
-                        const bool inj_hi = ((lv >> 4) & 15u) == static_cast<uint32_t>(level);
-                        const uint2 nbr = s.nbr[c];
-                        const int n0 = static_cast<int>(nbr.x & 0xFFFFu), n1 = static_cast<int>(nbr.x >> 16);
-                        const int n2 = static_cast<int>(nbr.y & 0xFFFFu), n3 = static_cast<int>(nbr.y >> 16);
-                        // One word: the own word stays in a register; two: it is
-                        // read back from the set (fewer registers per column).
-                        uint32_t ow[NB];
-#pragma unroll
-                        for (int w = 0; w < NB; ++w)
-                            ow[w] = NB == 1 ? own[k][w] : cur[w * K::kExt + c];
-                        uint32_t v[NB];
-#pragma unroll
-                        for (int w = 0; w < NB; ++w) {
-                            const uint32_t* Cw = cur + w * K::kExt;
-                            const uint32_t below = w > 0 ? ow[w > 0 ? w - 1 : 0] : 0u;
-                            const uint32_t above = w + 1 < NB ? ow[w + 1 < NB ? w + 1 : w] : 0u;
-                            const uint32_t up = __funnelshift_l(below, ow[w], 1); // cell y takes y-1
-                            const uint32_t dn = __funnelshift_r(ow[w], above, 1); // cell y takes y+1
-                            const uint32_t nb = up | dn | Cw[n0] | Cw[n1] | Cw[n2] | Cw[n3];
-                            uint32_t x = ow[w] | (s.planes[0][w][c] & nb);
-                            if (w == 0 && inj_lo)
-                                x |= 1u;
-                            if (w == w_hi && inj_hi)
-                                x |= b_hi;
-                            v[w] = x;
+                    for (int w = 0; w < NB; ++w) {
+                        const uint2* Cw = cur + w * K::kExt;
+                        const uint2 a0 = Cw[n0], a1 = Cw[n1], a2 = Cw[n2], a3 = Cw[n3];
+                        const uint2 below = w > 0 ? ow[w > 0 ? w - 1 : 0] : make_uint2(0u, 0u);
+                        const uint2 above = w + 1 < NB ? ow[w + 1 < NB ? w + 1 : w] : make_uint2(0u, 0u);
+                        const uint32_t o = s.open[w][c];
+                        // cell y takes y-1 (funnel left) and y+1 (funnel right)
+                        const uint32_t nbx = __funnelshift_l(below.x, ow[w].x, 1) | __funnelshift_r(ow[w].x, above.x, 1)
+                            | a0.x | a1.x | a2.x | a3.x;
+                        const uint32_t nby = __funnelshift_l(below.y, ow[w].y, 1) | __funnelshift_r(ow[w].y, above.y, 1)
+                            | a0.y | a1.y | a2.y | a3.y;
+                        uint32_t xb = ow[w].x | (o & nbx), xs = ow[w].y | (o & nby);
+                        if (w == 0) {
+                            xb |= ib_lo ? 1u : 0u;
+                            xs |= is_lo ? 1u : 0u;
                         }
+                        if (w == w_hi) {
+                            xb |= ib_hi ? b_hi : 0u;
+                            xs |= is_hi ? b_hi : 0u;
+                        }
+                        v[w] = make_uint2(xb, xs);
+                    }
 #pragma unroll
-                        for (int w = 0; w < NB; ++w) {
-                            if (NB == 1)
-                                own[k][w] = v[w];
-                            nxt[w * K::kExt + c] = v[w];
-                            cnt[k][w][0] ^= v[w];
-                            if ((u & 1) == 0) // level even
-                                cnt[k][w][1] ^= v[w];
-                            if (u == 2) // level % 4 == 0
-                                cnt[k][w][2] ^= v[w];
-                            if (level == 8)
-                                cnt[k][w][3] = v[w];
+                    for (int w = 0; w < NB; ++w) {
+                        if (NB == 1)
+                            own[k][w] = v[w];
+                        nxt[w * K::kExt + c] = v[w];
+                        cnt[k][w][0][0] ^= v[w].x;
+                        cnt[k][w][1][0] ^= v[w].y;
+                        if (even) {
+                            cnt[k][w][0][1] ^= v[w].x;
+                            cnt[k][w][1][1] ^= v[w].y;
+                        }
+                        if (four) {
+                            cnt[k][w][0][2] ^= v[w].x;
+                            cnt[k][w][1][2] ^= v[w].y;
+                        }
+                        if (eight) {
+                            cnt[k][w][0][3] = v[w].x;
+                            cnt[k][w][1][3] = v[w].y;
                         }
                     }
-                    if (rc >= 0) {
-#pragma unroll
-                        for (int w = 0; w < NB; ++w) {
-                            const uint32_t pl[4] = { s.ring[4 * f][w][ri], s.ring[4 * f + 1][w][ri],
-                                s.ring[4 * f + 2][w][ri], s.ring[4 * f + 3][w][ri] };
-                            nxt[w * K::kExt + rc] = at_least(level, pl);
-                        }
-                    }
-                    __syncthreads();
                 }
+                if (rc >= 0) {
+#pragma unroll
+                    for (int w = 0; w < NB; ++w) {
+                        const uint32_t pb[4] = { s.ring[0][w][ri], s.ring[1][w][ri], s.ring[2][w][ri], s.ring[3][w][ri] };
+                        const uint32_t ps[4] = { s.ring[4][w][ri], s.ring[5][w][ri], s.ring[6][w][ri], s.ring[7][w][ri] };
+                        nxt[w * K::kExt + rc] = make_uint2(at_least(level, pb), at_least(level, ps));
+                    }
+                }
+                __syncthreads();
             }
-            if (!sky && parked)
-#pragma unroll
-                for (int k = 0; k < CPT; ++k)
-#pragma unroll
-                    for (int w = 0; w < NB; ++w)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            park[((k * NB + w) * 4 + i) * THREADS + tid] = cnt[k][w][i];
         }
 
         // ---- new light of the region's rows ------------------------------------
+        // Light bytes of the word stream (rows wb ..), 4 rows per 32-bit word,
+        // go out as aligned 4-row memory words of each column from row
+        // A = wb & ~3: memory word j takes stream bytes 4j - e .. 4j - e + 3
+        // (e = wb - A), i.e. the stream words j - 1 and j. Each thread builds
+        // its column's memory words in its warp's staging area (the dead set,
+        // open and ring planes; odd pitch kW); the warp then stores them with
+        // consecutive lanes on consecutive words of a column (a few lines per
+        // store instead of one per lane). Words jlo .. jlo + nw - 1 hold the
+        // region's rows (the first and last may be partial: byte stores).
+        constexpr int kW = 8 * NB + 1;
+        static_assert(THREADS * kW * sizeof(uint32_t) <= sizeof(s.set) + sizeof(s.open) + sizeof(s.ring),
+            "output staging fits the dead planes");
+        const int32_t A = wb & ~3;
+        const uint32_t sh = 8u * static_cast<uint32_t>(wb - A);
+        const int jlo = (y0 - A) >> 2;
+        const int nw = max(((y0 + ny - 1 - A) >> 2) - jlo + 1, 1);
+        const int rq = 32 / nw, rr = 32 - rq * nw; // a lane's step of 32 (column, word) pairs
+        uint32_t* stage = reinterpret_cast<uint32_t*>(&s.set[0][0][0]) + (tid & ~31) * kW;
+        uint32_t* colbase = reinterpret_cast<uint32_t*>(&s.nbr[0]) + (tid & ~31); // the warp's column offsets (nbr is dead)
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
-            if ((cl[k] & 0xFFFFu) == 0xFFFFu)
-                continue;
-            const int d = static_cast<int>(cl[k] & 0xFFFFu);
-            const int g = s.pos[d];
-            uint8_t* lc = light + (static_cast<uint64_t>(z0 - 1 + g / P) * a.W + (x0 - 1 + g % P)) * H;
-            const int32_t t = s.top[d];
-            // Light bytes of the word stream (rows wb ..), 4 rows per 32-bit
-            // word, stored as aligned 4-row words of the column from row
-            // A = wb & ~3: memory word j takes stream bytes 4j - e .. 4j - e + 3
-            // (e = wb - A), i.e. the stream words j - 1 and j.
-            const int32_t A = wb & ~3;
-            const uint32_t sh = 8u * static_cast<uint32_t>(wb - A);
-            uint32_t carry = 0u; // stream word 8w - 1
+            if ((cl[k] & 0xFFFFu) != 0xFFFFu) {
+                const int g = s.pos[cl[k] & 0xFFFFu];
+                colbase[lane] = static_cast<uint32_t>((z0 - 1 + g / P) * a.W + (x0 - 1 + g % P)) * static_cast<uint32_t>(H);
+                const int32_t t = s.top[cl[k] & 0xFFFFu];
+                uint32_t carry = 0u; // stream word 8w - 1
 #pragma unroll
-            for (int w = 0; w < NB; ++w) {
-                uint32_t bp[4], sp[4];
+                for (int w = 0; w < NB; ++w) {
+                    uint32_t bp[4], sp[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    bp[i] = parked ? park[((k * NB + w) * 4 + i) * THREADS + tid]
-                                   : (need_block && !need_sky ? cnt[k][w][i] : 0u);
-                    sp[i] = need_sky ? cnt[k][w][i] : above_mask(wb + 32 * w, t); // no dark cell: 15 above the top
+                    for (int i = 0; i < 4; ++i) {
+                        bp[i] = floods ? cnt[k][w][0][i] : 0u;
+                        sp[i] = floods ? cnt[k][w][1][i] : above_mask(wb + 32 * w, t); // no dark cell: 15 above the top
+                    }
+                    uint32_t bytes[8];
+                    planes_to_bytes(bp, sp, bytes);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        stage[lane * kW + 8 * w + q] = __funnelshift_l(q == 0 ? carry : bytes[q > 0 ? q - 1 : 0], bytes[q], sh);
+                    carry = bytes[7];
                 }
-                uint32_t bn[4], sn[4];
-                level_nibbles(bp[0], bp[1], bp[2], bp[3], bn[0], bn[1], bn[2], bn[3]);
-                level_nibbles(sp[0], sp[1], sp[2], sp[3], sn[0], sn[1], sn[2], sn[3]);
-                // nibble q of n_i = level of row 4q + i of the word.
-                uint32_t out[9];
-                out[0] = carry;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    uint32_t word = 0u;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        word |= (((bn[i] >> (4 * q)) & 15u) | (((sn[i] >> (4 * q)) & 15u) << 4)) << (8 * i);
-                    out[q + 1] = word;
-                }
-                carry = out[8];
-#pragma unroll
-                for (int q = 0; q <= 8; ++q) {
-                    if (q == 8 && w + 1 < NB)
-                        break; // memory word 8(w + 1) is stored with the next stream word
-                    const int j = 8 * w + q;
+                stage[lane * kW + 8 * NB] = __funnelshift_l(carry, 0u, sh);
+            }
+            __syncwarp();
+            const int dbase = (tid & ~31) + k * THREADS; // slot of lane 0's column
+            int c = lane / nw, jj = lane - c * nw;
+            for (int p = lane; p < 32 * nw; p += 32) {
+                const int d = dbase + c;
+                if (d < n_act) {
+                    const int j = jlo + jj;
+                    const uint32_t word = stage[c * kW + j];
+                    uint8_t* lc = light + colbase[c];
                     const int32_t r = A + 4 * j; // rows r .. r + 3
                     const int32_t lo = max(r, y0), hi = min(r + 3, y0 + ny - 1);
-                    if (lo > hi)
-                        continue;
-                    const uint32_t word = __funnelshift_l(out[q], q < 8 ? out[q + 1] : 0u, sh);
                     if (lo == r && hi == r + 3) {
                         *reinterpret_cast<uint32_t*>(lc + r) = word;
                     } else {
@@ -798,26 +854,33 @@ __global__ void __launch_bounds__(THREADS, RegionClass<THREADS, NB>::kCtasPerSm)
                             lc[y] = static_cast<uint8_t>(word >> (8 * (y - r)));
                     }
                 }
+                c += rq;
+                jj += rr;
+                if (jj >= nw) {
+                    jj -= nw;
+                    ++c;
+                }
             }
+            __syncwarp(); // the staging area is refilled for the next column
         }
-        __syncthreads(); // shared planes and counters are reused by the next region
+        cp_async_wait_all(); // the next region's centres
+        __syncthreads();     // shared planes and counters are reused by the next region
     }
 }
 
-template <int THREADS, int NB>
+template <int THREADS, int CPT, int NB>
 int launch_region_list(blk_ctx* ctx, const RegionRelightArgs& base, int list, cudaStream_t st)
 {
-    using K = RegionClass<THREADS, NB>;
+    using K = RegionClass<THREADS, CPT, NB>;
     static bool attr_set[64] = {};
     const int dev = ctx->device;
-    constexpr size_t kSmem = sizeof(RegionSmem<THREADS, NB>);
-    static_assert(K::kCtasPerSm * K::kParkWords <= 32768, "park slice per SM");
+    constexpr size_t kSmem = sizeof(RegionSmem<THREADS, CPT, NB>);
     if (dev < 0 || dev >= 64) {
         set_error("device index out of range");
         return BLK_ERR_INVALID_ARGUMENT;
     }
     if (!attr_set[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(relight_region_kernel<THREADS, NB>,
+        const cudaError_t e = cudaFuncSetAttribute(relight_region_kernel<THREADS, CPT, NB>,
             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
         if (e != cudaSuccess)
             return cuda_fail(e, "cudaFuncSetAttribute(relight_region_kernel)");
@@ -826,9 +889,8 @@ int launch_region_list(blk_ctx* ctx, const RegionRelightArgs& base, int list, cu
     RegionRelightArgs a = base;
     a.regions = ctx->region_lists + 2ull * list * ctx->region_capacity;
     a.count = ctx->region_counts + list;
-    a.park = ctx->region_park + static_cast<uint64_t>(list) * ctx->park_ctas * region_park_words_per_sm();
     const unsigned grid = ctx->park_ctas * K::kCtasPerSm;
-    relight_region_kernel<THREADS, NB><<<grid, THREADS, kSmem, st>>>(a);
+    relight_region_kernel<THREADS, CPT, NB><<<grid, THREADS, kSmem, st>>>(a);
     return cuda_fail(cudaGetLastError(), "relight_region_kernel launch");
 }
 
@@ -846,10 +908,6 @@ __global__ void dirty_compact_kernel(const uint32_t* win_lo, const uint32_t* win
 }
 
 } // namespace
-
-// Scratch words one region kernel needs per SM (block counters parked during
-// a sky flood); every size class fits in it, and each class has its own area.
-uint64_t region_park_words_per_sm() { return 32768; }
 
 // The relight of an edit step, after mark_changes_kernel: regions per env,
 // the tile path's dirty tiles (regions beyond the region kernels' limits),
@@ -926,23 +984,22 @@ int launch_region_relight(blk_ctx* ctx, const cudaStream_t (&side)[kRegionLists]
     a.columns = ctx->columns_per_env;
     a.capacity = ctx->region_capacity;
     a.centres = ctx->region_centres;
-    a.park = ctx->region_park;
     a.flags = ctx->flags;
     // Size classes (lists of region_build_kernel), each on its own stream so
     // that their tails overlap: list 2 s + nb - 1 holds regions of nb words
-    // solved by CTAs of 256 << s threads (at most 512 << s solved and 256 << s
-    // ring columns); the largest first.
-    int rc = launch_region_list<1024, 2>(ctx, a, 5, side[5]);
+    // solved by CTAs of 512 x 1, 1024 x 1 and 1024 x 2 columns (threads x
+    // columns per thread); the largest first.
+    int rc = launch_region_list<1024, 2, 2>(ctx, a, 5, side[5]);
     if (rc == BLK_OK)
-        rc = launch_region_list<1024, 1>(ctx, a, 4, side[4]);
+        rc = launch_region_list<1024, 2, 1>(ctx, a, 4, side[4]);
     if (rc == BLK_OK)
-        rc = launch_region_list<512, 2>(ctx, a, 3, side[3]);
+        rc = launch_region_list<1024, 1, 2>(ctx, a, 3, side[3]);
     if (rc == BLK_OK)
-        rc = launch_region_list<512, 1>(ctx, a, 2, side[2]);
+        rc = launch_region_list<1024, 1, 1>(ctx, a, 2, side[2]);
     if (rc == BLK_OK)
-        rc = launch_region_list<256, 2>(ctx, a, 1, side[1]);
+        rc = launch_region_list<512, 1, 2>(ctx, a, 1, side[1]);
     if (rc == BLK_OK)
-        rc = launch_region_list<256, 1>(ctx, a, 0, side[0]);
+        rc = launch_region_list<512, 1, 1>(ctx, a, 0, side[0]);
     return rc;
 }
 
