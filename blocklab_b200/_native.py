@@ -119,6 +119,8 @@ SIGNATURES = {
     "blk_render_frames": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _UP]),
     "blk_generate_envs": (ctypes.c_int, [_VP, _VP, _U32, _VP, _VP, _VP, _U32, _UP]),
     "blk_render_observations": (ctypes.c_int, [_VP, _VP, _U32, _U32, _VP, _VP, _UP]),
+    "blk_set_generation_path": (ctypes.c_int, [_VP, ctypes.c_int]),
+    "blk_generation_fallback_tiles": (ctypes.c_int, [_VP, _VP]),
 }
 
 

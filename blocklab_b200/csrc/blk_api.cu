@@ -970,6 +970,8 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->dirty_window, 2 * n_tiles, "dirty windows"));
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
+    A(dalloc(&ctx->fallback_list, n_tiles, "generation fallback tiles"));
+    A(dalloc(&ctx->fallback_count, 1, "generation fallback count"));
     ctx->box_capacity = 2 * std::max<uint32_t>(c.max_edits, 1);
     ctx->region_capacity = ctx->box_capacity; // every item holds a marked change
     A(dalloc(&ctx->region_lists, 2ull * kRegionLists * ctx->region_capacity, "relight region lists"));
@@ -1027,7 +1029,9 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     if (rc == BLK_OK)
         rc = cuda_fail(cudaMemset(ctx->hmap, 0, envs * ctx->columns_per_env * sizeof(int16_t)), "cudaMemset hmap");
     if (rc == BLK_OK)
-        rc = launch_tiles(ctx, 0, 0, 0); // sets the kernel's shared-memory attribute
+        rc = launch_tiles(ctx, 0, 0, 0); // sets the kernels' shared-memory attributes
+    if (rc == BLK_OK)
+        rc = launch_generation(ctx, 0, 0);
     if (rc == BLK_OK)
         rc = cuda_fail(cudaDeviceSynchronize(), "context setup");
     if (rc != BLK_OK) {
@@ -1057,7 +1061,7 @@ int blk_ctx_destroy(blk_ctx* ctx)
         cudaEventDestroy(ctx->relight_fork);
     void* bufs[] = { ctx->ids, ctx->light, ctx->hmap, ctx->seeds, ctx->origins, ctx->origin_stage, ctx->terrain_top, ctx->halo_order, ctx->ovr, ctx->col_count, ctx->col_offset,
         ctx->entries, ctx->ovr_owner, ctx->scan_partials, ctx->edits, ctx->edit_env_count, ctx->edit_env_offset, ctx->edit_order, ctx->edit_changes,
-        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->region_lists, ctx->region_centres, ctx->region_counts, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
+        ctx->dirty_window, ctx->dirty_list, ctx->dirty_count, ctx->fallback_list, ctx->fallback_count, ctx->region_lists, ctx->region_centres, ctx->region_counts, ctx->render_params, ctx->col_summary, ctx->env_mask, ctx->env_list, ctx->seed_list, ctx->flags, ctx->park };
     for (void* b : bufs)
         if (b)
             cudaFree(b);
@@ -1136,7 +1140,7 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const int32_t* env_ori
     const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;
     BLK_CHECK(launch_surface(ctx, st));
     prof_mark(ctx, mark, 1, st);
-    BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_tiles), st));
+    BLK_CHECK(launch_generation(ctx, static_cast<uint32_t>(n_tiles), st));
     prof_mark(ctx, mark, 2, st);
     ctx->generated = true;
     return BLK_OK;
@@ -1194,7 +1198,7 @@ int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, co
     }
     BLK_CHECK(launch_surface(ctx, st, ctx->env_mask));
     prof_mark(ctx, mark, 1, st);
-    BLK_CHECK(launch_tiles(ctx, 0, static_cast<uint32_t>(n_items), st, true));
+    BLK_CHECK(launch_generation(ctx, static_cast<uint32_t>(n_items), st, true));
     prof_mark(ctx, mark, 2, st);
     return BLK_OK;
 }
@@ -1589,6 +1593,32 @@ int blk_sync(blk_ctx* ctx, uintptr_t stream_handle)
         set_error(msg);
         return BLK_ERR_DEVICE_FLAG;
     }
+    return BLK_OK;
+}
+
+int blk_set_generation_path(blk_ctx* ctx, int path)
+{
+    if (!ctx || (path != BLK_GENERATION_SURFACE && path != BLK_GENERATION_TILES)) {
+        set_error("blk_set_generation_path: null context or unknown path");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    ctx->generation_path = path;
+    return BLK_OK;
+}
+
+int blk_generation_fallback_tiles(blk_ctx* ctx, uint32_t* count)
+{
+    if (!ctx || !count) {
+        set_error("blk_generation_fallback_tiles: null argument");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (ctx->generation_path != BLK_GENERATION_SURFACE) {
+        *count = 0;
+        return BLK_OK;
+    }
+    BLK_CUDA(cudaDeviceSynchronize(), "device synchronize");
+    BLK_CUDA(cudaMemcpy(count, ctx->fallback_count, sizeof(uint32_t), cudaMemcpyDeviceToHost), "fallback count read");
     return BLK_OK;
 }
 

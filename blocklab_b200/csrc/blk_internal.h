@@ -65,6 +65,11 @@ struct blk_ctx {
     uint32_t box_capacity = 0;            // 2 * max_edits (an edit changes at most two cells)
     uint32_t* h_dirty_count = nullptr;    // pinned [1]
 
+    // Generation: the surface kernel's tiles left to the tile kernel.
+    uint32_t* fallback_list = nullptr;    // [num_envs * tiles] tile ids
+    uint32_t* fallback_count = nullptr;   // [1]
+    int generation_path = BLK_GENERATION_SURFACE;
+
     uint32_t* park = nullptr;             // tile-kernel scratch: 16 words x 1024 threads per CTA
     uint32_t park_ctas = 0;
     blk_render_params* render_params = nullptr; // [num_envs] staging of host-resident render parameters
@@ -135,6 +140,9 @@ int launch_column_summary(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_
 int launch_surface(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask = nullptr);
 // Mode 0 over a tile list (ctx->dirty_list, n_tiles entries, 0xFFFFFFFF = skip) when `listed`.
 int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed = false);
+// Generation of all tiles (or the listed ones) on ctx->generation_path: the
+// surface kernel, then the tile kernel over the tiles it left.
+int launch_generation(blk_ctx* ctx, uint32_t n_tiles, cudaStream_t stream, bool listed = false);
 int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,
     float* out_nchw, cudaStream_t stream);
 void halo_order_table(uint16_t* out);

@@ -84,6 +84,9 @@ struct TileArgs {
     uint64_t columns;
     int32_t mode; // 0 = generate, 1 = relight dirty tiles from the resident ids
     int32_t listed; // mode 0: tiles from dirty_list (0xFFFFFFFF = skip) instead of all
+    const uint32_t* list_count;     // mode 0 listed: device-side entry count of dirty_list (else n_tiles)
+    uint32_t* fallback_list;        // surface kernel: tiles it leaves to the tile kernel
+    uint32_t* fallback_count;
 };
 
 // Rows a tile lights (see plan_tile in process_tile).
@@ -117,6 +120,7 @@ struct Smem {
     int32_t omin;              // generation: lowest open row of the ext region (rows below are opaque everywhere)
     TilePlan plan;             // the tile's plan, computed once per tile by thread 0
 
+    __device__ int32_t terrain_top(int c) const { return top_t[c]; }
     __device__ uint32_t* O() { return pool; }
     __device__ uint32_t* B(int i) { return pool + (1 + i) * kPlane; }
 };
@@ -223,6 +227,144 @@ __device__ inline void id_bits(const uint4 (&v)[2], uint32_t& open, uint32_t& to
             open |= pack4_hi(zero_bytes(w[j] & 0xFBFBFBFBu)) << (16 * q + 4 * j);
             torch |= pack4_hi(zero_bytes(w[j] ^ 0x04040404u)) << (16 * q + 4 * j);
         }
+    }
+}
+
+// ---- pieces shared by the tile kernel and the surface kernel ---------------
+// SM is a tile's shared-memory layout: output staging in `pool` (kPitch bytes
+// per column, kStageWarps warps at a time, kRounds rounds), and per ext column
+// the final top top_f and the packed override list ovr (begin << 5 |
+// min(count, 31), or kOvrInline | y << 8 | block); terrain_top(c) is the
+// terrain surface of ext column c.
+
+// Calls fn(y, block) for the winning override of every y of ext column c whose
+// y lies in [ylo, yhi] (entries sorted by y, then input order; the last of a y
+// run wins).
+template <class SM, class Fn>
+__device__ inline void ext_for_each_winner(const TileArgs& a, const SM& s, int c, int x0, int z0, uint64_t env_col0,
+    int32_t ylo, int32_t yhi, Fn&& fn)
+{
+    const uint32_t packed = s.ovr[c];
+    if (packed & kOvrInline) {
+        const int32_t y = static_cast<int32_t>((packed >> 8) & 0x1FFu);
+        if (y >= ylo && y <= yhi)
+            fn(y, static_cast<uint8_t>(packed & 0xFFu));
+        return;
+    }
+    uint32_t n = packed & kCntSat;
+    uint32_t beg = packed >> 5;
+    if (n == kCntSat) {
+        // Long list: reread its bounds.
+        const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
+        const uint64_t col = env_col0 + static_cast<uint64_t>(gz) * a.W + gx;
+        beg = __ldg(a.col_offset + col);
+        n = __ldg(a.col_offset + col + 1) - beg;
+    }
+    const uint64_t* e = a.entries + beg;
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint64_t v = __ldg(e + i);
+        const int32_t y = static_cast<int32_t>(entry_y(v));
+        if (y < ylo || y > yhi)
+            continue;
+        if (i + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + i + 1))) == y)
+            continue;
+        fn(y, entry_block(v));
+    }
+}
+
+// Output staging: each warp owns one z row of 32 columns, contiguous in
+// memory. A lane builds its column's bytes in its staging column, then the
+// warp stores the row with coalesced 16-byte stores.
+template <class SM>
+__device__ inline uint8_t* stage_column(SM& s)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    return reinterpret_cast<uint8_t*>(s.pool) + (warp % SM::kStageWarps) * (kTile * SM::kPitch) + lane * SM::kPitch;
+}
+
+// Copies the warp's staged 16-row chunks selected by `mask` (bit ch = rows
+// 16ch..) of its 32 columns to dst (the row's first column).
+template <int H, class SM>
+__device__ inline void copy_staged(const TileArgs& a, const SM& s, int x0, uint8_t* dst, uint32_t mask)
+{
+    constexpr int kChunks = H / 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint8_t* stage = reinterpret_cast<const uint8_t*>(s.pool) + (warp % SM::kStageWarps) * (kTile * SM::kPitch);
+    const int ncols = min(kTile, a.W - x0);
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+        const int idx = i * 32 + lane;
+        const int col = idx / kChunks, ch = idx - col * kChunks;
+        if (col < ncols && ((mask >> ch) & 1u))
+            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(col) * H + ch * 16)
+                = *reinterpret_cast<const uint4*>(stage + col * SM::kPitch + ch * 16);
+    }
+}
+
+// One 16-row chunk of trivial light bytes: sky 15 above the final top topf,
+// 0 at or below it, no block light.
+__device__ inline void stage_trivial_chunk(uint8_t* my, int32_t topf, int r0)
+{
+    uint32_t wv[4];
+    // Bytes of rows at or below topf keep sky 0: shift by 8 bits per such row
+    // of the word (the funnel shift clamps at 32).
+    const int32_t t8 = 8 * (topf - r0 + 1);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        wv[q] = __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(max(t8 - 32 * q, 0)));
+    *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+}
+
+// Generation: block ids (layer rule, then the winning overrides) and the height
+// map of the tile's 32 x 32 columns; c0 = this thread's interior ext column.
+template <int NW, class SM>
+__device__ void ids_pass(const TileArgs& a, SM& s, uint32_t env, int x0, int z0, int c0, int32_t origin_y)
+{
+    constexpr int H = 32 * NW;
+    constexpr int kChunks = H / 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t env_col0 = static_cast<uint64_t>(env) * a.columns;
+    uint8_t* env_ids = a.ids + static_cast<uint64_t>(env) * a.env_stride;
+    for (int round = 0; round < SM::kRounds; ++round) {
+        __syncthreads();
+        if (warp / SM::kStageWarps != round)
+            continue;
+        const int gx = x0 + lane, gz = z0 + warp;
+        if (in_world(a, gx, gz)) {
+            const int32_t top = s.terrain_top(c0);
+            uint8_t* my = stage_column(s);
+            a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(s.top_f[c0] + origin_y);
+            // Layer rule: id = [y <= top] + [y <= top-1] + [y <= top-4]
+            // = 3 - (number of those thresholds below y). U(t) holds 0x01 in
+            // the bytes of a 4-row word whose row is above t: 0x01010101
+            // shifted by 8 bits per row at or below t (clamped at 32).
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch) {
+                const int r0 = ch * 16;
+                uint32_t wv[4];
+                if (r0 > top) {
+                    wv[0] = wv[1] = wv[2] = wv[3] = 0u;
+                } else if (r0 + 15 <= top - 4) {
+                    wv[0] = wv[1] = wv[2] = wv[3] = 0x03030303u;
+                } else {
+                    const int32_t a0 = 8 * (top - r0 + 1);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int32_t sh = a0 - 32 * q;
+                        wv[q] = 0x03030303u - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(sh, 0)))
+                            - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(sh - 8, 0)))
+                            - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(sh - 32, 0)));
+                    }
+                }
+                *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+            // Winning overrides (latest of each y) replace the terrain bytes.
+            if ((s.ovr[c0] & (kOvrInline | kCntSat)) != 0u)
+                ext_for_each_winner(a, s, c0, x0, z0, env_col0, 0, H - 1, [&](int32_t y, uint8_t b) { my[y] = b; });
+        }
+        __syncwarp();
+        if (z0 + warp < a.D)
+            copy_staged<H>(a, s, x0, env_ids + (static_cast<uint64_t>(z0 + warp) * a.W + x0) * H, 0xFFFFFFFFu);
     }
 }
 
@@ -439,44 +581,10 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
         }
     }
 
-    // Override list of ext column c: pointer and count.
-    auto overrides_of = [&](int c, const uint64_t*& e, uint32_t& n) {
-        const uint32_t packed = s.ovr[c];
-        n = packed & kCntSat;
-        uint32_t beg = packed >> 5;
-        if (n == kCntSat) {
-            // Long list: reread its bounds.
-            const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
-            const uint64_t col = env_col0 + static_cast<uint64_t>(gz) * a.W + gx;
-            beg = __ldg(a.col_offset + col);
-            n = __ldg(a.col_offset + col + 1) - beg;
-        }
-        e = a.entries + beg;
-    };
-
     // Calls fn(y, block) for the winning override of every y of ext column c
-    // whose y lies in [ylo, yhi] (entries sorted by y, then input order; the
-    // last of a y run wins).
+    // whose y lies in [ylo, yhi].
     auto for_each_winner = [&](int c, int32_t ylo, int32_t yhi, auto&& fn) {
-        const uint32_t packed = s.ovr[c];
-        if (packed & kOvrInline) {
-            const int32_t y = static_cast<int32_t>((packed >> 8) & 0x1FFu);
-            if (y >= ylo && y <= yhi)
-                fn(y, static_cast<uint8_t>(packed & 0xFFu));
-            return;
-        }
-        const uint64_t* e;
-        uint32_t n;
-        overrides_of(c, e, n);
-        for (uint32_t i = 0; i < n; ++i) {
-            const uint64_t v = __ldg(e + i);
-            const int32_t y = static_cast<int32_t>(entry_y(v));
-            if (y < ylo || y > yhi)
-                continue;
-            if (i + 1 < n && static_cast<int32_t>(entry_y(__ldg(e + i + 1))) == y)
-                continue;
-            fn(y, entry_block(v));
-        }
+        ext_for_each_winner(a, s, c, x0, z0, env_col0, ylo, yhi, fn);
     };
 
     // Generation: open-cell and source bits of ext column c for the 32 rows
@@ -580,43 +688,15 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     // stage at once up to H = 160, half of them per round above. The helpers
     // derive everything from tid, the tile
     // origin and shared memory, so nothing of theirs stays live across a flood.
-    constexpr int kPitch = Smem<NW>::kPitch;
     constexpr int kChunks = H / 16;
     constexpr int KB = Smem<NW>::kBand;
     // Output rows of one window when a tile needs several: with margins of 16
     // rows below and 14 above they fill KB words.
     constexpr int kWinRows = ((32 * KB - 30) / 16) * 16;
-    auto stage_of = [&]() {
-        return reinterpret_cast<uint8_t*>(s.pool) + (warp % Smem<NW>::kStageWarps) * (kTile * kPitch) + lane * kPitch;
-    };
+    auto stage_of = [&]() { return stage_column(s); };
     auto row_offset = [&]() { return (static_cast<uint64_t>(z0 + warp) * a.W + x0) * H; };
-
-    // Copies the staged 16-row chunks selected by `mask` (bit ch = rows 16ch..).
-    auto copy_out = [&](uint8_t* dst, uint32_t mask) {
-        const uint8_t* stage = reinterpret_cast<const uint8_t*>(s.pool) + (warp % Smem<NW>::kStageWarps) * (kTile * kPitch);
-        const int ncols = min(kTile, a.W - x0);
-#pragma unroll
-        for (int i = 0; i < kChunks; ++i) {
-            const int idx = i * 32 + lane;
-            const int col = idx / kChunks, ch = idx - col * kChunks;
-            if (col < ncols && ((mask >> ch) & 1u))
-                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(col) * H + ch * 16)
-                    = *reinterpret_cast<const uint4*>(stage + col * kPitch + ch * 16);
-        }
-    };
-
-    // One 16-row chunk of light bytes: block bits, sky bits for the chunk rows
-    // in sky_rows, trivial sky light (15 above the final top) elsewhere.
-    auto emit_trivial = [&](uint8_t* my, int32_t topf, int r0) {
-        uint32_t wv[4];
-        // Bytes of rows at or below topf keep sky 0: shift by 8 bits per such
-        // row of the word (the funnel shift clamps at 32).
-        const int32_t t8 = 8 * (topf - r0 + 1);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            wv[q] = __funnelshift_lc(0u, 0xF0F0F0F0u, static_cast<uint32_t>(max(t8 - 32 * q, 0)));
-        *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    };
+    auto copy_out = [&](uint8_t* dst, uint32_t mask) { copy_staged<H>(a, s, x0, dst, mask); };
+    auto emit_trivial = [&](uint8_t* my, int32_t topf, int r0) { stage_trivial_chunk(my, topf, r0); };
     // One band word (32 rows from r0): block levels from b, sky levels from s
     // (sky) or trivial; writes the 16-row halves selected by lo_on / hi_on.
     auto emit_word = [&](uint8_t* my, int32_t topf, int r0, const uint32_t (&b)[4], const uint32_t (&sv)[4], bool sky,
@@ -630,50 +710,8 @@ __device__ void process_tile(const TileArgs& a, Smem<NW>& s, uint32_t env, int x
     };
 
     // ---- block ids and height map (generation) -------------------------------
-    if (MODE == 0) {
-        for (int round = 0; round < Smem<NW>::kRounds; ++round) {
-            __syncthreads();
-            if (warp / Smem<NW>::kStageWarps != round)
-                continue;
-            const int gx = x0 + lane, gz = z0 + warp;
-            if (in_world(a, gx, gz)) {
-                const int c0 = slot[0];
-                const int32_t top = s.top_t[c0];
-                uint8_t* my = stage_of();
-                a.hmap[env_col0 + static_cast<uint64_t>(gz) * a.W + gx] = static_cast<int16_t>(s.top_f[c0] + origin_y);
-                // Layer rule: id = [y <= top] + [y <= top-1] + [y <= top-4]
-                // = 3 - (number of those thresholds below y). U(t) holds 0x01 in
-                // the bytes of a 4-row word whose row is above t: 0x01010101
-                // shifted by 8 bits per row at or below t (clamped at 32).
-#pragma unroll
-                for (int ch = 0; ch < kChunks; ++ch) {
-                    const int r0 = ch * 16;
-                    uint32_t wv[4];
-                    if (r0 > top) {
-                        wv[0] = wv[1] = wv[2] = wv[3] = 0u;
-                    } else if (r0 + 15 <= top - 4) {
-                        wv[0] = wv[1] = wv[2] = wv[3] = 0x03030303u;
-                    } else {
-                        const int32_t a0 = 8 * (top - r0 + 1);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const int32_t a = a0 - 32 * q;
-                            wv[q] = 0x03030303u - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(a, 0)))
-                                - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(a - 8, 0)))
-                                - __funnelshift_lc(0u, 0x01010101u, static_cast<uint32_t>(max(a - 32, 0)));
-                        }
-                    }
-                    *reinterpret_cast<uint4*>(my + r0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-                }
-                // Winning overrides (latest of each y) replace the terrain bytes.
-                if ((s.ovr[c0] & (kOvrInline | kCntSat)) != 0u)
-                    for_each_winner(c0, 0, H - 1, [&](int32_t y, uint8_t b) { my[y] = b; });
-            }
-            __syncwarp();
-            if (z0 + warp < a.D)
-                copy_out(env_ids + row_offset(), 0xFFFFFFFFu);
-        }
-    }
+    if (MODE == 0)
+        ids_pass<NW>(a, s, env, x0, z0, slot[0], origin_y);
 
     // ---- light: rows that can hold non-trivial light ---------------------------
     // Block band: torch rows +-14; sky band: rows of dark open cells +-14.
@@ -919,7 +957,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
     Smem<NW>& s = *reinterpret_cast<Smem<NW>*>(smem_raw);
     // Relight works on the dirty tiles (regions too large for the region
     // kernels). Every CTA reads the same count.
-    const uint32_t n = MODE != 0 ? *a.dirty_count : a.n_tiles;
+    const uint32_t n = MODE != 0 ? *a.dirty_count : (a.list_count ? *a.list_count : a.n_tiles);
     const uint32_t tiles_per_env = static_cast<uint32_t>(a.tiles_x * a.tiles_z);
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
         int32_t wlo_rows = 0, whi_rows = 32 * NW - 1;
@@ -938,6 +976,309 @@ __global__ void __launch_bounds__(kThreads, 1) tile_kernel(TileArgs a)
             whi_rows = min(static_cast<int32_t>(win >> 16) | 15, 32 * NW - 1);
         }
         process_tile<NW, MODE>(a, s, env, x0, z0, wlo_rows, whi_rows);
+        __syncthreads();
+    }
+}
+
+// ---- surface kernel: generation with one light word per column ---------------
+//
+// On terrain worlds the open cells of a column are the rows above its final
+// top, and block light reaches at most 14 rows above a torch, less its
+// horizontal distance; torches stand on the surface. So the rows of a column
+// that can hold block light start at its own first open row b = top_f + 1 and
+// span far fewer than 32 rows (the benchmark's reset worlds: at most 29, 11 on
+// average), while one band over the 60 x 60 ext columns of varied terrain needs
+// two or three 32-row words. This kernel floods ONE word per column, based at
+// that column's own first open row. A column's word is kept in its 64-bit plane
+// entry at bit offset 16 (lo = w << 16, hi = w >> 16); the rows [b, b + 31] of a
+// neighbour with first open row b_n are that entry shifted right by
+// 16 - (b_n - b), one funnel shift, for |b_n - b| <= 16.
+//
+// Exactness. The word flood is the exact flood of the world in which every
+// open cell above its column's word is made opaque ("truncated"). That world
+// has the real world's light if no truncated cell is lit in the real world,
+// and that holds if no cell next to a truncated cell is lit in the word flood:
+// its light is then a solution of the real world's equation, whose solution is
+// unique. The cells next to truncated ones are the top bits of a word: bit 31
+// (the cell above) and bits >= 32 + (b_n - b) for a neighbour whose word ends
+// lower. After the flood every column of the cone tests its level set against
+// those bits (a halo column at cone distance d ends with S_{1+d}, which holds
+// every cell a path into the interior can use there: a path that enters a
+// truncated cell x at cone distance d_x came through a neighbour of level
+// >= 2 + d_x); torches of the outer ring are tested before it. A tile that
+// fails a test, or holds open cells under a column top (caves and overhangs,
+// which need the sky flood), a torch 16 or more rows above its column's first
+// open row, or neighbouring first open rows more than 16 apart, is appended to
+// fallback_list and generated by the tile kernel, which handles every world.
+
+template <int NW>
+struct SurfSmem {
+    static constexpr int kPitch = 32 * NW + 16;
+    static constexpr int kStageWarps = kWarps * kTile * kPitch <= 198 * 1024 ? kWarps : kWarps / 2;
+    static constexpr int kRounds = kWarps / kStageWarps;
+    static constexpr int kStageWords = kStageWarps * kTile * kPitch / 4;
+    static constexpr int kPoolWords = 4 * kExtCols > kStageWords ? 4 * kExtCols : kStageWords;
+    // Two planes of one uint2 entry per ext column during the flood; output
+    // staging otherwise.
+    uint32_t pool[kPoolWords];
+    uint32_t ovr[kExtCols];
+    int16_t top_f[kExtCols];
+    int16_t top_t[kTile * kTile]; // terrain surface of the interior columns
+    uint32_t flags;               // kSurfFallback | kSurfTorch
+
+    __device__ uint2* P(int i) { return reinterpret_cast<uint2*>(pool) + i * kExtCols; }
+    __device__ int32_t terrain_top(int c) const { return top_t[(c / kExt - kHalo) * kTile + c % kExt - kHalo]; }
+};
+
+constexpr uint32_t kSurfFallback = 1u; // the tile is left to the tile kernel
+constexpr uint32_t kSurfTorch = 2u;    // a torch lies in the cone
+constexpr int kSurfPad = 16;           // bit offset of a word in its plane entry; largest |b_n - b|
+
+__device__ inline uint2 surf_entry(uint32_t w) { return make_uint2(w << kSurfPad, w >> (32 - kSurfPad)); }
+// Rows [b, b + 31] of a neighbour's entry, amt = 16 - (b_n - b) in 0..32.
+__device__ inline uint32_t surf_window(uint2 e, uint32_t amt) { return __funnelshift_rc(e.x, e.y, amt); }
+
+// Generates one tile; returns false (uniformly over the CTA) when the tile must
+// be generated by the tile kernel instead (its light is then not written).
+template <int NW>
+__device__ bool process_surface_tile(const TileArgs& a, SurfSmem<NW>& s, uint32_t env, int x0, int z0)
+{
+    constexpr int H = 32 * NW;
+    constexpr int kChunks = H / 16;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const uint64_t env_col0 = static_cast<uint64_t>(env) * a.columns;
+    const int32_t origin_y = __ldg(&a.origins[env].y);
+
+    if (tid == 0)
+        s.flags = 0u;
+    // ---- column summaries and the conditions of this path -------------------
+    uint4 pa[kColIters];
+#pragma unroll
+    for (int it = 0; it < kColIters; ++it) {
+        const int c = tid + it * kThreads;
+        pa[it] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < kExtCols) {
+            const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
+            if (in_world(a, gx, gz))
+                pa[it] = __ldg(a.col_summary + env_col0 + static_cast<uint64_t>(gz) * a.W + gx);
+        }
+    }
+    __syncthreads();
+    uint32_t fl = 0u;
+#pragma unroll
+    for (int it = 0; it < kColIters; ++it) {
+        const int c = tid + it * kThreads;
+        if (c >= kExtCols)
+            break;
+        const int gx = x0 - kHalo + c % kExt, gz = z0 - kHalo + c / kExt;
+        if (!in_world(a, gx, gz)) {
+            s.top_f[c] = -2;
+            s.ovr[c] = 0;
+            continue;
+        }
+        const uint4 v = pa[it];
+        const int32_t topf = static_cast<int16_t>(v.x >> 16);
+        const int ex = c % kExt - kHalo, ez = c / kExt - kHalo;
+        if (ex >= 0 && ex < kTile && ez >= 0 && ez < kTile)
+            s.top_t[ez * kTile + ex] = static_cast<int16_t>(v.x & 0xFFFFu);
+        s.top_f[c] = static_cast<int16_t>(topf);
+        s.ovr[c] = v.y;
+        if (cone_distance(c) <= kMaxDistance) {
+            const int32_t tlo = static_cast<int16_t>(v.z & 0xFFFFu), thi = static_cast<int16_t>(v.z >> 16);
+            const int32_t dlo = static_cast<int16_t>(v.w & 0xFFFFu), dhi = static_cast<int16_t>(v.w >> 16);
+            if (dlo <= dhi)
+                fl |= kSurfFallback; // open cells under the top
+            if (tlo <= thi) {
+                fl |= kSurfTorch;
+                if (thi - (topf + 1) >= kSurfPad)
+                    fl |= kSurfFallback;
+            }
+        }
+    }
+    fl = __reduce_or_sync(0xFFFFFFFFu, fl);
+    if (lane == 0 && fl != 0u)
+        atomicOr(&s.flags, fl);
+    __syncthreads();
+    const uint32_t tf = s.flags;
+    if (tf & kSurfFallback)
+        return false;
+
+    // ---- slot ownership (as in process_tile) -----------------------------------
+    int slot[kSlots];
+    slot[0] = (kHalo + tid / kTile) * kExt + kHalo + tid % kTile;
+#pragma unroll
+    for (int k = 1; k < kSlots; ++k) {
+        const int wk = (k == 2) ? (kWarps - 1 - warp) : warp;
+        const int r = (k - 1) * kThreads + wk * 32 + lane;
+        slot[k] = kDummySlot;
+        if (r < kHaloCols) {
+            const int c = __ldg(a.halo_order + r);
+            const int d = cone_distance(c);
+            if (d < kMaxDistance)
+                slot[k] = c | (d << 16);
+        }
+    }
+
+    ids_pass<NW>(a, s, env, x0, z0, slot[0], origin_y);
+
+    // Level bit planes of the interior column's word (rows b .. b + 31).
+    uint32_t cnt[4] = { 0u, 0u, 0u, 0u };
+    if (tf & kSurfTorch) {
+        __syncthreads(); // every warp has copied its staged ids out of the pool
+        // Plane 0: the torches of every ext column (rows b .. b + 15 after the
+        // check above); plane 1: zero, so that a column updated beyond its
+        // reach reads older values of its neighbours, never stale garbage.
+        for (int c = tid; c < kExtCols; c += kThreads) {
+            const int32_t b = s.top_f[c] + 1;
+            uint32_t src = 0u;
+            if (b >= 0 && (s.ovr[c] & (kOvrInline | kCntSat)) != 0u)
+                ext_for_each_winner(a, s, c, x0, z0, env_col0, b, b + kSurfPad - 1, [&](int32_t y, uint8_t blk) {
+                    if (blk == Torch)
+                        src |= 1u << (y - b);
+                });
+            s.P(0)[c] = surf_entry(src);
+            s.P(1)[c] = make_uint2(0u, 0u);
+        }
+        __syncthreads();
+
+        // Per slot: its word, its rows inside the region and the shift amount
+        // of each neighbour (x - 1, x + 1, z - 1, z + 1).
+        uint32_t own[kSlots], inside[kSlots], amt[kSlots][4];
+        int last[kSlots];
+        bool bad = false;
+#pragma unroll
+        for (int k = 0; k < kSlots; ++k) {
+            const int c = slot[k] & 0xFFFF;
+            const int d = slot[k] >> 16;
+            const int32_t tc = s.top_f[c];
+            const int32_t b = tc + 1;
+            inside[k] = tc < -1 ? 0u : inside_mask(b, H); // 0 for b >= H too
+            own[k] = surf_window(s.P(0)[c], kSurfPad);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int32_t tn = s.top_f[c + (j == 0 ? -1 : j == 1 ? 1 : j == 2 ? -kExt : kExt)];
+                int32_t dlt = 0; // any amount for a neighbour or column without open rows
+                if (tc >= -1 && tn >= -1 && b < H && tn + 1 < H) {
+                    dlt = tn - tc;
+                    if (d < kMaxDistance && (dlt < -kSurfPad || dlt > kSurfPad))
+                        bad = true;
+                    dlt = max(-kSurfPad, min(kSurfPad, dlt));
+                }
+                amt[k][j] = static_cast<uint32_t>(kSurfPad - dlt);
+            }
+            // Last step of this slot for its warp: the nearest lane's reach.
+            last[k] = k == 0 ? kMaxDistance : kMaxDistance - __reduce_min_sync(0xFFFFFFFFu, d);
+        }
+        if (__syncthreads_or(bad))
+            return false;
+
+        cnt[0] = own[0];
+        // S_k = S_{k+1} | (open & dilate6(S_{k+1})), open = the rows of the word
+        // inside the region; the level bit planes accumulate as in flood().
+#pragma unroll
+        for (int step = 1; step <= kMaxDistance; ++step) {
+            const uint2* cur = s.P((step - 1) & 1);
+            uint2* nxt = s.P(step & 1);
+            const int level = 15 - step;
+#pragma unroll
+            for (int k = 0; k < kSlots; ++k) {
+                if (k > 0 && step > last[k])
+                    continue; // uniform over the warp
+                const int c = slot[k] & 0xFFFF;
+                const uint32_t lat = surf_window(cur[c - 1], amt[k][0]) | surf_window(cur[c + 1], amt[k][1])
+                    | surf_window(cur[c - kExt], amt[k][2]) | surf_window(cur[c + kExt], amt[k][3]);
+                const uint32_t w = own[k];
+                const uint32_t v = (w | (w << 1) | (w >> 1) | lat) & inside[k];
+                own[k] = v;
+                nxt[c] = surf_entry(v);
+                if (k == 0) {
+                    cnt[0] ^= v;
+                    if ((level & 1) == 0)
+                        cnt[1] ^= v;
+                    if ((level & 3) == 0)
+                        cnt[2] ^= v;
+                    if (level == 8)
+                        cnt[3] = v;
+                }
+            }
+            __syncthreads();
+        }
+
+        // No lit cell next to a truncated one (bits >= g: g = 32 + the lowest
+        // neighbour offset b_n - b below zero; bit 31 always).
+#pragma unroll
+        for (int k = 0; k < kSlots; ++k) {
+            if ((slot[k] >> 16) >= kMaxDistance)
+                continue; // no column
+            const uint32_t amax = max(max(amt[k][0], amt[k][1]), max(amt[k][2], amt[k][3]));
+            const uint32_t g = min(31u, 48u - amax);
+            bad |= (own[k] & (0xFFFFFFFFu << g)) != 0u;
+        }
+        if (__syncthreads_or(bad))
+            return false;
+    }
+
+    // ---- light bytes: 0 up to the final top, sky 15 above it, block levels of
+    // the word's rows -------------------------------------------------------------
+    for (int round = 0; round < SurfSmem<NW>::kRounds; ++round) {
+        __syncthreads();
+        if (warp / SurfSmem<NW>::kStageWarps != round)
+            continue;
+        const int gx = x0 + lane, gz = z0 + warp;
+        if (in_world(a, gx, gz)) {
+            uint8_t* my = stage_column(s);
+            const int32_t topf = s.top_f[slot[0]];
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch)
+                stage_trivial_chunk(my, topf, ch * 16);
+            if ((cnt[0] | cnt[1] | cnt[2] | cnt[3]) != 0u) {
+                // Rows b .. b + 31 (all open: sky 15) as bytes, written as the
+                // 4-byte words from b & ~3: rows below b keep 0, rows above
+                // b + 31 sky 15 without block light.
+                const uint32_t sky[4] = { 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu };
+                uint32_t o[8];
+                planes_to_bytes(cnt, sky, o);
+                const int32_t b = topf + 1;
+                const uint32_t sh = 8u * static_cast<uint32_t>(b & 3);
+                const int base = b & ~3;
+                uint32_t prev = 0u;
+#pragma unroll
+                for (int q = 0; q <= 8; ++q) {
+                    const uint32_t cur = q < 8 ? o[q] : 0xF0F0F0F0u;
+                    if (base + 4 * q < H)
+                        *reinterpret_cast<uint32_t*>(my + base + 4 * q) = __funnelshift_l(prev, cur, sh);
+                    prev = cur;
+                }
+            }
+        }
+        __syncwarp();
+        if (gz < a.D)
+            copy_staged<H>(a, s, x0,
+                a.light + static_cast<uint64_t>(env) * a.env_stride + (static_cast<uint64_t>(gz) * a.W + x0) * H,
+                0xFFFFFFFFu);
+    }
+    return true;
+}
+
+// Persistent: one CTA per SM walks the tiles (all, or the listed ones).
+template <int NW>
+__global__ void __launch_bounds__(kThreads, 1) surface_kernel(TileArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    SurfSmem<NW>& s = *reinterpret_cast<SurfSmem<NW>*>(smem_raw);
+    const uint32_t tiles_per_env = static_cast<uint32_t>(a.tiles_x * a.tiles_z);
+    for (uint32_t i = blockIdx.x; i < a.n_tiles; i += gridDim.x) {
+        const uint32_t tile_id = a.listed ? a.dirty_list[i] : i;
+        if (tile_id == 0xFFFFFFFFu)
+            continue; // uniform over the CTA
+        const uint32_t env = tile_id / tiles_per_env;
+        const uint32_t t_in_env = tile_id % tiles_per_env;
+        const int x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
+        const int z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
+        const bool done = process_surface_tile<NW>(a, s, env, x0, z0);
+        if (!done && threadIdx.x == 0)
+            a.fallback_list[atomicAdd(a.fallback_count, 1u)] = tile_id;
         __syncthreads();
     }
 }
@@ -1009,20 +1350,31 @@ __device__ inline uint4 summarize_column(int32_t top, uint64_t col, const uint32
             break;
         }
         topf = max(hi_opaque, yt);
-        // Open cells below the final top: non-opaque overrides there, and
-        // terrain air between the terrain surface and a higher opaque override.
+        // Open cells below the final top: non-opaque overrides there, and the
+        // rows of terrain air between the terrain surface and the final top
+        // that no opaque override fills (r: the next row above the surface not
+        // yet known to be filled, walking the winners upwards).
+        int32_t r = tc + 1;
         for (uint32_t k = 0; k < n; ++k) {
             const uint64_t v = e[k];
             const int32_t y = static_cast<int32_t>(entry_y(v));
             if (k + 1 < n && static_cast<int32_t>(entry_y(e[k + 1])) == y)
                 continue;
-            if (!is_opaque(entry_block(v)) && y < topf) {
+            const bool opaque = is_opaque(entry_block(v));
+            if (!opaque && y < topf) {
                 dlo = min(dlo, y);
                 dhi = max(dhi, y);
             }
+            if (opaque && y >= r && y < topf) {
+                if (y > r) {
+                    dlo = min(dlo, r);
+                    dhi = max(dhi, y - 1);
+                }
+                r = y + 1;
+            }
         }
-        if (tc + 1 < topf) {
-            dlo = min(dlo, tc + 1);
+        if (r < topf) {
+            dlo = min(dlo, r);
             dhi = max(dhi, topf - 1);
         }
     }
@@ -1135,6 +1487,33 @@ int launch_mode(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t 
     return cuda_fail(cudaGetLastError(), "tile_kernel launch");
 }
 
+template <int NW>
+int launch_surface_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
+{
+    static bool attr_set[64] = {};
+    static int sm_count[64] = {};
+    const int dev = ctx->device;
+    if (dev < 0 || dev >= 64) {
+        set_error("device index out of range");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(surface_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            static_cast<int>(sizeof(SurfSmem<NW>)));
+        if (e != cudaSuccess)
+            return cuda_fail(e, "cudaFuncSetAttribute(surface_kernel)");
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute(multiprocessor count)");
+        attr_set[dev] = true;
+    }
+    if (n_tiles == 0)
+        return BLK_OK;
+    uint32_t grid = n_tiles < static_cast<uint32_t>(sm_count[dev]) ? n_tiles : static_cast<uint32_t>(sm_count[dev]);
+    surface_kernel<NW><<<grid, kThreads, sizeof(SurfSmem<NW>), stream>>>(a);
+    return cuda_fail(cudaGetLastError(), "surface_kernel launch");
+}
+
 // Generation and relight are separate kernels: each gets the registers of its
 // own code path.
 template <int NW>
@@ -1149,8 +1528,35 @@ int launch_nw(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t st
 // cone distance first, 32 at a time (one warp), each group of 32 using 32
 // distinct shared-memory banks (ext column index mod 32) so that a warp's
 // plane accesses, and those of its +-1 / +-60 neighbours, are conflict-free.
+// Within a group, each half-warp holds distinct columns mod 16, so that the
+// surface kernel's 8-byte plane entries (served a half-warp at a time) are
+// conflict-free too.
 void halo_order_table(uint16_t* out)
 {
+    // Lanes of one group: the two columns of a residue mod 16 go to different
+    // halves; residues with one column fill the emptier half.
+    auto place = [&](const std::vector<int>& grp, int at) {
+        std::vector<int> half[2];
+        std::vector<int> by_res[16];
+        for (int c : grp)
+            by_res[c & 15].push_back(c);
+        for (int r = 0; r < 16; ++r) {
+            for (int c : by_res[r]) {
+                const bool has0 = std::any_of(half[0].begin(), half[0].end(), [&](int x) { return (x & 15) == r; });
+                const bool has1 = std::any_of(half[1].begin(), half[1].end(), [&](int x) { return (x & 15) == r; });
+                int h = half[0].size() <= half[1].size() ? 0 : 1;
+                if ((h == 0 && has0 && !has1) || (h == 1 && has1 && !has0))
+                    h ^= 1;
+                if (half[h].size() >= 16)
+                    h ^= 1;
+                half[h].push_back(c);
+            }
+        }
+        int n = at;
+        for (int h = 0; h < 2; ++h)
+            for (int c : half[h])
+                out[n++] = static_cast<uint16_t>(c);
+    };
     std::vector<int> rest;
     for (int d = 1; d <= 2 * kHalo; ++d)
         for (int c = 0; c < kExtCols; ++c) {
@@ -1165,8 +1571,8 @@ void halo_order_table(uint16_t* out)
     size_t first = 0;
     while (n < kHaloCols) {
         uint32_t banks = 0;
-        int got = 0;
-        for (size_t i = first; i < rest.size() && got < 32; ++i) {
+        std::vector<int> grp;
+        for (size_t i = first; i < rest.size() && grp.size() < 32; ++i) {
             if (taken[i])
                 continue;
             const uint32_t bit = 1u << (rest[i] & 31);
@@ -1174,17 +1580,17 @@ void halo_order_table(uint16_t* out)
                 continue;
             banks |= bit;
             taken[i] = 1;
-            out[n++] = static_cast<uint16_t>(rest[i]);
-            ++got;
+            grp.push_back(rest[i]);
         }
-        for (size_t i = first; i < rest.size() && got < 32; ++i) // fewer than 32 banks left
+        for (size_t i = first; i < rest.size() && grp.size() < 32; ++i) // fewer than 32 banks left
             if (!taken[i]) {
                 taken[i] = 1;
-                out[n++] = static_cast<uint16_t>(rest[i]);
-                ++got;
+                grp.push_back(rest[i]);
             }
         while (first < rest.size() && taken[first])
             ++first;
+        place(grp, n);
+        n += static_cast<int>(grp.size());
     }
 }
 
@@ -1251,7 +1657,9 @@ int launch_surface(blk_ctx* ctx, cudaStream_t stream, const uint8_t* env_mask)
     return rc != BLK_OK ? rc : launch_column_summary(ctx, stream, env_mask);
 }
 
-int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed)
+namespace {
+
+TileArgs tile_args(blk_ctx* ctx, int mode, uint32_t n_tiles, bool listed)
 {
     TileArgs a {};
     a.ids = ctx->ids;
@@ -1277,6 +1685,13 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, 
     a.columns = ctx->columns_per_env;
     a.mode = mode;
     a.listed = listed ? 1 : 0;
+    a.fallback_list = ctx->fallback_list;
+    a.fallback_count = ctx->fallback_count;
+    return a;
+}
+
+int launch_tile_args(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
+{
     switch (ctx->cfg.height / 32) {
     case 1:
         return launch_nw<1>(ctx, a, n_tiles, stream);
@@ -1298,6 +1713,56 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, 
         set_error("unsupported height");
         return BLK_ERR_INVALID_ARGUMENT;
     }
+}
+
+int launch_surface_args(blk_ctx* ctx, const TileArgs& a, uint32_t n_tiles, cudaStream_t stream)
+{
+    switch (ctx->cfg.height / 32) {
+    case 1:
+        return launch_surface_nw<1>(ctx, a, n_tiles, stream);
+    case 2:
+        return launch_surface_nw<2>(ctx, a, n_tiles, stream);
+    case 3:
+        return launch_surface_nw<3>(ctx, a, n_tiles, stream);
+    case 4:
+        return launch_surface_nw<4>(ctx, a, n_tiles, stream);
+    case 5:
+        return launch_surface_nw<5>(ctx, a, n_tiles, stream);
+    case 6:
+        return launch_surface_nw<6>(ctx, a, n_tiles, stream);
+    case 7:
+        return launch_surface_nw<7>(ctx, a, n_tiles, stream);
+    case 8:
+        return launch_surface_nw<8>(ctx, a, n_tiles, stream);
+    default:
+        set_error("unsupported height");
+        return BLK_ERR_INVALID_ARGUMENT;
+    }
+}
+
+} // namespace
+
+int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, bool listed)
+{
+    return launch_tile_args(ctx, tile_args(ctx, mode, n_tiles, listed), n_tiles, stream);
+}
+
+int launch_generation(blk_ctx* ctx, uint32_t n_tiles, cudaStream_t stream, bool listed)
+{
+    if (ctx->generation_path == BLK_GENERATION_TILES)
+        return launch_tiles(ctx, 0, n_tiles, stream, listed);
+    cudaError_t e = cudaMemsetAsync(ctx->fallback_count, 0, sizeof(uint32_t), stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "fallback count reset");
+    int rc = launch_surface_args(ctx, tile_args(ctx, 0, n_tiles, listed), n_tiles, stream);
+    if (rc != BLK_OK)
+        return rc;
+    // The tiles the surface kernel left (their number is on the device): the
+    // tile kernel's CTAs read it and walk that many list entries.
+    TileArgs g = tile_args(ctx, 0, n_tiles, true);
+    g.dirty_list = ctx->fallback_list;
+    g.list_count = ctx->fallback_count;
+    return launch_tile_args(ctx, g, n_tiles, stream);
 }
 
 } // namespace blk

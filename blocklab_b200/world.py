@@ -304,6 +304,19 @@ class WorldBatch:
         del keep
         return out
 
+    def set_generation_path(self, path: str) -> None:
+        """'surface' (default): the surface kernel, one light word per column,
+        with the tile kernel for the tiles it cannot prove exact; 'tiles': the
+        tile kernel for every tile. Both give the same worlds."""
+        code = {"surface": 0, "tiles": 1}[path]
+        check(N.lib.blk_set_generation_path(self._ctx, code))
+
+    def generation_fallback_tiles(self) -> int:
+        """Tiles of the last generation left to the tile kernel (waits for the device)."""
+        n = ctypes.c_uint32()
+        check(N.lib.blk_generation_fallback_tiles(self._ctx, ctypes.byref(n)))
+        return int(n.value)
+
     def profile(self, enable: bool) -> None:
         """Turns per-phase CUDA-event timing on or off (events on the call's stream)."""
         check(N.lib.blk_profile_enable(self._ctx, 1 if enable else 0))

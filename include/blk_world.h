@@ -309,6 +309,23 @@ int blk_profile_enable(blk_ctx* ctx, int enable);
  * clears the accumulators afterwards. */
 int blk_profile_read(blk_ctx* ctx, blk_profile* out, int reset);
 
+/* Generation path. BLK_GENERATION_SURFACE (the default) generates each tile
+ * with the surface kernel, which lights one 32-row word per column starting at
+ * the column's first open row, and hands the tiles it cannot prove exact
+ * (caves, overhangs, tall light, steep steps between columns) to the tile
+ * kernel; BLK_GENERATION_TILES runs the tile kernel on every tile. Both give
+ * the same worlds. For tests and diagnostics; no counterpart in the reference,
+ * whose generator has one path (src/world/WorldGenerator.cu:673-829). */
+typedef enum blk_generation_path {
+    BLK_GENERATION_SURFACE = 0,
+    BLK_GENERATION_TILES = 1
+} blk_generation_path;
+
+int blk_set_generation_path(blk_ctx* ctx, int path);
+/* Number of tiles of the last blk_generate / blk_generate_envs that the surface
+ * kernel left to the tile kernel (waits for the context's device). */
+int blk_generation_fallback_tiles(blk_ctx* ctx, uint32_t* count);
+
 /* RGBA8 -> float32 NCHW with the alpha channel dropped, value * (1.0f/255.0f).
  * Same signature and meaning as the reference's convertRgba8ToFloatNchw
  * (src/environment/CudaObservation.h:7-8); both pointers are device memory.
