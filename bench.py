@@ -47,11 +47,12 @@ SAMPLE = dict(W=128, H=128, D=128)
 SUSTAINED_S = 0.5  # every configuration is timed for at least this long
 # This library's kernel launches per step (from the launch lists in profiles/):
 # reset: torch placement, override count / scan (3) / scatter / sort, fBm
-# surface with the column summaries, tile kernel, conversion; relight: edit
+# surface with the column summaries, surface kernel, tile kernel over the
+# tiles the surface kernel left, conversion; relight: edit
 # count / scan (3) / scatter, setBlock application, change marking, region
 # build, dirty-tile compaction, four region kernels, tile kernel.
-LAUNCHES = dict(reset=10, relight=14, daynight=1, scaleout=15, render=1)
-TRAFFIC_CSV = os.path.join(ROOT, "profiles", "tile_kernel_reset_traffic.csv")
+LAUNCHES = dict(reset=11, relight=14, daynight=1, scaleout=15, render=1)
+TRAFFIC_CSV = os.path.join(ROOT, "profiles", "generation_reset_traffic.csv")
 
 
 def parse_args():
@@ -207,9 +208,10 @@ def measured_peaks():
 
 
 def load_traffic():
-    """DRAM bytes read + written by one benchmark launch of the tile kernel:
-    ncu's own CSV of that launch (profiles/tile_kernel_reset_traffic.csv,
-    written by the command in the summary beside it), or None when absent."""
+    """DRAM bytes read + written by one benchmark generation (the surface
+    kernel and the tile kernel's launch over the tiles it left): ncu's own CSV
+    of those two launches (profiles/generation_reset_traffic.csv, written by the
+    command in the summary beside it), or None when absent."""
     if not os.path.exists(TRAFFIC_CSV):
         return None
     got = {}
@@ -222,11 +224,11 @@ def load_traffic():
     i_unit = hdr.index("Metric Unit") if "Metric Unit" in hdr else None
     scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
     for r in rows:
-        if r is hdr or len(r) <= i_val or "tile_kernel" not in r[i_kernel]:
+        if r is hdr or len(r) <= i_val or not ("tile_kernel" in r[i_kernel] or "surface_kernel" in r[i_kernel]):
             continue
         unit = r[i_unit] if i_unit is not None else "byte"
         if r[i_name] in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
-            got[r[i_name]] = float(r[i_val].replace(",", "")) * scale.get(unit, 1)
+            got[r[i_name]] = got.get(r[i_name], 0.0) + float(r[i_val].replace(",", "")) * scale.get(unit, 1)
     if len(got) != 2:
         return None
     return int(sum(got.values()))
@@ -324,6 +326,7 @@ def reset_record(args, rank, world, local, dev, pg, peaks, peak_kind):
     wb.sync()
     tile_ms = prof["generate_tiles_ms"] / max(prof["generate_calls"], 1)
     prep_ms = prof["generate_prep_ms"] / max(prof["generate_calls"], 1)
+    fallback = wb.generation_fallback_tiles()
     n_sus = sustained_steps(ms / args.steps, args.steps, dev, pg)
     sus_ms, sus_clocks = time_steps(step, n_sus, 1, dev, pg, local)
 
@@ -400,10 +403,11 @@ def reset_record(args, rank, world, local, dev, pg, peaks, peak_kind):
                    "l2": f"outputs {2 * vox_step / 1e9:.2f} GB per step per GPU rewritten every step (> 126 MB L2)",
                    "parallelism": f"env shards x{world}"},
         "env_resets_per_s": E * world * args.steps / (ms / 1e3),
-        "roofline": {"bound": "hbm", "kernel": "tile_kernel<4, 0>", "achieved": achieved, "peak": peaks["hbm_gbs"],
+        "roofline": {"bound": "hbm", "kernel": "surface_kernel<4> + tile_kernel<4, 0> over the tiles it left",
+                     "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "algorithmic_bytes_per_launch": algo_bytes, "kernel_ms": tile_ms, "traffic": traffic,
-                     "traffic_source": "profiles/tile_kernel_reset_traffic.csv (ncu, one full-size launch)"
+                     "traffic_source": "profiles/generation_reset_traffic.csv (ncu, one full-size generation)"
                      if traffic is not None else None},
         "e2e": {"value": total_vox / (e2e_ms / 1e3), "unit": "voxels/s",
                 "h2d_bytes_per_step": seeds.numel() * 4 + frames.numel(),
@@ -412,7 +416,8 @@ def reset_record(args, rank, world, local, dev, pg, peaks, peak_kind):
         "clocks": clocks,
         "sustained": {"steps": n_sus, "ms_per_step": sus_ms / n_sus,
                       "value": vox_step * world * n_sus / (sus_ms / 1e3), "clocks": sus_clocks},
-        "profile": {"generate_prep_ms": prep_ms, "generate_tiles_ms": tile_ms},
+        "profile": {"generate_prep_ms": prep_ms, "generate_tiles_ms": tile_ms,
+                    "fallback_tiles_per_generation": fallback, "tiles_per_generation": E * (W // 32) * (D // 32)},
     }
 
 
