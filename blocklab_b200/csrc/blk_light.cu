@@ -1174,6 +1174,7 @@ __device__ bool process_surface_tile(const TileArgs& a, SurfSmem<NW>& s, uint32_
             return false;
 
         cnt[0] = own[0];
+        uint32_t s2 = 0u; // S_2 of the interior column: the cells a truncation could change
         // S_k = S_{k+1} | (open & dilate6(S_{k+1})), open = the rows of the word
         // inside the region; the level bit planes accumulate as in flood().
 #pragma unroll
@@ -1200,20 +1201,24 @@ __device__ bool process_surface_tile(const TileArgs& a, SurfSmem<NW>& s, uint32_
                         cnt[2] ^= v;
                     if (level == 8)
                         cnt[3] = v;
+                    if (level == 2)
+                        s2 = v;
                 }
             }
             __syncthreads();
         }
 
-        // No lit cell next to a truncated one (bits >= g: g = 32 + the lowest
-        // neighbour offset b_n - b below zero; bit 31 always).
+        // No cell of level >= 2 next to a truncated one (bits >= g: g = 32 +
+        // the lowest neighbour offset b_n - b below zero; bit 31 always). The
+        // interior column tests S_2; a halo column its last set, S_{1+d} or
+        // a part of a later one.
 #pragma unroll
         for (int k = 0; k < kSlots; ++k) {
             if ((slot[k] >> 16) >= kMaxDistance)
                 continue; // no column
             const uint32_t amax = max(max(amt[k][0], amt[k][1]), max(amt[k][2], amt[k][3]));
             const uint32_t g = min(31u, 48u - amax);
-            bad |= (own[k] & (0xFFFFFFFFu << g)) != 0u;
+            bad |= ((k == 0 ? s2 : own[k]) & (0xFFFFFFFFu << g)) != 0u;
         }
         if (__syncthreads_or(bad))
             return false;
@@ -1397,8 +1402,14 @@ __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds,
 {
     __shared__ float lat[4][100];
     __shared__ int32_t lat_ix[4], lat_iz[4], lat_nx[4], lat_nz[4];
+    // Per octave and block row z: the row's offset into lat and its weight.
+    __shared__ int32_t row_off[4][kFbmBlock];
+    __shared__ float row_w[4][kFbmBlock];
+    static_assert(kFbmBlock * 4 == 256, "one block of threads covers four rows of columns per pass");
     const int bx = blockIdx.x * kFbmBlock, bz = blockIdx.y * kFbmBlock;
     const int ex = min(bx + kFbmBlock - 1, W - 1), ez = min(bz + kFbmBlock - 1, D - 1);
+    // A thread keeps one column x of the block and walks its rows z.
+    const int xx = threadIdx.x % kFbmBlock;
     for (uint32_t env = blockIdx.z; env < num_envs; env += gridDim.z) {
         if (env_mask && !env_mask[env])
             continue; // uniform over the block
@@ -1427,23 +1438,38 @@ __global__ void __launch_bounds__(256) terrain_fbm_kernel(const uint32_t* seeds,
             for (int k = threadIdx.x; k < nx * nz; k += blockDim.x)
                 lat[o][k] = fbm_lattice(so, lat_ix[o] + k % nx, lat_iz[o] + k / nx);
         }
+        {
+            // Row tables: thread t covers octave t / 64, row t % 64.
+            const int o = threadIdx.x / kFbmBlock, zz = threadIdx.x % kFbmBlock;
+            int32_t iz;
+            float wz;
+            fbm_cell(o, org.z + bz + zz, iz, wz);
+            row_off[o][zz] = (iz - lat_iz[o]) * lat_nx[o];
+            row_w[o][zz] = wz;
+        }
+        // This thread's column: per octave its lattice offset and weight.
+        int32_t col_off[4];
+        float col_w[4];
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+            int32_t ix;
+            fbm_cell(o, org.x + bx + xx, ix, col_w[o]);
+            col_off[o] = ix - lat_ix[o];
+        }
         __syncthreads();
         const uint64_t env_col0 = static_cast<uint64_t>(env) * W * D;
-        for (int k = threadIdx.x; k < kFbmBlock * kFbmBlock; k += blockDim.x) {
-            const int x = bx + (k % kFbmBlock), z = bz + (k / kFbmBlock);
+        const int x = bx + xx;
+        for (int zz = threadIdx.x / kFbmBlock; zz < kFbmBlock; zz += 4) {
+            const int z = bz + zz;
             if (x >= W || z >= D)
                 continue;
             float acc = 0.0f;
             float amp = 1.0f;
 #pragma unroll
             for (int o = 0; o < 4; ++o) {
-                int32_t ix, iz;
-                float wx, wz;
-                fbm_cell(o, org.x + x, ix, wx);
-                fbm_cell(o, org.z + z, iz, wz);
                 const int nx = lat_nx[o];
-                const float* L = lat[o] + (iz - lat_iz[o]) * nx + (ix - lat_ix[o]);
-                const float n = fbm_mix(L[0], L[1], L[nx], L[nx + 1], wx, wz);
+                const float* L = lat[o] + row_off[o][zz] + col_off[o];
+                const float n = fbm_mix(L[0], L[1], L[nx], L[nx + 1], col_w[o], row_w[o][zz]);
                 acc = __fadd_rn(acc, __fmul_rn(amp, n));
                 amp = __fmul_rn(amp, 0.5f);
             }

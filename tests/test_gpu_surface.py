@@ -141,13 +141,16 @@ def test_steps_between_columns(B, oracle):
 def test_torch_height_above_surface(B, oracle):
     """Torches up to 15 rows above their column's first open row stay on the
     surface path (in a flat world their light ends inside the word); a torch
-    16 rows up is left to the tile kernel from the start. Beside a 10-row
-    pillar, light from a torch 8 rows above the pillar's top reaches rows above
-    the neighbouring low columns' words, which the exactness test catches."""
+    16 rows up is left to the tile kernel from the start. On a 10-row pillar,
+    light from a torch 9 rows above the pillar's top reaches the rows just
+    above the neighbouring low columns' words at level 2, which the exactness
+    test catches; from 8 rows up it reaches them at level 1 only, which
+    spreads no further, and the tile stays on the surface path."""
     W, H, D, base = 64, 64, 64, 20
     assert _pillar_world(B, oracle, W, H, D, base, [], [(10, 21, 10), (30, 28, 30), (40, 36, 40)]) == 0
     assert _pillar_world(B, oracle, W, H, D, base, [], [(30, 37, 30)]) > 0
-    assert _pillar_world(B, oracle, W, H, D, base, [(30, 30, 10)], [(30, 39, 30)]) > 0
+    assert _pillar_world(B, oracle, W, H, D, base, [(30, 30, 10)], [(30, 40, 30)]) > 0
+    assert _pillar_world(B, oracle, W, H, D, base, [(30, 30, 10)], [(30, 39, 30)]) == 0
 
 
 def test_light_into_pits(B, oracle):
