@@ -1598,7 +1598,7 @@ int blk_sync(blk_ctx* ctx, uintptr_t stream_handle)
 
 int blk_set_generation_path(blk_ctx* ctx, int path)
 {
-    if (!ctx || (path != BLK_GENERATION_SURFACE && path != BLK_GENERATION_TILES)) {
+    if (!ctx || (path != BLK_GENERATION_SURFACE && path != BLK_GENERATION_TILES && path != BLK_GENERATION_AUTO)) {
         set_error("blk_set_generation_path: null context or unknown path");
         return BLK_ERR_INVALID_ARGUMENT;
     }
@@ -1613,7 +1613,7 @@ int blk_generation_fallback_tiles(blk_ctx* ctx, uint32_t* count)
         return BLK_ERR_INVALID_ARGUMENT;
     }
     BLK_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    if (ctx->generation_path != BLK_GENERATION_SURFACE) {
+    if (generation_path_of(ctx) != BLK_GENERATION_SURFACE) {
         *count = 0;
         return BLK_OK;
     }

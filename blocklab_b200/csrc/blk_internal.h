@@ -68,7 +68,7 @@ struct blk_ctx {
     // Generation: the surface kernel's tiles left to the tile kernel.
     uint32_t* fallback_list = nullptr;    // [num_envs * tiles] tile ids
     uint32_t* fallback_count = nullptr;   // [1]
-    int generation_path = BLK_GENERATION_SURFACE;
+    int generation_path = BLK_GENERATION_AUTO;
 
     uint32_t* park = nullptr;             // tile-kernel scratch: 16 words x 1024 threads per CTA
     uint32_t park_ctas = 0;
@@ -143,6 +143,8 @@ int launch_tiles(blk_ctx* ctx, int mode, uint32_t n_tiles, cudaStream_t stream, 
 // Generation of all tiles (or the listed ones) on ctx->generation_path: the
 // surface kernel, then the tile kernel over the tiles it left.
 int launch_generation(blk_ctx* ctx, uint32_t n_tiles, cudaStream_t stream, bool listed = false);
+// The path launch_generation takes (BLK_GENERATION_SURFACE or BLK_GENERATION_TILES).
+int generation_path_of(const blk_ctx* ctx);
 int launch_render(blk_ctx* ctx, const blk_render_params* params, uint32_t width, uint32_t height, uint8_t* out,
     float* out_nchw, cudaStream_t stream);
 void halo_order_table(uint16_t* out);

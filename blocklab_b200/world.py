@@ -305,10 +305,11 @@ class WorldBatch:
         return out
 
     def set_generation_path(self, path: str) -> None:
-        """'surface' (default): the surface kernel, one light word per column,
-        with the tile kernel for the tiles it cannot prove exact; 'tiles': the
-        tile kernel for every tile. Both give the same worlds."""
-        code = {"surface": 0, "tiles": 1}[path]
+        """'surface': the surface kernel, one light word per column, with the
+        tile kernel for the tiles it cannot prove exact; 'tiles': the tile
+        kernel for every tile; 'auto' (default): 'tiles' for steep fBm terrain
+        (amplitude above 80), else 'surface'. All give the same worlds."""
+        code = {"surface": 0, "tiles": 1, "auto": 2}[path]
         check(N.lib.blk_set_generation_path(self._ctx, code))
 
     def generation_fallback_tiles(self) -> int:

@@ -309,16 +309,19 @@ int blk_profile_enable(blk_ctx* ctx, int enable);
  * clears the accumulators afterwards. */
 int blk_profile_read(blk_ctx* ctx, blk_profile* out, int reset);
 
-/* Generation path. BLK_GENERATION_SURFACE (the default) generates each tile
- * with the surface kernel, which lights one 32-row word per column starting at
- * the column's first open row, and hands the tiles it cannot prove exact
- * (caves, overhangs, tall light, steep steps between columns) to the tile
- * kernel; BLK_GENERATION_TILES runs the tile kernel on every tile. Both give
- * the same worlds. For tests and diagnostics; no counterpart in the reference,
- * whose generator has one path (src/world/WorldGenerator.cu:673-829). */
+/* Generation path. BLK_GENERATION_SURFACE generates each tile with the surface
+ * kernel, which lights one 32-row word per column starting at the column's
+ * first open row, and hands the tiles it cannot prove exact (caves, overhangs,
+ * tall light, steep steps between columns) to the tile kernel;
+ * BLK_GENERATION_TILES runs the tile kernel on every tile. BLK_GENERATION_AUTO
+ * (the default) takes the tile kernel for steep fBm terrain (amplitude above
+ * 80, where most tiles would be handed over) and the surface kernel otherwise.
+ * All give the same worlds. No counterpart in the reference, whose generator
+ * has one path (src/world/WorldGenerator.cu:673-829). */
 typedef enum blk_generation_path {
     BLK_GENERATION_SURFACE = 0,
-    BLK_GENERATION_TILES = 1
+    BLK_GENERATION_TILES = 1,
+    BLK_GENERATION_AUTO = 2
 } blk_generation_path;
 
 int blk_set_generation_path(blk_ctx* ctx, int path);

@@ -32,6 +32,7 @@ def _both_paths(B, cfg, seeds, make_overrides):
     surface path's fallback tile count."""
     wb = B.WorldBatch(cfg)
     ovr = make_overrides(wb)
+    wb.set_generation_path("surface")
     wb.generate(seeds, ovr)
     wb.sync()
     fallback = wb.generation_fallback_tiles()
@@ -113,6 +114,7 @@ def _pillar_world(B, oracle, W, H, D, base, pillars, torches):
     cfg = B.WorldConfig(num_envs=1, width=W, height=H, depth=D, terrain=TERRAIN_FLAT, base=base,
                         max_overrides=max(len(blk), 1))
     wb = B.WorldBatch(cfg)
+    wb.set_generation_path("surface")
     wb.generate([1], B.make_overrides(xyz, blk))
     wb.sync()
     fallback = wb.generation_fallback_tiles()
@@ -166,3 +168,25 @@ def test_light_into_pits(B, oracle):
     outer = [(x, z, 32) for x in range(18, 46) for z in range(18, 46) if not (24 <= x < 40 and 24 <= z < 40)]
     rim = [(x, z, 16) for x in range(12, 52) for z in range(12, 52) if not (18 <= x < 46 and 18 <= z < 46)]
     assert _pillar_world(B, oracle, W, H, D, base, ring + outer + rim, [(23, base + 33, 31)]) > 0
+
+
+def test_automatic_path_choice(B):
+    """The default path takes the tile kernel for steep fBm terrain (no tile is
+    reported as handed over) and the surface kernel otherwise."""
+    seeds = np.arange(1, 3, dtype=np.uint32)
+    for amp, steep in ((50.0, False), (120.0, True)):
+        cfg = B.WorldConfig(num_envs=2, width=128, height=256, depth=128, amplitude=amp, max_overrides=2 * 300)
+        wb = B.WorldBatch(cfg)
+        wb.generate(seeds, wb.place_torches(seeds, 300))
+        wb.sync()
+        auto = _state(wb)
+        n_auto = wb.generation_fallback_tiles()
+        wb.set_generation_path("surface")
+        wb.generate(seeds, wb.place_torches(seeds, 300))
+        wb.sync()
+        _assert_same(auto, _state(wb), f"amplitude {amp}")
+        if steep:
+            assert n_auto == 0 and wb.generation_fallback_tiles() > 0
+        else:
+            assert n_auto == wb.generation_fallback_tiles()
+        wb.close()
