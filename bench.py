@@ -334,7 +334,10 @@ def reset_record(args, rank, world, local, dev, pg, peaks, peak_kind):
     # its seeds and frames from pinned host memory and reads its height maps
     # back to pinned host memory. The copies run on a second stream with double
     # buffers, so that one step's transfers overlap its neighbours' kernels;
-    # every step's own transfers lie inside the timed region.
+    # every step's own transfers lie inside the timed region. Timed over the
+    # sustained loop's step count (at least SUSTAINED_S), so that the first
+    # step's input copy and the last step's read-back, which nothing overlaps,
+    # are a small part of it.
     seeds_pinned = torch.from_numpy(seeds_host.view(np.int32)).pin_memory()
     copy_stream = torch.cuda.Stream(dev)
     hm_host = [torch.empty((E, D, W), dtype=torch.int16, pin_memory=True) for _ in range(2)]
@@ -379,7 +382,7 @@ def reset_record(args, rank, world, local, dev, pg, peaks, peak_kind):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     copy_stream.wait_event(e0)
-    e2e_run(args.steps)
+    e2e_run(n_sus)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(dev, pg)
@@ -409,7 +412,7 @@ def reset_record(args, rank, world, local, dev, pg, peaks, peak_kind):
                      "algorithmic_bytes_per_launch": algo_bytes, "kernel_ms": tile_ms, "traffic": traffic,
                      "traffic_source": "profiles/generation_reset_traffic.csv (ncu, one full-size generation)"
                      if traffic is not None else None},
-        "e2e": {"value": total_vox / (e2e_ms / 1e3), "unit": "voxels/s",
+        "e2e": {"value": vox_step * world * n_sus / (e2e_ms / 1e3), "unit": "voxels/s", "steps": n_sus,
                 "h2d_bytes_per_step": seeds.numel() * 4 + frames.numel(),
                 "d2h_bytes_per_step": hm_host[0].numel() * 2},
         "gpu_launches": LAUNCHES["reset"] * args.steps,
