@@ -174,11 +174,12 @@ __global__ void ovr_count_kernel(const blk_override* ovr, uint32_t n, RegionDims
     }
 }
 
-// Scatters each override into its column segment. The override that takes
-// the segment's first slot is recorded as the segment's owner (owner[i] = 1),
-// so exactly one thread sorts each segment afterwards.
+// Scatters each override into its column segment, taking the segment's slots
+// from its count down (the counts the scan read; left at zero). The override
+// that takes slot 0 is recorded as the segment's owner (owner[i] = 1), so
+// exactly one thread sorts each segment afterwards.
 __global__ void ovr_scatter_kernel(const blk_override* ovr, uint32_t n, RegionDims r, const uint32_t* col_offset,
-    uint32_t* cursor, uint64_t* entries, uint8_t* owner)
+    uint32_t* count, uint64_t* entries, uint8_t* owner)
 {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const blk_override o = ovr[i];
@@ -188,7 +189,7 @@ __global__ void ovr_scatter_kernel(const blk_override* ovr, uint32_t n, RegionDi
             continue;
         }
         const uint64_t col = static_cast<uint64_t>(o.env) * r.W * r.D + static_cast<uint64_t>(z) * r.W + x;
-        const uint32_t slot = atomicAdd(cursor + col, 1u);
+        const uint32_t slot = atomicSub(count + col, 1u) - 1u;
         entries[col_offset[col] + slot] = (static_cast<uint64_t>(y) << 40) | (static_cast<uint64_t>(i) << 8) | o.block;
         owner[i] = slot == 0 ? 1 : 0;
     }
@@ -1130,7 +1131,6 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const int32_t* env_ori
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
     BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, n_cols + 1, st));
     if (n_overrides) {
-        BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset cursors");
         ovr_scatter_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset,
             ctx->col_count, ctx->entries, ctx->ovr_owner);
         ovr_sort_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset, ctx->entries,
@@ -1189,7 +1189,6 @@ int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, co
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
     BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, n_cols + 1, st));
     if (n_overrides) {
-        BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset cursors");
         ovr_scatter_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset,
             ctx->col_count, ctx->entries, ctx->ovr_owner);
         ovr_sort_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_offset, ctx->entries,
