@@ -1027,6 +1027,10 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     }
     if (rc == BLK_OK)
         rc = cuda_fail(cudaMemset(ctx->flags, 0, sizeof(uint32_t)), "cudaMemset flags");
+    if (rc == BLK_OK) {
+        rc = cuda_fail(cudaMemset(ctx->col_count, 0, (n_cols) * sizeof(uint32_t)), "cudaMemset column counts");
+        ctx->counts_zero = rc == BLK_OK;
+    }
     if (rc == BLK_OK)
         rc = cuda_fail(cudaMemset(ctx->hmap, 0, envs * ctx->columns_per_env * sizeof(int16_t)), "cudaMemset hmap");
     if (rc == BLK_OK)
@@ -1126,7 +1130,11 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const int32_t* env_ori
     const uint64_t n_cols = envs * ctx->columns_per_env;
     const RegionDims r = region(ctx);
     const int mark = prof_begin(ctx, 0, st);
-    BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
+    // The counts start at zero: left so by the previous generation's scatter
+    // unless another call used them as scratch since.
+    if (!ctx->counts_zero)
+        BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
+    ctx->counts_zero = false;
     if (n_overrides)
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
     BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, n_cols + 1, st));
@@ -1137,6 +1145,7 @@ int blk_generate(blk_ctx* ctx, const uint32_t* env_seeds, const int32_t* env_ori
             ctx->ovr_owner);
         BLK_CUDA(cudaGetLastError(), "override kernels");
     }
+    ctx->counts_zero = true; // the scatter counted every column back down
     const uint64_t n_tiles = envs * ctx->tiles_x * ctx->tiles_z;
     BLK_CHECK(launch_surface(ctx, st));
     prof_mark(ctx, mark, 1, st);
@@ -1184,7 +1193,11 @@ int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, co
     r.env_mask = ctx->env_mask;
     const uint64_t n_cols = envs * ctx->columns_per_env;
     const int mark = prof_begin(ctx, 0, st);
-    BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
+    // The counts start at zero: left so by the previous generation's scatter
+    // unless another call used them as scratch since.
+    if (!ctx->counts_zero)
+        BLK_CUDA(cudaMemsetAsync(ctx->col_count, 0, (n_cols + 1) * sizeof(uint32_t), st), "memset column counts");
+    ctx->counts_zero = false;
     if (n_overrides)
         ovr_count_kernel<<<grid_for(n_overrides, 256), 256, 0, st>>>(ovr, n_overrides, r, ctx->col_count);
     BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, n_cols + 1, st));
@@ -1195,6 +1208,7 @@ int blk_generate_envs(blk_ctx* ctx, const uint32_t* env_ids, uint32_t n_envs, co
             ctx->ovr_owner);
         BLK_CUDA(cudaGetLastError(), "override kernels");
     }
+    ctx->counts_zero = true; // the scatter counted every column back down
     BLK_CHECK(launch_surface(ctx, st, ctx->env_mask));
     prof_mark(ctx, mark, 1, st);
     BLK_CHECK(launch_generation(ctx, static_cast<uint32_t>(n_items), st, true));
@@ -1299,6 +1313,7 @@ int blk_build_render_voxels(blk_ctx* ctx, uint32_t env, void* voxels, uint32_t m
         return BLK_ERR_CAPACITY;
     }
     a.row_count = ctx->col_count; // scratch: the override counts are not live between calls
+    ctx->counts_zero = false;
     uint32_t* row_offset = ctx->col_offset;
     voxel_count_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, st>>>(a);
     BLK_CHECK(exclusive_scan(ctx, a.row_count, row_offset, rows, st));
@@ -1554,6 +1569,7 @@ int blk_snapshot_overrides(blk_ctx* ctx, uint32_t env, blk_override* out, uint32
     const uint8_t* ids = ctx->ids + static_cast<uint64_t>(env) * ctx->env_stride;
     const int16_t* top = ctx->terrain_top + static_cast<uint64_t>(env) * columns;
     // Scratch: the override CSR counts / offsets are not live between calls.
+    ctx->counts_zero = false; // the counts serve as scratch here
     snapshot_count_kernel<<<grid_for(columns, 256), 256, 0, st>>>(ids, top, region(ctx), ctx->col_count);
     BLK_CUDA(cudaGetLastError(), "snapshot count launch");
     BLK_CHECK(exclusive_scan(ctx, ctx->col_count, ctx->col_offset, columns, st));

@@ -36,6 +36,7 @@ struct blk_ctx {
     // Override column CSR (generation input).
     blk_override* ovr = nullptr;      // staging of host-resident override lists
     uint32_t* col_count = nullptr;    // [env * columns + 1]
+    bool counts_zero = false;         // col_count is all zero (a generation's scatter leaves it so)
     uint32_t* col_offset = nullptr;   // [env * columns + 1]
     uint64_t* entries = nullptr;      // [max_overrides], key y<<40 | order<<8 | block
     uint8_t* ovr_owner = nullptr;     // [max_overrides], 1 for the override owning its column segment
