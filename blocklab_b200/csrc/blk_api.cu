@@ -972,7 +972,7 @@ int blk_ctx_create(int device, const blk_world_config* config, blk_ctx** out)
     A(dalloc(&ctx->dirty_list, n_tiles, "dirty list"));
     A(dalloc(&ctx->dirty_count, 1, "dirty count"));
     A(dalloc(&ctx->fallback_list, n_tiles, "generation fallback tiles"));
-    A(dalloc(&ctx->fallback_count, 1, "generation fallback count"));
+    A(dalloc(&ctx->fallback_count, 2, "generation fallback count and tile cursor"));
     ctx->box_capacity = 2 * std::max<uint32_t>(c.max_edits, 1);
     ctx->region_capacity = ctx->box_capacity; // every item holds a marked change
     A(dalloc(&ctx->region_lists, 2ull * kRegionLists * ctx->region_capacity, "relight region lists"));

@@ -68,7 +68,7 @@ struct blk_ctx {
 
     // Generation: the surface kernel's tiles left to the tile kernel.
     uint32_t* fallback_list = nullptr;    // [num_envs * tiles] tile ids
-    uint32_t* fallback_count = nullptr;   // [1]
+    uint32_t* fallback_count = nullptr;   // [2]: their number, then the surface kernel's tile cursor
     int generation_path = BLK_GENERATION_AUTO;
 
     uint32_t* park = nullptr;             // tile-kernel scratch: 16 words x 1024 threads per CTA

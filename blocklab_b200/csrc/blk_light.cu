@@ -87,6 +87,7 @@ struct TileArgs {
     const uint32_t* list_count;     // mode 0 listed: device-side entry count of dirty_list (else n_tiles)
     uint32_t* fallback_list;        // surface kernel: tiles it leaves to the tile kernel
     uint32_t* fallback_count;
+    uint32_t* tile_cursor;          // surface kernel: next list position to take
 };
 
 // Rows a tile lights (see plan_tile in process_tile).
@@ -1047,8 +1048,10 @@ __device__ inline uint32_t surf_window(uint2 e, uint32_t amt) { return __funnels
 
 // Generates one tile; returns false (uniformly over the CTA) when the tile must
 // be generated by the tile kernel instead (its light is then not written).
+// Thread 0 takes the CTA's next list position from the shared cursor into
+// *next once this tile's column loads are in flight.
 template <int NW>
-__device__ bool process_surface_tile(const TileArgs& a, SurfSmem<NW>& s, uint32_t env, int x0, int z0)
+__device__ bool process_surface_tile(const TileArgs& a, SurfSmem<NW>& s, uint32_t env, int x0, int z0, uint32_t* next)
 {
     constexpr int H = 32 * NW;
     constexpr int kChunks = H / 16;
@@ -1074,6 +1077,8 @@ __device__ bool process_surface_tile(const TileArgs& a, SurfSmem<NW>& s, uint32_
                 pa[it] = __ldg(a.col_summary + env_col0 + static_cast<uint64_t>(gz) * a.W + gx);
         }
     }
+    if (tid == 0)
+        *next = atomicAdd(a.tile_cursor, 1u);
     __syncthreads();
     uint32_t fl = 0u;
     int32_t lo = 1 << 20, hi = -(1 << 20);
@@ -1285,25 +1290,36 @@ __device__ bool process_surface_tile(const TileArgs& a, SurfSmem<NW>& s, uint32_
     return true;
 }
 
-// Persistent: one CTA per SM walks the tiles (all, or the listed ones).
+// Persistent: one CTA per SM takes the tiles (all, or the listed ones) from a
+// shared cursor, so that the CTAs end together although tiles differ in cost.
 template <int NW>
 __global__ void __launch_bounds__(kThreads, 1) surface_kernel(TileArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ uint32_t next;
     SurfSmem<NW>& s = *reinterpret_cast<SurfSmem<NW>*>(smem_raw);
     const uint32_t tiles_per_env = static_cast<uint32_t>(a.tiles_x * a.tiles_z);
-    for (uint32_t i = blockIdx.x; i < a.n_tiles; i += gridDim.x) {
+    if (threadIdx.x == 0)
+        next = atomicAdd(a.tile_cursor, 1u);
+    __syncthreads();
+    uint32_t i = next;
+    while (i < a.n_tiles) {
+        __syncthreads(); // every thread has read `next` before it is rewritten
         const uint32_t tile_id = a.listed ? a.dirty_list[i] : i;
-        if (tile_id == 0xFFFFFFFFu)
-            continue; // uniform over the CTA
-        const uint32_t env = tile_id / tiles_per_env;
-        const uint32_t t_in_env = tile_id % tiles_per_env;
-        const int x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
-        const int z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
-        const bool done = process_surface_tile<NW>(a, s, env, x0, z0);
-        if (!done && threadIdx.x == 0)
-            a.fallback_list[atomicAdd(a.fallback_count, 1u)] = tile_id;
+        if (tile_id == 0xFFFFFFFFu) {
+            if (threadIdx.x == 0)
+                next = atomicAdd(a.tile_cursor, 1u);
+        } else {
+            const uint32_t env = tile_id / tiles_per_env;
+            const uint32_t t_in_env = tile_id % tiles_per_env;
+            const int x0 = static_cast<int>(t_in_env % a.tiles_x) * kTile;
+            const int z0 = static_cast<int>(t_in_env / a.tiles_x) * kTile;
+            const bool done = process_surface_tile<NW>(a, s, env, x0, z0, &next);
+            if (!done && threadIdx.x == 0)
+                a.fallback_list[atomicAdd(a.fallback_count, 1u)] = tile_id;
+        }
         __syncthreads();
+        i = next;
     }
 }
 
@@ -1732,6 +1748,7 @@ TileArgs tile_args(blk_ctx* ctx, int mode, uint32_t n_tiles, bool listed)
     a.listed = listed ? 1 : 0;
     a.fallback_list = ctx->fallback_list;
     a.fallback_count = ctx->fallback_count;
+    a.tile_cursor = ctx->fallback_count + 1;
     return a;
 }
 
@@ -1807,9 +1824,10 @@ int launch_generation(blk_ctx* ctx, uint32_t n_tiles, cudaStream_t stream, bool 
 {
     if (generation_path_of(ctx) == BLK_GENERATION_TILES)
         return launch_tiles(ctx, 0, n_tiles, stream, listed);
-    cudaError_t e = cudaMemsetAsync(ctx->fallback_count, 0, sizeof(uint32_t), stream);
+    // Fallback count and tile cursor.
+    cudaError_t e = cudaMemsetAsync(ctx->fallback_count, 0, 2 * sizeof(uint32_t), stream);
     if (e != cudaSuccess)
-        return cuda_fail(e, "fallback count reset");
+        return cuda_fail(e, "generation counters reset");
     int rc = launch_surface_args(ctx, tile_args(ctx, 0, n_tiles, listed), n_tiles, stream);
     if (rc != BLK_OK)
         return rc;
